@@ -1,0 +1,104 @@
+// device_common.cuh -- PTX helpers shared by the attention kernels (sm_100a).
+//
+// Bulk copies (cp.async.bulk, the 1-D form of TMA) move contiguous K/V
+// blocks from HBM into shared memory and complete on an mbarrier.  No copy
+// here uses .multicast::cluster: the kernels run unchanged on every GPU of a
+// multi-GPU job.  Every wait on an mbarrier is bounded by a clock64() budget;
+// on expiry the kernel records NLLB_DEV_ERR_TIMEOUT in the context's device
+// error word and leaves without writing outputs.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace nllb {
+
+constexpr int kHeadDim = 64;
+constexpr float kLog2e = 1.4426950408889634f;
+
+// device error word bits (read and cleared by nllb_attn_sync)
+constexpr int NLLB_DEV_ERR_TIMEOUT = 1;
+constexpr int NLLB_DEV_ERR_BAD_PARENT = 2;
+
+// ~1 s at 2 GHz: far above any legitimate wait for a copy of a few KB.
+constexpr long long kWaitBudgetCycles = 2000000000LL;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+
+// Make barrier initialisation visible to the async (bulk-copy) proxy.
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+// global -> shared bulk copy; dst, src 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for phase `parity` of `bar`; false if the budget ran out.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - t0 > kWaitBudgetCycles) return false;
+    }
+    return true;
+}
+
+__device__ __forceinline__ float4 f4_scale(float4 a, float s) {
+    return make_float4(a.x * s, a.y * s, a.z * s, a.w * s);
+}
+__device__ __forceinline__ float4 f4_fma(float s, float4 v, float4 acc) {
+    return make_float4(fmaf(s, v.x, acc.x), fmaf(s, v.y, acc.y), fmaf(s, v.z, acc.z),
+                       fmaf(s, v.w, acc.w));
+}
+__device__ __forceinline__ float f4_dot(float4 a, float4 b) {
+    return fmaf(a.w, b.w, fmaf(a.z, b.z, fmaf(a.y, b.y, a.x * b.x)));
+}
+
+// Sum over the 16 lanes of a half-warp (both halves reduce independently).
+// Must be reached by all 32 lanes.
+__device__ __forceinline__ float halfwarp_sum(float x) {
+    x += __shfl_xor_sync(0xffffffffu, x, 8);
+    x += __shfl_xor_sync(0xffffffffu, x, 4);
+    x += __shfl_xor_sync(0xffffffffu, x, 2);
+    x += __shfl_xor_sync(0xffffffffu, x, 1);
+    return x;
+}
+
+// exp2 of a difference that may be -inf - -inf (empty state): weight 0.
+__device__ __forceinline__ float safe_exp2_diff(float a, float m) {
+    return (a == -INFINITY) ? 0.0f : exp2f(a - m);
+}
+
+}  // namespace nllb

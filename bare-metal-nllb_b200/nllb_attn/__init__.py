@@ -1,0 +1,233 @@
+"""ctypes binding of libnllb_attn.so, the C ABI declared in include/nllb_attn.h.
+
+The product is the shared library; this module only gives Python callers
+(tests, bench.py) the same calls a C host makes.  Device-pointer calls take
+torch CUDA tensors (or raw integer addresses); ``*_host`` calls take numpy
+arrays.  Nothing here computes attention: every call goes through the
+library, and a missing library raises at import of :func:`load`.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Optional, Sequence
+
+PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.path.join(PKG_DIR, "libnllb_attn.so")
+
+OK, EINVAL, ECAPACITY, ECUDA, ETIMEOUT, ENODEV, ESTATE = range(7)
+
+# Every function include/nllb_attn.h declares, with (restype, argtypes).
+_c_int, _c_void_p, _c_size_t = ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t
+_fp = ctypes.c_void_p  # float*/const float*/int* passed as raw addresses
+
+
+class Dims(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in (
+        "n_layers", "n_heads", "head_dim", "max_sentences", "n_beams", "max_tgt", "max_src")]
+
+
+class PrefillArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", _fp), ("k", _fp), ("v", _fp), ("out", _fp),
+        ("batch", ctypes.c_int), ("n_heads", ctypes.c_int), ("seq_len", ctypes.c_int),
+        ("head_dim", ctypes.c_int),
+        ("stride_batch", ctypes.c_int64), ("stride_head", ctypes.c_int64),
+        ("stride_row", ctypes.c_int64),
+        ("valid_len", _fp), ("mask", _fp),
+        ("mask_stride_batch", ctypes.c_int64), ("mask_stride_head", ctypes.c_int64),
+        ("scale", ctypes.c_float),
+    ]
+
+
+SIGNATURES = {
+    "nllb_attn_create": (_c_int, [_c_int, ctypes.POINTER(Dims), ctypes.POINTER(_c_void_p)]),
+    "nllb_attn_destroy": (None, [_c_void_p]),
+    "nllb_attn_device_bytes": (_c_size_t, [ctypes.POINTER(Dims)]),
+    "nllb_attn_set_stream": (_c_int, [_c_void_p, _c_void_p]),
+    "nllb_attn_get_stream": (_c_void_p, [_c_void_p]),
+    "nllb_attn_sync": (_c_int, [_c_void_p]),
+    "nllb_attn_reset": (_c_int, [_c_void_p]),
+    "nllb_attn_strerror": (ctypes.c_char_p, [_c_int]),
+    "nllb_attn_last_error": (ctypes.c_char_p, []),
+    "nllb_attn_prefill": (_c_int, [_c_void_p, ctypes.POINTER(PrefillArgs)]),
+    "nllb_attn_prefill_host": (_c_int, [_c_void_p, ctypes.POINTER(PrefillArgs)]),
+    "nllb_attn_decode_self": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _fp, _fp, _fp, _fp]),
+    "nllb_attn_decode_self_host": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _fp, _fp, _fp, _fp]),
+    "nllb_attn_reorder": (_c_int, [_c_void_p, _c_int, _fp]),
+    "nllb_attn_reorder_host": (_c_int, [_c_void_p, _c_int, _fp]),
+    "nllb_attn_set_memory": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _fp, _fp,
+                                      ctypes.c_int64, ctypes.c_int64]),
+    "nllb_attn_set_memory_host": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _fp, _fp,
+                                           ctypes.c_int64, ctypes.c_int64]),
+    "nllb_attn_cross": (_c_int, [_c_void_p, _c_int, _c_int, _fp, _fp]),
+    "nllb_attn_cross_host": (_c_int, [_c_void_p, _c_int, _c_int, _fp, _fp]),
+    "nllb_attention_head": (None, [_fp, _fp, _fp, _fp, _fp, _fp, _c_int, _c_int]),
+    "nllb_attention_head_flash": (None, [_fp, _fp, _fp, _fp, _fp, _c_int, _c_int]),
+    "nllb_attn_last_status": (_c_int, []),
+}
+
+_LIB: Optional[ctypes.CDLL] = None
+
+
+def load(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Load the library (once) and declare every signature."""
+    global _LIB
+    if _LIB is not None and path == LIB_PATH:
+        return _LIB
+    if not os.path.exists(path):
+        raise FileNotFoundError(
+            f"{path} is missing: build it with `make -C {PKG_DIR}` (nvcc, sm_100a)")
+    lib = ctypes.CDLL(path)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    if path == LIB_PATH:
+        _LIB = lib
+    return lib
+
+
+class NllbAttnError(RuntimeError):
+    def __init__(self, status: int, what: str, detail: str):
+        super().__init__(f"{what}: status {status} ({detail})")
+        self.status = status
+
+
+def _check(lib, rc: int, what: str) -> None:
+    if rc != OK:
+        raise NllbAttnError(rc, what, lib.nllb_attn_last_error().decode())
+
+
+def ptr(x) -> Optional[int]:
+    """Raw address of a torch tensor, numpy array or int (None passes NULL)."""
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    if hasattr(x, "data_ptr"):
+        if not x.is_contiguous():
+            raise ValueError("tensor must be contiguous")
+        return x.data_ptr()
+    if hasattr(x, "ctypes"):
+        if not x.flags["C_CONTIGUOUS"]:
+            raise ValueError("array must be C-contiguous")
+        return x.ctypes.data
+    raise TypeError(f"cannot take the address of {type(x)!r}")
+
+
+class Context:
+    """One nllb_attn_ctx: caches, encoder memory and beam history on one GPU."""
+
+    def __init__(self, device: int = 0, n_layers: int = 12, n_heads: int = 16,
+                 max_sentences: int = 1, n_beams: int = 4, max_tgt: int = 256,
+                 max_src: int = 512, lib: Optional[ctypes.CDLL] = None):
+        self.lib = lib or load()
+        self.dims = Dims(n_layers, n_heads, 64, max_sentences, n_beams, max_tgt, max_src)
+        h = ctypes.c_void_p()
+        _check(self.lib, self.lib.nllb_attn_create(device, ctypes.byref(self.dims), ctypes.byref(h)),
+               "nllb_attn_create")
+        self.handle = h
+        self.n_beams, self.n_heads = n_beams, n_heads
+
+    def close(self) -> None:
+        if self.handle:
+            self.lib.nllb_attn_destroy(self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # -- plumbing --
+    def set_stream(self, stream_handle: int) -> None:
+        _check(self.lib, self.lib.nllb_attn_set_stream(self.handle, stream_handle), "set_stream")
+
+    def sync(self) -> None:
+        _check(self.lib, self.lib.nllb_attn_sync(self.handle), "nllb_attn_sync")
+
+    def reset(self) -> None:
+        _check(self.lib, self.lib.nllb_attn_reset(self.handle), "nllb_attn_reset")
+
+    # -- prefill --
+    @staticmethod
+    def prefill_args(q, k, v, out, batch, n_heads, seq_len, strides, valid_len=None,
+                     mask=None, mask_strides=(0, 0), scale=0.125) -> PrefillArgs:
+        sb, sh, sr = strides
+        return PrefillArgs(ptr(q), ptr(k), ptr(v), ptr(out), batch, n_heads, seq_len, 64,
+                           sb, sh, sr, ptr(valid_len), ptr(mask), mask_strides[0],
+                           mask_strides[1], scale)
+
+    def prefill(self, args: PrefillArgs) -> None:
+        _check(self.lib, self.lib.nllb_attn_prefill(self.handle, ctypes.byref(args)), "prefill")
+
+    def prefill_host(self, args: PrefillArgs) -> None:
+        _check(self.lib, self.lib.nllb_attn_prefill_host(self.handle, ctypes.byref(args)),
+               "prefill_host")
+
+    # -- decoder self-attention --
+    def decode_self(self, layer, step, n_sent, q, k_new, v_new, out) -> None:
+        _check(self.lib, self.lib.nllb_attn_decode_self(
+            self.handle, layer, step, n_sent, ptr(q), ptr(k_new), ptr(v_new), ptr(out)),
+            "decode_self")
+
+    def decode_self_host(self, layer, step, n_sent, q, k_new, v_new, out) -> None:
+        _check(self.lib, self.lib.nllb_attn_decode_self_host(
+            self.handle, layer, step, n_sent, ptr(q), ptr(k_new), ptr(v_new), ptr(out)),
+            "decode_self_host")
+
+    def reorder(self, n_sent, parent) -> None:
+        _check(self.lib, self.lib.nllb_attn_reorder(self.handle, n_sent, ptr(parent)), "reorder")
+
+    def reorder_host(self, n_sent, parent) -> None:
+        _check(self.lib, self.lib.nllb_attn_reorder_host(self.handle, n_sent, ptr(parent)),
+               "reorder_host")
+
+    # -- cross-attention --
+    def set_memory(self, layer, sentence, n_src, k, v, stride_head, stride_row) -> None:
+        _check(self.lib, self.lib.nllb_attn_set_memory(
+            self.handle, layer, sentence, n_src, ptr(k), ptr(v), stride_head, stride_row),
+            "set_memory")
+
+    def set_memory_host(self, layer, sentence, n_src, k, v, stride_head, stride_row) -> None:
+        _check(self.lib, self.lib.nllb_attn_set_memory_host(
+            self.handle, layer, sentence, n_src, ptr(k), ptr(v), stride_head, stride_row),
+            "set_memory_host")
+
+    def cross(self, layer, n_sent, q, out) -> None:
+        _check(self.lib, self.lib.nllb_attn_cross(self.handle, layer, n_sent, ptr(q), ptr(out)),
+               "cross")
+
+    def cross_host(self, layer, n_sent, q, out) -> None:
+        _check(self.lib, self.lib.nllb_attn_cross_host(self.handle, layer, n_sent, ptr(q),
+                                                       ptr(out)), "cross_host")
+
+
+def attention_head_flash(Q, K, V, mask, out, seq_len: int, head_dim: int = 64) -> int:
+    """The drop-in for attention_head_flash (tensor.c:286); returns its status."""
+    lib = load()
+    lib.nllb_attention_head_flash(ptr(Q), ptr(K), ptr(V), ptr(mask), ptr(out), seq_len, head_dim)
+    return lib.nllb_attn_last_status()
+
+
+def attention_head(Q, K, V, mask, out, scores_buf, seq_len: int, head_dim: int = 64) -> int:
+    """The drop-in for attention_head (tensor.c:255); returns its status."""
+    lib = load()
+    lib.nllb_attention_head(ptr(Q), ptr(K), ptr(V), ptr(mask), ptr(out), ptr(scores_buf),
+                            seq_len, head_dim)
+    return lib.nllb_attn_last_status()
+
+
+def exported_symbols(header_path: str) -> Sequence[str]:
+    """Function names declared in the C header (for the export check)."""
+    import re
+    text = open(header_path).read()
+    return sorted(set(re.findall(r"NLLB_ATTN_API\s+[\w\s\*]*?\b(nllb_\w+)\s*\(", text)))

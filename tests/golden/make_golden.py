@@ -1,0 +1,46 @@
+"""Regenerate tests/golden/golden_outputs.npz from the reference itself.
+
+Runs the reference's own attention code (tensor.c / decoder.c compiled from
+the reference sources into oracle/_ref/ by oracle/Makefile) on the seeded
+inputs defined in cases.py and stores its outputs.  Needs the reference
+sources at build time (REF_DIR, default /root/reference); the fixtures are
+committed so that nothing else ever needs them.
+
+    python tests/golden/make_golden.py
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+import cases  # noqa: E402
+from cases import po  # noqa: E402
+
+
+def main() -> None:
+    po.build(quiet=False)
+    out = {}
+    for name in cases.PREFILL_CASES:
+        q, k, v, vl = cases.prefill_case(name)
+        out[name] = po.ref_prefill_flash(q, k, v, vl)
+    Q, K, V, mask = cases.head_mask_case()
+    out["head_flash_mask"] = po.ref_attention_head(Q, K, V, mask, flash=True)
+    out["head_mask"] = po.ref_attention_head(Q, K, V, mask, flash=False)
+    for name, steps in cases.DECODE_CASES.items():
+        q, k, v, parents = cases.decode_case(name)
+        full = po.ref_decode_sweep(q, k, v, parents)
+        out[name] = full[list(steps)]
+    for name in cases.CROSS_CASES:
+        K, V, q = cases.cross_case(name)
+        out[name] = po.ref_cross(K, V, q)
+    np.savez_compressed(cases.GOLDEN_NPZ, **out)
+    for k_, v_ in out.items():
+        print(f"{k_:22s} {str(v_.shape):22s} sum={float(np.sum(v_, dtype=np.float64)):+.6f}")
+    print("wrote", cases.GOLDEN_NPZ, os.path.getsize(cases.GOLDEN_NPZ), "bytes")
+
+
+if __name__ == "__main__":
+    main()
