@@ -9,10 +9,14 @@
 //     (64 KB) are in flight per CTA while the third is consumed;
 //   * a half-warp owns 64-float rows: 16 lanes x float4, dot product by four
 //     xor-shuffles; online softmax in base 2 per half-warp;
-//   * split-KV when (sentences x heads) cannot fill the 148 SMs: each split
-//     writes (max, sum, acc) to a workspace and the last CTA of a
-//     (sentence, head) to finish - found with one atomic, no waiting - merges
-//     them (flash-decoding combine).
+//   * split-KV when (sentences x heads) cannot fill the 148 SMs: the splits
+//     of one (sentence, head) form a thread-block cluster; each leaves its
+//     (max, sum, acc) record in its own shared memory and cluster rank 0
+//     merges them over distributed shared memory (flash-decoding combine
+//     without a global workspace, atomics or a second launch);
+//   * programmatic dependent launch: a kernel lets the next one in the stream
+//     start its prologue early and waits (griddepcontrol.wait) before it
+//     touches anything a predecessor writes.
 //
 // Self-attention cache row (p, slot) of a (sentence, head) is at
 // ((p * n_beams) + slot) * 64: all beams' rows of one position are adjacent,
@@ -28,33 +32,58 @@ namespace nllb {
 namespace {
 
 constexpr int kThreads = 128;
-constexpr int kStages = 3;
+constexpr int kBarBytes = 128;  // mbarriers at the start of dynamic shared memory
 
 // ---------------------------------------------------------------------------
-// Split record helpers
+// Split merge over the cluster
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void store_part(float* rec, int q4, float m, float l, float4 acc) {
-    if (q4 == 0) {
-        rec[0] = m;
-        rec[1] = l;
+// rec: this CTA's per-beam records [NB][68] (m, l, -, -, acc[64]) in shared
+// memory; abort_flag: this CTA's abort word.  Rank 0 merges the n_split
+// records of each beam and writes out[bb*row_stride + 0..63].  Every thread of
+// every CTA of the cluster calls this (the barriers are cluster-wide), so
+// no CTA leaves while its records may still be read.
+template <int NB>
+__device__ __forceinline__ void cluster_merge(const float* rec, const int* abort_flag, int n_split,
+                                              float* out, size_t row_stride) {
+    cluster_sync_all();
+    if (cluster_ctarank() == 0) {
+        bool any_abort = false;
+        for (int r = 0; r < n_split; ++r) any_abort |= ld_cluster_s32(map_rank(abort_flag, r)) != 0;
+        if (!any_abort) {
+            for (int idx = threadIdx.x; idx < NB * 16; idx += blockDim.x) {
+                const int bb = idx >> 4, q4 = idx & 15;
+                const float* mine = rec + bb * kPartFloats;
+                float M = -INFINITY;
+                for (int r = 0; r < n_split; ++r) M = fmaxf(M, ld_cluster_f32(map_rank(mine, r)));
+                float L = 0.f;
+                float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int r = 0; r < n_split; ++r) {
+                    const uint32_t base = map_rank(mine, r);
+                    const float w = safe_exp2_diff(ld_cluster_f32(base), M);
+                    L = fmaf(w, ld_cluster_f32(base + 4), L);
+                    A = f4_fma(w, ld_cluster_f4(base + 16 + 16 * q4), A);
+                }
+                reinterpret_cast<float4*>(out + bb * row_stride)[q4] = f4_scale(A, 1.0f / L);
+            }
+        }
     }
-    reinterpret_cast<float4*>(rec + 4)[q4] = acc;
+    cluster_sync_all();
 }
 
-// Merge the n_split records of one (sentence, head, beam) and write out.
-__device__ __forceinline__ void merge_parts(const float* part0, int n_split, int rec_stride,
-                                            int q4, float* dst) {
-    float M = -INFINITY;
-    for (int i = 0; i < n_split; ++i) M = fmaxf(M, __ldcg(part0 + (size_t)i * rec_stride));
-    float L = 0.f;
-    float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int i = 0; i < n_split; ++i) {
-        const float* rec = part0 + (size_t)i * rec_stride;
-        const float w = safe_exp2_diff(__ldcg(rec), M);
-        L = fmaf(w, __ldcg(rec + 1), L);
-        A = f4_fma(w, __ldcg(reinterpret_cast<const float4*>(rec + 4) + q4), A);
+// Merge `nsrc` (m, l, acc) records of one beam held in shared memory
+// (record j at recs + j*stride) into (M, L, A quad q4).
+__device__ __forceinline__ void merge_local(const float* recs, int nsrc, int stride, int q4, float& M,
+                                            float& L, float4& A) {
+    M = -INFINITY;
+    for (int j = 0; j < nsrc; ++j) M = fmaxf(M, recs[j * stride]);
+    L = 0.f;
+    A = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < nsrc; ++j) {
+        const float* rc = recs + j * stride;
+        const float w = safe_exp2_diff(rc[0], M);
+        L = fmaf(w, rc[1], L);
+        A = f4_fma(w, reinterpret_cast<const float4*>(rc + 4)[q4], A);
     }
-    reinterpret_cast<float4*>(dst)[q4] = f4_scale(A, 1.0f / L);
 }
 
 // ---------------------------------------------------------------------------
@@ -62,19 +91,20 @@ __device__ __forceinline__ void merge_parts(const float* part0, int n_split, int
 // ---------------------------------------------------------------------------
 template <int NB>
 __global__ void __launch_bounds__(kThreads) decode_self_kernel(const SelfParams p) {
-    constexpr int CP = 64 / NB;       // positions per chunk
-    constexpr int NSUB = 8 / NB;      // half-warps per beam
-    constexpr int RPH = CP / NSUB;    // positions per half-warp per chunk (= 8)
+    constexpr int CP = kSelfChunkRows / NB;  // positions per chunk
+    constexpr int NSUB = 8 / NB;         // half-warps per beam
+    constexpr int RPH = CP / NSUB;       // positions per half-warp per chunk
     constexpr int KV_FLOATS = CP * NB * 64;
     constexpr int H_BYTES = CP * 8;
 
     extern __shared__ __align__(128) unsigned char smem[];
-    float* sK = reinterpret_cast<float*>(smem);
-    float* sV = sK + kStages * KV_FLOATS;
-    unsigned char* sH = reinterpret_cast<unsigned char*>(sV + kStages * KV_FLOATS);
-    uint64_t* bar = reinterpret_cast<uint64_t*>(sH + kStages * H_BYTES);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
+    float* sK = reinterpret_cast<float*>(smem + kBarBytes);
+    float* sV = sK + kSelfStages * KV_FLOATS;
+    unsigned char* sH = reinterpret_cast<unsigned char*>(sV + kSelfStages * KV_FLOATS);
     __shared__ int s_abort;
-    __shared__ int s_last;
+
+    pdl_launch_dependents();
 
     const int split = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
     const int tid = threadIdx.x, hw = tid >> 4, l16 = tid & 15;
@@ -90,16 +120,18 @@ __global__ void __launch_bounds__(kThreads) decode_self_kernel(const SelfParams 
     const float* gK = p.kc + head_pos0 * NB * 64;
     const float* gV = p.vc + head_pos0 * NB * 64;
     const unsigned char* gH = p.hist + (size_t)s * p.Tp * 8;
+    const size_t qrow = ((size_t)s * NB + b) * (size_t)p.H * 64 + (size_t)h * 64;
 
     if (tid == 0) {
-        for (int i = 0; i < kStages; ++i) mbar_init(&bar[i], 1);
+        for (int i = 0; i < kSelfStages; ++i) mbar_init(&bar[i], 1);
         fence_barrier_init();
         s_abort = 0;
     }
     __syncthreads();
+    pdl_wait_primary();  // cache, history and q come from earlier kernels
 
     auto issue = [&](int c) {
-        const int st = c % kStages;
+        const int st = c % kSelfStages;
         const int pc0 = p0 + c * CP;
         const int np = min(CP, p1 - pc0);
         const uint32_t kvb = (uint32_t)np * NB * 256u;
@@ -110,24 +142,29 @@ __global__ void __launch_bounds__(kThreads) decode_self_kernel(const SelfParams 
         bulk_g2s(sH + st * H_BYTES, gH + (size_t)pc0 * 8, hb, &bar[st]);
     };
     if (tid == 0) {
-        for (int c = 0; c < kStages - 1 && c < nchunk; ++c) issue(c);
+        for (int c = 0; c < kSelfStages - 1 && c < nchunk; ++c) issue(c);
     }
 
-    const size_t qrow = ((size_t)s * NB + b) * (size_t)p.H * 64 + (size_t)h * 64;
     const float4 qv = __ldg(reinterpret_cast<const float4*>(p.q + qrow) + l16);
+    // the new token's k/v, loaded now so their latency hides behind the stream
+    float4 kn = make_float4(0.f, 0.f, 0.f, 0.f), vn = kn;
+    if (owns_new) {
+        kn = __ldg(reinterpret_cast<const float4*>(p.k_new + qrow) + l16);
+        vn = __ldg(reinterpret_cast<const float4*>(p.v_new + qrow) + l16);
+    }
 
     float m = -INFINITY, l = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     int consumed = 0;
 
     for (int c = 0; c < nchunk; ++c) {
-        const int st = c % kStages;
-        const uint32_t par = (uint32_t)((c / kStages) & 1);
+        const int st = c % kSelfStages;
+        const uint32_t par = (uint32_t)((c / kSelfStages) & 1);
         if (!mbar_wait_bounded(&bar[st], par)) s_abort = 1;
         __syncthreads();  // stage (c-1) fully consumed; abort flag visible
         if (s_abort) break;
         consumed = c + 1;
-        if (tid == 0 && c + kStages - 1 < nchunk) issue(c + kStages - 1);
+        if (tid == 0 && c + kSelfStages - 1 < nchunk) issue(c + kSelfStages - 1);
 
         const int np = min(CP, p1 - (p0 + c * CP));
         const float* K = sK + st * KV_FLOATS;
@@ -168,88 +205,66 @@ __global__ void __launch_bounds__(kThreads) decode_self_kernel(const SelfParams 
         }
     }
 
+    float* red = sK;                    // [8 half-warps][68], overlays the ring (free after the loop)
+    float* rec = sK + 8 * kPartFloats;  // [NB][68] this CTA's merged records
+    float* out_base = p.out + (size_t)s * NB * p.H * 64 + (size_t)h * 64;
+    const size_t out_stride = (size_t)p.H * 64;
+
     if (s_abort) {
-        // drain copies still in flight into this CTA's shared memory, then leave
+        // let copies still in flight into this CTA's shared memory land, then stop
         if (tid == 0) {
             atomicOr(p.err, NLLB_DEV_ERR_TIMEOUT);
-            const int issued = min(nchunk, consumed + kStages - 1);
+            const int issued = min(nchunk, consumed + kSelfStages - 1);
             for (int c = consumed; c < issued; ++c)
-                (void)mbar_wait_bounded(&bar[c % kStages], (uint32_t)((c / kStages) & 1));
+                (void)mbar_wait_bounded(&bar[c % kSelfStages], (uint32_t)((c / kSelfStages) & 1));
         }
-        return;
-    }
-
-    // The new token at position `step`: every beam attends to its own k_new.
-    if (owns_new) {
-        const float4 kn = __ldg(reinterpret_cast<const float4*>(p.k_new + qrow) + l16);
-        const float4 vn = __ldg(reinterpret_cast<const float4*>(p.v_new + qrow) + l16);
-        const float d = halfwarp_sum(f4_dot(qv, kn)) * p.scale_log2;
-        if (sub == 0) {
-            const float mn = fmaxf(m, d);
-            const float corr = safe_exp2_diff(m, mn);
-            const float e = exp2f(d - mn);
-            l = fmaf(l, corr, e);
-            acc = f4_fma(e, vn, f4_scale(acc, corr));
-            m = mn;
-            // append to the cache: position `step`, physical slot b
-            const size_t row = (head_pos0 + (size_t)p.step) * NB + b;
-            reinterpret_cast<float4*>(p.kc_w + row * 64)[l16] = kn;
-            reinterpret_cast<float4*>(p.vc_w + row * 64)[l16] = vn;
-            if (h == 0 && l16 == 0) p.hist_w[((size_t)s * p.Tp + p.step) * 8 + b] = (unsigned char)b;
+    } else {
+        // The new token at position `step`: every beam attends to its own k_new.
+        if (owns_new) {
+            const float d = halfwarp_sum(f4_dot(qv, kn)) * p.scale_log2;
+            if (sub == 0) {
+                const float mn = fmaxf(m, d);
+                const float corr = safe_exp2_diff(m, mn);
+                const float e = exp2f(d - mn);
+                l = fmaf(l, corr, e);
+                acc = f4_fma(e, vn, f4_scale(acc, corr));
+                m = mn;
+                // append to the cache: position `step`, physical slot b
+                const size_t row = (head_pos0 + (size_t)p.step) * NB + b;
+                reinterpret_cast<float4*>(p.kc_w + row * 64)[l16] = kn;
+                reinterpret_cast<float4*>(p.vc_w + row * 64)[l16] = vn;
+                if (h == 0 && l16 == 0)
+                    p.hist_w[((size_t)s * p.Tp + p.step) * 8 + b] = (unsigned char)b;
+            }
         }
-    }
-
-    // Merge the NSUB half-warp states of each beam (stage buffers are free now).
-    __syncthreads();
-    float* red = sK;  // [8 hw][68]
-    {
-        float* rec = red + hw * kPartFloats;
-        if (l16 == 0) {
-            rec[0] = m;
-            rec[1] = l;
+        __syncthreads();
+        {
+            float* r = red + hw * kPartFloats;
+            if (l16 == 0) {
+                r[0] = m;
+                r[1] = l;
+            }
+            reinterpret_cast<float4*>(r + 4)[l16] = acc;
         }
-        reinterpret_cast<float4*>(rec + 4)[l16] = acc;
-    }
-    __syncthreads();
-
-    const size_t unit = (size_t)s * p.H + h;
-    for (int idx = tid; idx < NB * 16; idx += kThreads) {
-        const int bb = idx >> 4, q4 = idx & 15;
-        float M = -INFINITY;
-#pragma unroll
-        for (int j = 0; j < NSUB; ++j) M = fmaxf(M, red[(bb + NB * j) * kPartFloats]);
-        float L = 0.f;
-        float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int j = 0; j < NSUB; ++j) {
-            const float* rec = red + (bb + NB * j) * kPartFloats;
-            const float w = safe_exp2_diff(rec[0], M);
-            L = fmaf(w, rec[1], L);
-            A = f4_fma(w, reinterpret_cast<const float4*>(rec + 4)[q4], A);
-        }
-        if (p.n_split == 1) {
-            float* dst = p.out + ((size_t)s * NB + bb) * (size_t)p.H * 64 + (size_t)h * 64;
-            reinterpret_cast<float4*>(dst)[q4] = f4_scale(A, 1.0f / L);
-        } else {
-            float* rec = p.part + ((unit * p.n_split + split) * NB + bb) * kPartFloats;
-            store_part(rec, q4, M, L, A);
+        __syncthreads();
+        for (int idx = tid; idx < NB * 16; idx += kThreads) {
+            const int bb = idx >> 4, q4 = idx & 15;
+            float M, L;
+            float4 A;
+            merge_local(red + bb * kPartFloats, NSUB, NB * kPartFloats, q4, M, L, A);
+            if (p.n_split == 1) {
+                reinterpret_cast<float4*>(out_base + bb * out_stride)[q4] = f4_scale(A, 1.0f / L);
+            } else {
+                float* r = rec + bb * kPartFloats;
+                if (q4 == 0) {
+                    r[0] = M;
+                    r[1] = L;
+                }
+                reinterpret_cast<float4*>(r + 4)[q4] = A;
+            }
         }
     }
-    if (p.n_split == 1) return;
-
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_last = (atomicAdd(&p.counters[unit], 1) == p.n_split - 1);
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    for (int idx = tid; idx < NB * 16; idx += kThreads) {
-        const int bb = idx >> 4, q4 = idx & 15;
-        const float* part0 = p.part + (unit * p.n_split * NB + bb) * kPartFloats;
-        float* dst = p.out + ((size_t)s * NB + bb) * (size_t)p.H * 64 + (size_t)h * 64;
-        merge_parts(part0, p.n_split, NB * kPartFloats, q4, dst);
-    }
-    if (tid == 0) p.counters[unit] = 0;
+    if (p.n_split > 1) cluster_merge<NB>(rec, &s_abort, p.n_split, out_base, out_stride);
 }
 
 // ---------------------------------------------------------------------------
@@ -262,14 +277,23 @@ __global__ void __launch_bounds__(kThreads) cross_kernel(const CrossParams p) {
     constexpr int KV_FLOATS = CP * 64;
 
     extern __shared__ __align__(128) unsigned char smem[];
-    float* sK = reinterpret_cast<float*>(smem);
-    float* sV = sK + kStages * KV_FLOATS;
-    uint64_t* bar = reinterpret_cast<uint64_t*>(sV + kStages * KV_FLOATS);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
+    float* sK = reinterpret_cast<float*>(smem + kBarBytes);
+    float* sV = sK + kCrossStages * KV_FLOATS;
     __shared__ int s_abort;
-    __shared__ int s_last;
+
+    pdl_launch_dependents();
 
     const int split = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
     const int tid = threadIdx.x, hw = tid >> 4, l16 = tid & 15;
+
+    if (tid == 0) {
+        for (int i = 0; i < kCrossStages; ++i) mbar_init(&bar[i], 1);
+        fence_barrier_init();
+        s_abort = 0;
+    }
+    __syncthreads();
+    pdl_wait_primary();  // memory, lengths and q come from earlier kernels
 
     const int len = __ldg(p.n_src + s);
     const int p0 = split * p.pos_per_split;
@@ -280,15 +304,8 @@ __global__ void __launch_bounds__(kThreads) cross_kernel(const CrossParams p) {
     const float* gK = p.km + head_row0 * 64;
     const float* gV = p.vm + head_row0 * 64;
 
-    if (tid == 0) {
-        for (int i = 0; i < kStages; ++i) mbar_init(&bar[i], 1);
-        fence_barrier_init();
-        s_abort = 0;
-    }
-    __syncthreads();
-
     auto issue = [&](int c) {
-        const int st = c % kStages;
+        const int st = c % kCrossStages;
         const int pc0 = p0 + c * CP;
         const int np = min(CP, p1 - pc0);
         const uint32_t kvb = (uint32_t)np * 256u;
@@ -297,7 +314,7 @@ __global__ void __launch_bounds__(kThreads) cross_kernel(const CrossParams p) {
         bulk_g2s(sV + st * KV_FLOATS, gV + (size_t)pc0 * 64, kvb, &bar[st]);
     };
     if (tid == 0) {
-        for (int c = 0; c < kStages - 1 && c < nchunk; ++c) issue(c);
+        for (int c = 0; c < kCrossStages - 1 && c < nchunk; ++c) issue(c);
     }
 
     float4 qv[NB];
@@ -317,13 +334,13 @@ __global__ void __launch_bounds__(kThreads) cross_kernel(const CrossParams p) {
     int consumed = 0;
 
     for (int c = 0; c < nchunk; ++c) {
-        const int st = c % kStages;
-        const uint32_t par = (uint32_t)((c / kStages) & 1);
+        const int st = c % kCrossStages;
+        const uint32_t par = (uint32_t)((c / kCrossStages) & 1);
         if (!mbar_wait_bounded(&bar[st], par)) s_abort = 1;
         __syncthreads();
         if (s_abort) break;
         consumed = c + 1;
-        if (tid == 0 && c + kStages - 1 < nchunk) issue(c + kStages - 1);
+        if (tid == 0 && c + kCrossStages - 1 < nchunk) issue(c + kCrossStages - 1);
 
         const int np = min(CP, p1 - (p0 + c * CP));
         const float* K = sK + st * KV_FLOATS;
@@ -369,67 +386,48 @@ __global__ void __launch_bounds__(kThreads) cross_kernel(const CrossParams p) {
         }
     }
 
+    float* red = sK;                         // [8 half-warps][NB][68], overlays the ring
+    float* rec = sK + 8 * NB * kPartFloats;  // [NB][68]
+    float* out_base = p.out + (size_t)s * NB * p.H * 64 + (size_t)h * 64;
+    const size_t out_stride = (size_t)p.H * 64;
+
     if (s_abort) {
         if (tid == 0) {
             atomicOr(p.err, NLLB_DEV_ERR_TIMEOUT);
-            const int issued = min(nchunk, consumed + kStages - 1);
+            const int issued = min(nchunk, consumed + kCrossStages - 1);
             for (int c = consumed; c < issued; ++c)
-                (void)mbar_wait_bounded(&bar[c % kStages], (uint32_t)((c / kStages) & 1));
+                (void)mbar_wait_bounded(&bar[c % kCrossStages], (uint32_t)((c / kCrossStages) & 1));
         }
-        return;
-    }
-
-    __syncthreads();
-    float* red = sK;  // [8 hw][NB][68]
+    } else {
+        __syncthreads();
 #pragma unroll
-    for (int b = 0; b < NB; ++b) {
-        float* rec = red + (hw * NB + b) * kPartFloats;
-        if (l16 == 0) {
-            rec[0] = m[b];
-            rec[1] = l[b];
+        for (int b = 0; b < NB; ++b) {
+            float* r = red + (hw * NB + b) * kPartFloats;
+            if (l16 == 0) {
+                r[0] = m[b];
+                r[1] = l[b];
+            }
+            reinterpret_cast<float4*>(r + 4)[l16] = acc[b];
         }
-        reinterpret_cast<float4*>(rec + 4)[l16] = acc[b];
-    }
-    __syncthreads();
-
-    const size_t unit = (size_t)s * p.H + h;
-    for (int idx = tid; idx < NB * 16; idx += kThreads) {
-        const int bb = idx >> 4, q4 = idx & 15;
-        float M = -INFINITY;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) M = fmaxf(M, red[(j * NB + bb) * kPartFloats]);
-        float L = 0.f;
-        float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const float* rec = red + (j * NB + bb) * kPartFloats;
-            const float w = safe_exp2_diff(rec[0], M);
-            L = fmaf(w, rec[1], L);
-            A = f4_fma(w, reinterpret_cast<const float4*>(rec + 4)[q4], A);
-        }
-        if (p.n_split == 1) {
-            float* dst = p.out + ((size_t)s * NB + bb) * (size_t)p.H * 64 + (size_t)h * 64;
-            reinterpret_cast<float4*>(dst)[q4] = f4_scale(A, 1.0f / L);
-        } else {
-            float* rec = p.part + ((unit * p.n_split + split) * NB + bb) * kPartFloats;
-            store_part(rec, q4, M, L, A);
+        __syncthreads();
+        for (int idx = tid; idx < NB * 16; idx += kThreads) {
+            const int bb = idx >> 4, q4 = idx & 15;
+            float M, L;
+            float4 A;
+            merge_local(red + bb * kPartFloats, 8, NB * kPartFloats, q4, M, L, A);
+            if (p.n_split == 1) {
+                reinterpret_cast<float4*>(out_base + bb * out_stride)[q4] = f4_scale(A, 1.0f / L);
+            } else {
+                float* r = rec + bb * kPartFloats;
+                if (q4 == 0) {
+                    r[0] = M;
+                    r[1] = L;
+                }
+                reinterpret_cast<float4*>(r + 4)[q4] = A;
+            }
         }
     }
-    if (p.n_split == 1) return;
-
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_last = (atomicAdd(&p.counters[unit], 1) == p.n_split - 1);
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    for (int idx = tid; idx < NB * 16; idx += kThreads) {
-        const int bb = idx >> 4, q4 = idx & 15;
-        const float* part0 = p.part + (unit * p.n_split * NB + bb) * kPartFloats;
-        float* dst = p.out + ((size_t)s * NB + bb) * (size_t)p.H * 64 + (size_t)h * 64;
-        merge_parts(part0, p.n_split, NB * kPartFloats, q4, dst);
-    }
-    if (tid == 0) p.counters[unit] = 0;
+    if (p.n_split > 1) cluster_merge<NB>(rec, &s_abort, p.n_split, out_base, out_stride);
 }
 
 // ---------------------------------------------------------------------------
@@ -438,6 +436,8 @@ __global__ void __launch_bounds__(kThreads) cross_kernel(const CrossParams p) {
 // new slot of (p, b) = old slot of (p, parent[b]), in place, one CTA per sentence.
 __global__ void reorder_kernel(unsigned char* hist, int Tp, const int* parent, int n_beams,
                                int* err) {
+    pdl_launch_dependents();
+    pdl_wait_primary();  // earlier kernels may still read the history / write parent
     const int s = blockIdx.x;
     __shared__ int par[8];
     __shared__ int bad;
@@ -475,10 +475,12 @@ __global__ void hist_init_kernel(unsigned char* hist, size_t n_rows) {
         reinterpret_cast<uint2*>(hist)[i] = ident;
 }
 
-// k[r*stride_row + h*stride_head + d] -> km[h][r][d] (one layer, one sentence)
+// k[r*stride_row + h*stride_head + d] -> km[h][r][d] (one layer, one sentence);
+// thread 0 of block 0 also records the row count.
 __global__ void set_memory_kernel(float* km, float* vm, int max_src, int H, const float* k,
                                   const float* v, long long stride_head, long long stride_row,
-                                  int n_src) {
+                                  int n_src, int* n_src_slot) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) *n_src_slot = n_src;
     const size_t total = (size_t)H * n_src * 16;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
          i += (size_t)gridDim.x * blockDim.x) {
@@ -493,14 +495,48 @@ __global__ void set_memory_kernel(float* km, float* vm, int max_src, int H, cons
     }
 }
 
+// Ring (K, V and history stages) or, after the loop, the merge records
+// overlaid on it, whichever is larger, after the barrier block.
 template <int NB>
 size_t self_smem_bytes() {
-    constexpr int CP = 64 / NB;
-    return (size_t)kStages * (2 * CP * NB * 64 * sizeof(float) + CP * 8) + kStages * sizeof(uint64_t);
+    constexpr int CP = kSelfChunkRows / NB;
+    const size_t ring = (size_t)kSelfStages * (2 * CP * NB * 64 * sizeof(float) + CP * 8);
+    const size_t merge = (size_t)(8 + NB) * kPartFloats * sizeof(float);
+    return kBarBytes + (ring > merge ? ring : merge);
 }
 
+template <int NB>
 size_t cross_smem_bytes() {
-    return (size_t)kStages * 2 * kCrossChunkRows * 64 * sizeof(float) + kStages * sizeof(uint64_t);
+    const size_t ring = (size_t)kCrossStages * 2 * kCrossChunkRows * 64 * sizeof(float);
+    const size_t merge = (size_t)(8 * NB + NB) * kPartFloats * sizeof(float);
+    return kBarBytes + (ring > merge ? ring : merge);
+}
+
+// Launch with programmatic stream serialisation and, for split-KV, a cluster
+// of n_split CTAs along x.
+template <typename Params>
+cudaError_t launch_ex(void (*kernel)(Params), dim3 grid, size_t smem, int cluster_x,
+                      cudaStream_t st, const Params& p) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attrs[2];
+    int n = 0;
+    attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+    if (cluster_x > 1) {
+        attrs[n].id = cudaLaunchAttributeClusterDimension;
+        attrs[n].val.clusterDim.x = (unsigned)cluster_x;
+        attrs[n].val.clusterDim.y = 1;
+        attrs[n].val.clusterDim.z = 1;
+        ++n;
+    }
+    cfg.attrs = attrs;
+    cfg.numAttrs = n;
+    return cudaLaunchKernelEx(&cfg, kernel, p);
 }
 
 template <int NB>
@@ -510,21 +546,19 @@ cudaError_t configure_nb() {
                                          (int)self_smem_bytes<NB>());
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(cross_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)cross_smem_bytes());
+                                (int)cross_smem_bytes<NB>());
 }
 
 template <int NB>
 cudaError_t launch_self_nb(const SelfParams& p, int n_sent, cudaStream_t st) {
-    dim3 grid(p.n_split, p.H, n_sent);
-    decode_self_kernel<NB><<<grid, kThreads, self_smem_bytes<NB>(), st>>>(p);
-    return cudaGetLastError();
+    return launch_ex(decode_self_kernel<NB>, dim3(p.n_split, p.H, n_sent), self_smem_bytes<NB>(),
+                     p.n_split, st, p);
 }
 
 template <int NB>
 cudaError_t launch_cross_nb(const CrossParams& p, int n_sent, cudaStream_t st) {
-    dim3 grid(p.n_split, p.H, n_sent);
-    cross_kernel<NB><<<grid, kThreads, cross_smem_bytes(), st>>>(p);
-    return cudaGetLastError();
+    return launch_ex(cross_kernel<NB>, dim3(p.n_split, p.H, n_sent), cross_smem_bytes<NB>(),
+                     p.n_split, st, p);
 }
 
 }  // namespace
@@ -559,8 +593,16 @@ cudaError_t launch_cross(const CrossParams& p, int n_sent, int n_beams, cudaStre
 
 cudaError_t launch_reorder(uint8_t* hist, int Tp, const int* parent, int n_sent, int n_beams,
                            int* err, cudaStream_t st) {
-    reorder_kernel<<<n_sent, 128, 0, st>>>(hist, Tp, parent, n_beams, err);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(n_sent, 1, 1);
+    cfg.blockDim = dim3(128, 1, 1);
+    cfg.stream = st;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, reorder_kernel, hist, Tp, parent, n_beams, err);
 }
 
 cudaError_t launch_hist_init(uint8_t* hist, int Tp, int n_sent, cudaStream_t st) {
@@ -573,11 +615,11 @@ cudaError_t launch_hist_init(uint8_t* hist, int Tp, int n_sent, cudaStream_t st)
 
 cudaError_t launch_set_memory(float* km, float* vm, int max_src, int H, const float* k,
                               const float* v, long long stride_head, long long stride_row,
-                              int n_src, cudaStream_t st) {
+                              int n_src, int* n_src_slot, cudaStream_t st) {
     const size_t total = (size_t)H * n_src * 16;
     const int blocks = (int)((total + 255) / 256 < 2048 ? (total + 255) / 256 : 2048);
     set_memory_kernel<<<blocks, 256, 0, st>>>(km, vm, max_src, H, k, v, stride_head, stride_row,
-                                              n_src);
+                                              n_src, n_src_slot);
     return cudaGetLastError();
 }
 

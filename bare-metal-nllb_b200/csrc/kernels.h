@@ -8,11 +8,36 @@
 
 namespace nllb {
 
-// Positions per bulk-copy chunk of the self-attention cache:
-// 64 cache rows (of 64 fp32) per chunk whatever the beam count.
-inline int self_chunk_positions(int n_beams) { return 64 / n_beams; }
-constexpr int kCrossChunkRows = 64;
+// Cache rows (of 64 fp32 = 256 B) per bulk-copy chunk, and chunks in flight
+// per CTA (ring depth), for the self-attention and the cross-attention
+// kernels.  A self-attention chunk holds kSelfChunkRows / n_beams positions
+// (all beams of each position), a cross-attention chunk kCrossChunkRows
+// memory rows.  Defaults measured on B200: 32 x 3 (4 CTAs per SM) for the
+// self-attention stream, 64 x 2 for cross-attention.
+#ifndef NLLB_SELF_CHUNK_ROWS
+#define NLLB_SELF_CHUNK_ROWS 32
+#endif
+#ifndef NLLB_SELF_STAGES
+#define NLLB_SELF_STAGES 3
+#endif
+#ifndef NLLB_CROSS_CHUNK_ROWS
+#define NLLB_CROSS_CHUNK_ROWS 64
+#endif
+#ifndef NLLB_CROSS_STAGES
+#define NLLB_CROSS_STAGES 2
+#endif
+constexpr int kSelfChunkRows = NLLB_SELF_CHUNK_ROWS;
+constexpr int kSelfStages = NLLB_SELF_STAGES;
+constexpr int kCrossChunkRows = NLLB_CROSS_CHUNK_ROWS;
+constexpr int kCrossStages = NLLB_CROSS_STAGES;
+static_assert(kSelfChunkRows % 16 == 0 && kSelfChunkRows >= 16, "chunk rows: multiple of 16");
+static_assert(kCrossChunkRows % 16 == 0 && kCrossChunkRows >= 16, "chunk rows: multiple of 16");
+static_assert(kSelfStages >= 1 && kSelfStages <= 16 && kCrossStages >= 1 && kCrossStages <= 16,
+              "ring depth: 1..16 (the barrier block holds 16)");
+inline int self_chunk_positions(int n_beams) { return kSelfChunkRows / n_beams; }
 constexpr int kPartFloats = 68;  // split record per beam: m, l, pad, pad, acc[64]
+// Split-KV CTAs of one (sentence, head) form one thread-block cluster.
+constexpr int kMaxSplit = 8;
 
 // ---- decoder self-attention (decode.cu) ----------------------------------
 // Cache layout of one layer: [sentence][head][T][n_beams][64] fp32 for K and
@@ -33,8 +58,6 @@ struct SelfParams {
     int step;             // position of the new token; cache holds 0..step-1
     int n_split, pos_per_split;
     float scale_log2;     // scale * log2(e)
-    float* part;          // split records [n_sent*H][n_split][n_beams][68]
-    int* counters;        // [n_sent*H]
     int* err;
 };
 
@@ -49,8 +72,6 @@ struct CrossParams {
     int H, max_src;
     int n_split, pos_per_split;
     float scale_log2;
-    float* part;
-    int* counters;
     int* err;
 };
 
@@ -79,7 +100,7 @@ cudaError_t launch_reorder(uint8_t* hist, int Tp, const int* parent, int n_sent,
 cudaError_t launch_hist_init(uint8_t* hist, int Tp, int n_sent, cudaStream_t st);
 cudaError_t launch_set_memory(float* km, float* vm, int max_src, int H, const float* k,
                               const float* v, long long stride_head, long long stride_row,
-                              int n_src, cudaStream_t st);
+                              int n_src, int* n_src_slot, cudaStream_t st);
 cudaError_t launch_prefill(const PrefillParams& p, cudaStream_t st);
 
 }  // namespace nllb

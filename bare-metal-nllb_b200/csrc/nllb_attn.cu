@@ -36,10 +36,6 @@ int cuda_fail(cudaError_t e, const char* what) {
         if (e_ != cudaSuccess) return cuda_fail(e_, #call);    \
     } while (0)
 
-// Split-K workspace: at most this many (sentence, head, split) records per call.
-constexpr int kPartRecords = 4096;
-constexpr int kMaxSplit = 64;
-
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
@@ -58,8 +54,6 @@ struct nllb_attn_ctx {
     float* vm = nullptr;
     int* n_src_dev = nullptr;  // [L][S]
     std::vector<int> n_src_host;
-    float* part = nullptr;
-    int* counters = nullptr;
     int* err = nullptr;
     // staging for *_host calls, grown on demand
     void* stg[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
@@ -95,8 +89,6 @@ size_t device_bytes(const nllb_attn_dims& d) {
     b += 2 * mem_floats(d) * sizeof(float);
     b += (size_t)d.max_sentences * hist_rows(d) * 8;
     b += (size_t)d.n_layers * d.max_sentences * sizeof(int);
-    b += (size_t)kPartRecords * d.n_beams * kPartFloats * sizeof(float);
-    b += (size_t)kPartRecords * sizeof(int);
     b += sizeof(int);
     return b;
 }
@@ -122,7 +114,6 @@ int check_device_error(nllb_attn_ctx* c) {
     NLLB_CK(cudaMemcpy(&e, c->err, sizeof(int), cudaMemcpyDeviceToHost));
     if (e == 0) return NLLB_ATTN_OK;
     NLLB_CK(cudaMemset(c->err, 0, sizeof(int)));
-    NLLB_CK(cudaMemset(c->counters, 0, (size_t)kPartRecords * sizeof(int)));
     if (e & NLLB_DEV_ERR_TIMEOUT)
         return fail(NLLB_ATTN_ETIMEOUT, "a kernel's bounded wait for a bulk copy gave up");
     return fail(NLLB_ATTN_EINVAL, "reorder: parent index outside [0, n_beams)");
@@ -135,14 +126,13 @@ int finish_host_call(nllb_attn_ctx* c) {
 
 // Split count for a (sentence, head) grid of `units` over `len` rows in
 // chunks of `chunk` rows: enough CTAs to cover the SMs twice, each split at
-// least one chunk, within the workspace.
+// least one chunk, at most one cluster (kMaxSplit CTAs) per (sentence, head).
 void choose_split(const nllb_attn_ctx* c, int units, int len, int chunk, int* n_split, int* pps) {
     int ns = 1;
     if (len > 0 && units < 2 * c->num_sms) {
         ns = (2 * c->num_sms + units - 1) / units;
         ns = std::min(ns, (len + chunk - 1) / chunk);
         ns = std::min(ns, kMaxSplit);
-        ns = std::min(ns, kPartRecords / std::max(units, 1));
         ns = std::max(ns, 1);
     }
     int per = len > 0 ? (len + ns - 1) / ns : chunk;
@@ -181,7 +171,7 @@ void nllb_attn_destroy(nllb_attn_ctx* c) {
     cudaSetDevice(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
     for (void* p : {(void*)c->kc, (void*)c->vc, (void*)c->hist, (void*)c->km, (void*)c->vm,
-                    (void*)c->n_src_dev, (void*)c->part, (void*)c->counters, (void*)c->err})
+                    (void*)c->n_src_dev, (void*)c->err})
         if (p) cudaFree(p);
     for (void* p : c->stg)
         if (p) cudaFree(p);
@@ -243,10 +233,7 @@ int nllb_attn_create(int device, const nllb_attn_dims* dims, nllb_attn_ctx** out
         NLLB_CKC(launch_hist_init(c->hist, c->Tp, d.max_sentences, c->stream));
         c->n_src_host.assign((size_t)d.n_layers * d.max_sentences, 0);
     }
-    NLLB_CKC(cudaMalloc(&c->part, (size_t)kPartRecords * d.n_beams * kPartFloats * sizeof(float)));
-    NLLB_CKC(cudaMalloc(&c->counters, (size_t)kPartRecords * sizeof(int)));
     NLLB_CKC(cudaMalloc(&c->err, sizeof(int)));
-    NLLB_CKC(cudaMemsetAsync(c->counters, 0, (size_t)kPartRecords * sizeof(int), c->stream));
     NLLB_CKC(cudaMemsetAsync(c->err, 0, sizeof(int), c->stream));
     NLLB_CKC(cudaStreamSynchronize(c->stream));
 #undef NLLB_CKC
@@ -419,8 +406,6 @@ static int decode_self_dev(nllb_attn_ctx* c, int layer, int step, int n_sent, co
     choose_split(c, n_sent * d.n_heads, step, self_chunk_positions(d.n_beams), &p.n_split,
                  &p.pos_per_split);
     p.scale_log2 = (1.0f / std::sqrt(64.0f)) * kLog2e;
-    p.part = c->part;
-    p.counters = c->counters;
     p.err = c->err;
     NLLB_CK(launch_decode_self(p, n_sent, d.n_beams, c->stream));
     return NLLB_ATTN_OK;
@@ -514,12 +499,10 @@ static int set_memory_dev(nllb_attn_ctx* c, int layer, int sentence, int n_src, 
                           const float* v, int64_t stride_head, int64_t stride_row) {
     const nllb_attn_dims& d = c->d;
     const size_t off = (((size_t)layer * d.max_sentences + sentence) * d.n_heads) * (size_t)d.max_src * 64;
-    NLLB_CK(launch_set_memory(c->km + off, c->vm + off, d.max_src, d.n_heads, k, v, stride_head, stride_row,
-                              n_src, c->stream));
     const size_t idx = (size_t)layer * d.max_sentences + sentence;
+    NLLB_CK(launch_set_memory(c->km + off, c->vm + off, d.max_src, d.n_heads, k, v, stride_head, stride_row,
+                              n_src, c->n_src_dev + idx, c->stream));
     c->n_src_host[idx] = n_src;
-    NLLB_CK(cudaMemcpyAsync(c->n_src_dev + idx, &c->n_src_host[idx], sizeof(int), cudaMemcpyHostToDevice,
-                            c->stream));
     return NLLB_ATTN_OK;
 }
 
@@ -568,8 +551,6 @@ static int cross_dev(nllb_attn_ctx* c, int layer, int n_sent, const float* q, fl
     p.max_src = d.max_src;
     choose_split(c, n_sent * d.n_heads, max_len, kCrossChunkRows, &p.n_split, &p.pos_per_split);
     p.scale_log2 = (1.0f / std::sqrt(64.0f)) * kLog2e;
-    p.part = c->part;
-    p.counters = c->counters;
     p.err = c->err;
     NLLB_CK(launch_cross(p, n_sent, d.n_beams, c->stream));
     return NLLB_ATTN_OK;

@@ -74,7 +74,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
@@ -118,13 +118,15 @@ class ClockSampler:
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--sentences", type=int, default=128, help="sentences per GPU")
     ap.add_argument("--max-len", type=int, default=256, help="decode steps per sweep")
     ap.add_argument("--no-ops", action="store_true", help="skip the per-config op measurements")
     ap.add_argument("--cpu-sample-s", type=float, default=10.0)
+    ap.add_argument("--ncu-case", choices=("decode", "decode1", "cross", "prefill"),
+                    help="run one small fixed case for an ncu capture and exit")
     return ap.parse_args()
 
 
@@ -226,17 +228,18 @@ def run_ours(args, rank, world, local_rank):
     value = world * per_rank_bytes * args.steps / t_max / 1e9  # GB/s
     ms_per_step = t_max / args.steps * 1e3
 
-    # dominant kernel alone: events around every decode launch of one sweep
-    dec_ms = 0.0
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(T)]
+    # dominant kernel alone: the same decode launches back to back (no reorder
+    # kernels in between; identical bytes), events around the whole sweep
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_dec = 3
     with torch.cuda.stream(stream):
-        for t in range(T):
-            ctx.reorder(S, parents[t])
-            evs[t][0].record(stream)
-            ctx.decode_self(0, t, S, q[t], k[t], v[t], out[t])
-            evs[t][1].record(stream)
+        a.record(stream)
+        for _ in range(n_dec):
+            for t in range(T):
+                ctx.decode_self(0, t, S, q[t], k[t], v[t], out[t])
+        b.record(stream)
     torch.cuda.synchronize(dev)
-    dec_ms = sum(a.elapsed_time(b) for a, b in evs)
+    dec_ms = a.elapsed_time(b) / n_dec
     kernel_gbs = per_rank_bytes / (dec_ms / 1e3) / 1e9
     hbm_peak, tflops_peak, peak_kind = load_peaks()
 
@@ -292,116 +295,193 @@ def run_ours(args, rank, world, local_rank):
     return result, ops
 
 
-def measure_ops(ctx_factory, dev, hbm_peak):
-    """Single-instance numbers for the op configurations (per launch, L2
-    flushed before each launch, CUDA events around the kernel only)."""
+def graph_seconds(fn, stream, dev, reps=3):
+    """Capture fn() (which launches on `stream`) in a CUDA graph and return the
+    best of `reps` replays, timed with CUDA events on that stream."""
     import torch
-    flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=dev)
-    stream = torch.cuda.Stream(device=dev)
-    res = {}
-
-    def timed(fn, n):
-        ts = []
-        with torch.cuda.stream(stream):
-            for i in range(n):
-                flush.fill_(float(i))
-                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                a.record(stream)
-                fn(i)
-                b.record(stream)
-                ts.append((a, b))
-        torch.cuda.synchronize(dev)
-        return [a.elapsed_time(b) * 1e-3 for a, b in ts]
-
-    g = torch.Generator(device=dev)
-    g.manual_seed(2)
-    # decode op: 1 sentence, cache 1->256, permutation before each step
-    T = 256
-    c = ctx_factory(n_layers=1, n_heads=HEADS, max_sentences=1, n_beams=BEAMS, max_tgt=T, max_src=1)
-    c.set_stream(stream.cuda_stream)
-    q, k, v = (torch.randn((T, BEAMS, DMODEL), generator=g, device=dev) for _ in range(3))
-    out = torch.empty_like(q)
-    par = torch.argsort(torch.rand((T, BEAMS), generator=g, device=dev), dim=-1).to(torch.int32)
-
-    def dec(t):
-        c.decode_self(0, t, 1, q[t], k[t], v[t], out[t])
-
     with torch.cuda.stream(stream):
-        for t in range(T):  # warm-up sweep
-            c.reorder(1, par[t])
-            dec(t)
-    c.reset()
-    ts = []
+        fn()
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        fn()
+    best = None
     with torch.cuda.stream(stream):
-        for t in range(T):
-            c.reorder(1, par[t])
-            flush.fill_(float(t))
+        graph.replay()
+        for _ in range(reps):
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
-            dec(t)
+            graph.replay()
             b.record(stream)
-            ts.append((a, b))
-    torch.cuda.synchronize(dev)
-    c.sync()
-    tt = [a.elapsed_time(b) * 1e-3 for a, b in ts]
-    tot_bytes = sweep_bytes_per_sentence(T)
-    res["decode_self_config"] = {
-        "shape": "1 sentence x 4 beams x 16 heads x 64, cache 1->256, permutation per step",
-        "gbs": round(tot_bytes / sum(tt) / 1e9, 1),
-        "us_per_launch_mean": round(sum(tt) / T * 1e6, 2),
-        "us_at_len_256": round(tt[-1] * 1e6, 2),
-        "gbs_at_len_256": round(step_bytes_per_sentence(256) / tt[-1] / 1e9, 1),
-        "frac_of_hbm_peak": round(tot_bytes / sum(tt) / 1e9 / hbm_peak, 4),
-        "l2": "flushed (256 MB write) before every launch",
-    }
-    c.close()
+            torch.cuda.synchronize(dev)
+            t = a.elapsed_time(b) * 1e-3
+            best = t if best is None else min(best, t)
+    del graph
+    return best
 
-    # cross op: Q [4,16,1,64], memory [16,512,64], 128 steps
-    n_src, steps = 512, 128
-    c = ctx_factory(n_layers=1, n_heads=HEADS, max_sentences=1, n_beams=BEAMS, max_tgt=4, max_src=n_src)
-    c.set_stream(stream.cuda_stream)
-    Km, Vm = (torch.randn((HEADS, n_src, HEAD_DIM), generator=g, device=dev) for _ in range(2))
-    c.set_memory(0, 0, n_src, Km, Vm, n_src * HEAD_DIM, HEAD_DIM)
-    qc = torch.randn((steps, BEAMS, DMODEL), generator=g, device=dev)
+
+def measure_ops(ctx_factory, dev, hbm_peak, tflops_note=""):
+    """The three op configurations at their own sizes.  Each is one CUDA graph
+    replaying the configuration over R independent instances in rotation, so
+    that consecutive launches touch disjoint data and the working set exceeds
+    the 126 MB L2 (no flush kernel inside the timed region)."""
+    import torch
+    stream = torch.cuda.Stream(device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(2)
+    res = {}
+
+    # decode op: 4 beams x 16 heads x 64, cache 1->256, permutation before each step
+    T, R = 256, 24
+    ctxs = [ctx_factory(n_layers=1, n_heads=HEADS, max_sentences=1, n_beams=BEAMS, max_tgt=T,
+                        max_src=1) for _ in range(R)]
+    for c in ctxs:
+        c.set_stream(stream.cuda_stream)
+    q, k, v = (torch.randn((R, T, BEAMS, DMODEL), generator=g, device=dev) for _ in range(3))
+    out = torch.empty_like(q)
+    par = torch.argsort(torch.rand((R, T, BEAMS), generator=g, device=dev), dim=-1).to(torch.int32)
+
+    def dec_sweep():
+        for t in range(T):
+            for r, c in enumerate(ctxs):
+                c.reorder(1, par[r, t])
+                c.decode_self(0, t, 1, q[r, t], k[r, t], v[r, t], out[r, t])
+
+    t_all = graph_seconds(dec_sweep, stream, dev)
+    for c in ctxs:
+        c.sync()
+        c.close()
+    tot = R * sweep_bytes_per_sentence(T)
+    res["decode_self_config"] = {
+        "shape": "1 sentence x 4 beams x 16 heads x 64, cache 1->256, permutation reorder before every step",
+        "gbs": round(tot / t_all / 1e9, 1),
+        "frac_of_hbm_peak": round(tot / t_all / 1e9 / hbm_peak, 4),
+        "us_per_step": round(t_all / (T * R) * 1e6, 2),
+        "how": f"CUDA graph of the sweep over {R} independent sentences in rotation "
+               f"({R * 2 * BEAMS * HEADS * T * ROW_BYTES / 1e6:.0f} MB of cache > L2); "
+               "a step = reorder + decode launch",
+    }
+    del q, k, v, out
+
+    # cross op: Q [4,16,1,64] over memory [16,512,64], 128 steps
+    n_src, steps, R = 512, 128, 32
+    ctxs = [ctx_factory(n_layers=1, n_heads=HEADS, max_sentences=1, n_beams=BEAMS, max_tgt=4,
+                        max_src=n_src) for _ in range(R)]
+    mems = []
+    for c in ctxs:
+        c.set_stream(stream.cuda_stream)
+        Km, Vm = (torch.randn((HEADS, n_src, HEAD_DIM), generator=g, device=dev) for _ in range(2))
+        with torch.cuda.stream(stream):
+            c.set_memory(0, 0, n_src, Km, Vm, n_src * HEAD_DIM, HEAD_DIM)
+        mems.append((Km, Vm))
+    qc = torch.randn((R, steps, BEAMS, DMODEL), generator=g, device=dev)
     oc = torch.empty_like(qc)
-    timed(lambda i: c.cross(0, 1, qc[i], oc[i]), 8)
-    tt = timed(lambda i: c.cross(0, 1, qc[i], oc[i]), steps)
-    c.sync()
+
+    def cross_steps():
+        for i in range(steps):
+            for r, c in enumerate(ctxs):
+                c.cross(0, 1, qc[r, i], oc[r, i])
+
+    t_all = graph_seconds(cross_steps, stream, dev)
+    for c in ctxs:
+        c.sync()
+        c.close()
     step_b = 2 * HEADS * n_src * ROW_BYTES + 2 * BEAMS * HEADS * ROW_BYTES
     res["cross_config"] = {
         "shape": "4 beams x 16 heads x 64 over memory [16,512,64], 128 steps",
-        "gbs": round(step_b * steps / sum(tt) / 1e9, 1),
-        "us_per_launch_mean": round(sum(tt) / steps * 1e6, 2),
-        "frac_of_hbm_peak": round(step_b * steps / sum(tt) / 1e9 / hbm_peak, 4),
-        "l2": "flushed (256 MB write) before every launch",
+        "gbs": round(R * steps * step_b / t_all / 1e9, 1),
+        "frac_of_hbm_peak": round(R * steps * step_b / t_all / 1e9 / hbm_peak, 4),
+        "us_per_step": round(t_all / (steps * R) * 1e6, 2),
+        "how": f"CUDA graph of 128 steps over {R} independent memories in rotation "
+               f"({R * 2 * HEADS * n_src * ROW_BYTES / 1e6:.0f} MB > L2)",
     }
-    c.close()
+    del mems, qc, oc
 
     # prefill op: [8,16,128,64], key padding 0-31
-    B, S = 8, 128
+    B, S, R = 8, 128, 16
     c = ctx_factory(n_layers=0, n_heads=HEADS, max_sentences=0, n_beams=BEAMS, max_tgt=0, max_src=0)
     c.set_stream(stream.cuda_stream)
-    qp, kp, vp = (torch.randn((B, HEADS, S, HEAD_DIM), generator=g, device=dev) for _ in range(3))
+    qp, kp, vp = (torch.randn((R, B, HEADS, S, HEAD_DIM), generator=g, device=dev) for _ in range(3))
     op = torch.empty_like(qp)
-    vl = (S - torch.randint(0, 32, (B,), generator=g, device=dev)).to(torch.int32)
-    args = c.prefill_args(qp, kp, vp, op, B, HEADS, S, (HEADS * S * 64, S * 64, 64), vl)
-    timed(lambda i: c.prefill(args), 5)
-    tt = timed(lambda i: c.prefill(args), 50)
+    vl = (S - torch.randint(0, 32, (R, B), generator=g, device=dev)).to(torch.int32)
+    args = [c.prefill_args(qp[r], kp[r], vp[r], op[r], B, HEADS, S, (HEADS * S * 64, S * 64, 64), vl[r])
+            for r in range(R)]
+
+    def prefill_rounds():
+        for _ in range(4):
+            for a in args:
+                c.prefill(a)
+
+    t_all = graph_seconds(prefill_rounds, stream, dev)
     c.sync()
+    c.close()
     flops = 4 * B * HEADS * S * S * HEAD_DIM
-    tmed = statistics.median(tt)
+    per = t_all / (4 * R)
     res["prefill_config"] = {
         "shape": "Q,K,V [8,16,128,64], scale 1/8, last 0-31 keys masked",
-        "tflops_dense": round(flops / tmed / 1e12, 2),
-        "us_median": round(tmed * 1e6, 2),
-        "path": "FFMA (fp32 SIMT)",
+        "tflops_dense": round(flops / per / 1e12, 2),
+        "us_per_launch": round(per * 1e6, 2),
+        "how": f"CUDA graph of 4 rounds over {R} independent inputs ({R * 4 * 16.8:.0f} MB > L2)",
     }
-    c.close()
     return res
+
+
+def ncu_case(which: str) -> None:
+    """Small, fixed cases for ncu captures (a few launches of one kernel each)."""
+    import torch
+    import nllb_attn as na
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    if which == "decode":
+        # 32 sentences x 4 beams x 16 heads, sweep to length 256 (last launches: 268 MB > L2)
+        S, T = 32, 256
+        c = na.Context(0, n_layers=1, max_sentences=S, n_beams=BEAMS, max_tgt=T, max_src=1)
+        q, k, v = (torch.randn((S, BEAMS, DMODEL), generator=g, device=dev) for _ in range(3))
+        out = torch.empty_like(q)
+        par = torch.argsort(torch.rand((S, BEAMS), generator=g, device=dev), -1).to(torch.int32)
+        for t in range(T):
+            c.reorder(S, par)
+            c.decode_self(0, t, S, q, k, v, out)
+    elif which == "decode1":
+        # one sentence (the decode-op configuration), sweep to length 256
+        T = 256
+        c = na.Context(0, n_layers=1, max_sentences=1, n_beams=BEAMS, max_tgt=T, max_src=1)
+        q, k, v = (torch.randn((BEAMS, DMODEL), generator=g, device=dev) for _ in range(3))
+        out = torch.empty_like(q)
+        par = torch.argsort(torch.rand((1, BEAMS), generator=g, device=dev), -1).to(torch.int32)
+        for t in range(T):
+            c.reorder(1, par)
+            c.decode_self(0, t, 1, q, k, v, out)
+    elif which == "cross":
+        c = na.Context(0, n_layers=1, max_sentences=1, n_beams=BEAMS, max_tgt=4, max_src=512)
+        Km, Vm = (torch.randn((HEADS, 512, HEAD_DIM), generator=g, device=dev) for _ in range(2))
+        c.set_memory(0, 0, 512, Km, Vm, 512 * HEAD_DIM, HEAD_DIM)
+        qc = torch.randn((BEAMS, DMODEL), generator=g, device=dev)
+        oc = torch.empty_like(qc)
+        for _ in range(3):
+            c.cross(0, 1, qc, oc)
+    elif which == "prefill":
+        B, S = 8, 128
+        c = na.Context(0, n_layers=0, max_sentences=0)
+        qp, kp, vp = (torch.randn((B, HEADS, S, HEAD_DIM), generator=g, device=dev) for _ in range(3))
+        op = torch.empty_like(qp)
+        vl = (S - torch.randint(0, 32, (B,), generator=g, device=dev)).to(torch.int32)
+        a = c.prefill_args(qp, kp, vp, op, B, HEADS, S, (HEADS * S * 64, S * 64, 64), vl)
+        for _ in range(3):
+            c.prefill(a)
+    else:
+        raise SystemExit(f"unknown --ncu-case {which}")
+    c.sync()
+    c.close()
+    print(f"ncu case {which}: ok")
 
 
 def main():
     args = parse_args()
+    if args.ncu_case:
+        ncu_case(args.ncu_case)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -470,8 +550,8 @@ def main():
                          "traffic": traffic,
                          "kernel": "decode_self_kernel<4>",
                          "peak_kind": res["peak_kind"],
-                         "how": "algorithmic bytes of one sweep / sum of CUDA-event durations of its "
-                                f"{T} decode launches on the launching stream"},
+                         "how": f"algorithmic bytes of one sweep / duration of its {T} decode launches run "
+                                "back to back on the launching stream (CUDA events around 3 sweeps)"},
             "cpu_baseline": cpu,
             "e2e": res["e2e"],
             "gpu_launches": 2 * T * args.steps,
