@@ -87,6 +87,7 @@ struct PrefillParams {
     const float* mask;
     long long msb, msh;
     float scale_log2;
+    int* err;
 };
 
 // Per-device kernel attributes (dynamic shared memory); call once per device.
@@ -102,5 +103,7 @@ cudaError_t launch_set_memory(float* km, float* vm, int max_src, int H, const fl
                               const float* v, long long stride_head, long long stride_row,
                               int n_src, int* n_src_slot, cudaStream_t st);
 cudaError_t launch_prefill(const PrefillParams& p, cudaStream_t st);
+// seq_len range served by the tcgen05 kernel (others: FFMA kernel)
+bool prefill_uses_tensor_cores(int seq_len);
 
 }  // namespace nllb

@@ -291,8 +291,9 @@ static int check_prefill(const nllb_attn_prefill_args* a) {
     return NLLB_ATTN_OK;
 }
 
-static PrefillParams prefill_params(const nllb_attn_prefill_args* a) {
+static PrefillParams prefill_params(const nllb_attn_prefill_args* a, int* err) {
     PrefillParams p;
+    p.err = err;
     p.q = a->q;
     p.k = a->k;
     p.v = a->v;
@@ -316,7 +317,7 @@ int nllb_attn_prefill(nllb_attn_ctx* c, const nllb_attn_prefill_args* a) {
     int rc = check_prefill(a);
     if (rc) return rc;
     if ((rc = set_device(c))) return rc;
-    NLLB_CK(launch_prefill(prefill_params(a), c->stream));
+    NLLB_CK(launch_prefill(prefill_params(a, c->err), c->stream));
     return NLLB_ATTN_OK;
 }
 
@@ -366,7 +367,7 @@ int nllb_attn_prefill_host(nllb_attn_ctx* c, const nllb_attn_prefill_args* a) {
                                 c->stream));
         d.mask = static_cast<float*>(c->stg[5]);
     }
-    NLLB_CK(launch_prefill(prefill_params(&d), c->stream));
+    NLLB_CK(launch_prefill(prefill_params(&d, c->err), c->stream));
     NLLB_CK(cudaMemcpyAsync(a->out, dout, bytes, cudaMemcpyDeviceToHost, c->stream));
     return finish_host_call(c);
 }

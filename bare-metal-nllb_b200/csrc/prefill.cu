@@ -1,16 +1,26 @@
 // prefill.cu -- encoder self-attention prefill, fp32 (sm_100a).
 //
-// Flash-attention form of attention_head_flash (tensor.c:286-332) /
-// encoder.c:166-205: one CTA per (64-query tile, head, sequence) streams
-// 64-key tiles of K and V through shared memory with an online softmax in
-// base 2, so nothing of size seq x seq is ever stored.  FFMA with fp32
-// accumulation: every product is an exact fp32 product, matching the
-// reference's arithmetic to rounding.
+// Two kernels compute attention_head_flash (tensor.c:286-332) /
+// encoder.c:166-205 for every (sequence, head, query row):
 //
-// Thread tile: 128 threads as 8 (ty) x 16 (tx).  A thread owns query rows
-// ty + 8i (i < 8); for scores it owns key columns tx + 16j (j < 4), for the
-// output it owns dims 4tx..4tx+3.  Row statistics reduce over the 16 tx
-// lanes of a half-warp with xor-shuffles.
+// prefill_tc_kernel (seq_len 33..256): 5th-generation tensor cores.  One CTA
+//   per (128-query tile, head, sequence) with 8 warps: query row r is TMEM
+//   lane r, owned by two threads (warps w and w+4 reach the same lane quarter)
+//   that take alternate 32-key halves of every 64-key chunk.  Inputs are split while they are staged into
+//   128-byte-swizzled shared memory: hi = x with the low 13 mantissa bits
+//   cleared (exact in tf32), lo = x - hi.  Each product is taken as
+//   hi*hi' + hi*lo' + lo*hi' (3xTF32 on tcgen05.mma kind::tf32, fp32
+//   accumulation in TMEM), which keeps fp32 accuracy.  The softmax is the
+//   reference's two-pass form: all scores of a row sit in TMEM (256 columns),
+//   pass 1 takes the row max, pass 2 forms P = exp(s - max) 64 keys at a time,
+//   stages P (split) and V^T (split) in shared memory and accumulates
+//   O += P.V in TMEM; the row sum is divided out at the end.  Q.K^T runs in
+//   groups of 128 keys (one N=128 MMA group for seq_len <= 128).  The loads of
+//   Q and the first K group are all issued before any is stored, and the V
+//   chunks travel in registers while the score MMAs and softmax run, so a CTA
+//   pays about two DRAM latencies, not one per tile.
+// prefill_ffma_kernel (other lengths): SIMT fp32 flash attention with an
+//   online softmax over 64-key tiles.
 #include "device_common.cuh"
 #include "kernels.h"
 
@@ -29,6 +39,9 @@ __global__ void __launch_bounds__(kThreads) prefill_ffma_kernel(const PrefillPar
     float* Ks = Qs + BQ * LDS;    // [BK][LDS]
     float* Vs = Ks + BK * LDS;    // [BK][LDS]
     float* Ps = Vs + BK * LDS;    // [BQ][LDS]
+
+    pdl_launch_dependents();
+    pdl_wait_primary();  // inputs come from earlier kernels
 
     const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
@@ -171,18 +184,316 @@ __global__ void __launch_bounds__(kThreads) prefill_ffma_kernel(const PrefillPar
     }
 }
 
+
+// ---------------------------------------------------------------------------
+// tcgen05 kernel
+// ---------------------------------------------------------------------------
+constexpr int TC_Q = 128;      // queries per CTA (MMA M)
+constexpr int TC_KG = 128;     // keys per score group (MMA N of Q.K^T)
+constexpr int TC_K = 64;       // keys per P.V chunk (MMA K of P.V)
+constexpr int TC_MAX_S = 256;  // score columns held in TMEM
+constexpr uint32_t TC_TMEM_COLS = 512;
+// shared-memory plan (bytes from a 1024-byte aligned base); every operand is
+// K-major, 128-byte swizzled, in 32-column k-blocks of rows*128 bytes
+constexpr uint32_t SQH = 0, SQL = 32768;        // Q hi/lo   [2][128 rows][128 B]
+constexpr uint32_t SKH = 65536, SKL = 98304;    // K hi/lo   [2][128 keys][128 B]
+constexpr uint32_t SVH = 131072, SVL = 147456;  // V^T hi/lo [2][64 dims][128 B]
+constexpr uint32_t SPH = 163840, SPL = 196608;  // P hi/lo   [2][128 rows][128 B]
+constexpr uint32_t SBAR = 229376;
+constexpr uint32_t TC_SMEM = SBAR + 64 + 1024;  // + alignment slack
+
+// byte offset of (row, col) in a K-major SWIZZLE_128B operand of `nrows`
+// rows x 64 fp32 columns: 32-column k-blocks of nrows*128 B, 128-B rows,
+// 16-B chunks XOR-ed with row % 8.
+__device__ __forceinline__ uint32_t sw128_off(int row, int col, int nrows) {
+    return (uint32_t)((col >> 5) * nrows * 128 + row * 128 + ((((col & 31) >> 2) ^ (row & 7)) << 4) +
+                      ((col & 3) << 2));
+}
+
+__device__ __forceinline__ void split_store4(unsigned char* hi_base, unsigned char* lo_base, uint32_t off,
+                                             float4 x) {
+    float4 h = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
+    float4 l = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
+    *reinterpret_cast<float4*>(hi_base + off) = h;
+    *reinterpret_cast<float4*>(lo_base + off) = l;
+}
+
+// D[128 x N] (+)= A[128 x 64] . B[N x 64]^T with both operands split:
+// Ah.Bh + Ah.Bl + Al.Bh over 8 k-steps of 8 (A has 128 rows, B has N rows).
+template <int N>
+__device__ __forceinline__ void mma_3xtf32(uint32_t d, uint32_t ah, uint32_t al, uint32_t bh, uint32_t bl,
+                                           bool accumulate_first) {
+    constexpr uint32_t idesc = umma_idesc_tf32(128, N);
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t ao = (ks >> 2) * (128 * 128) + (ks & 3) * 32;
+        const uint32_t bo = (ks >> 2) * (N * 128) + (ks & 3) * 32;
+        const uint64_t dah = umma_desc_k_sw128(ah + ao), dal = umma_desc_k_sw128(al + ao);
+        const uint64_t dbh = umma_desc_k_sw128(bh + bo), dbl = umma_desc_k_sw128(bl + bo);
+        tc_mma_tf32(d, dah, dbh, idesc, (accumulate_first || ks > 0) ? 1u : 0u);
+        tc_mma_tf32(d, dah, dbl, idesc, 1u);
+        tc_mma_tf32(d, dal, dbh, idesc, 1u);
+    }
+}
+
+__device__ __forceinline__ float4 ldg_row4(const float* base, long long row_off, int c4, bool valid) {
+    return valid ? __ldg(reinterpret_cast<const float4*>(base + row_off) + c4) : make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+constexpr int TC_THREADS = 256;  // two threads per query row / TMEM lane
+
+__device__ __forceinline__ float ex2_approx(float x) {  // 2^x, -inf -> +0
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const PrefillParams p) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    const uint32_t base_addr = (raw_addr + 1023u) & ~1023u;
+    unsigned char* base = smem_raw + (base_addr - raw_addr);
+    uint64_t* mma_bar = reinterpret_cast<uint64_t*>(base + SBAR);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + SBAR + 8);
+    volatile int* s_abort = reinterpret_cast<volatile int*>(base + SBAR + 16);
+    __shared__ float s_red[TC_THREADS];
+
+    pdl_launch_dependents();
+
+    const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int quarter = warp & 3, half = warp >> 2;  // TMEM lane quarter, column half
+    const int S = p.S;
+    const int q0 = qt * TC_Q;
+    const long long hbase = (long long)b * p.sb + (long long)h * p.sh;
+
+    if (warp == 0) tmem_alloc(tmem_slot, TC_TMEM_COLS);
+    if (tid == 0) {
+        mbar_init(mma_bar, 1);
+        fence_barrier_init();
+        *s_abort = 0;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tS = tmem + lane_off;             // scores: columns [0, 256)
+    const uint32_t tO = tmem + lane_off + TC_MAX_S;  // output: columns [256, 320)
+
+    pdl_wait_primary();  // q, k, v, lengths and mask come from earlier kernels
+
+    int kv_len = S;
+    bool uniform = false;  // valid_len 0: equal weights over all keys (see prefill_ffma_kernel)
+    if (p.valid_len) {
+        const int vl = __ldg(p.valid_len + b);
+        if (vl <= 0) uniform = true;
+        else kv_len = min(vl, S);
+    }
+    const int n_kg = (kv_len + TC_KG - 1) / TC_KG;  // score groups of 128 keys
+    const int n_kc = (kv_len + TC_K - 1) / TC_K;    // P.V chunks of 64 keys
+    const int rloc = quarter * 32 + lane;           // query row within the tile = TMEM lane
+    const int row = q0 + rloc;
+    const float* mrow = (p.mask && row < S)
+                            ? p.mask + (long long)b * p.msb + (long long)h * p.msh + (long long)row * S
+                            : nullptr;
+    const float sl2 = p.scale_log2;
+
+    uint32_t phase = 0;
+    auto wait_mma = [&]() -> bool {
+        if (!mbar_wait_bounded(mma_bar, phase & 1u)) *s_abort = 1;
+        ++phase;
+        __syncthreads();
+        return *s_abort == 0;
+    };
+    // 32 scores (base-2 logits) of this thread's row, keys j0..j0+31
+    auto scores32 = [&](int j0, float* v) {
+        tmem_ld32(tS + (uint32_t)j0, v);
+        if (uniform) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = (j0 + i < kv_len) ? 0.f : -INFINITY;
+        } else if (mrow) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                v[i] = (j0 + i < kv_len) ? fmaf(__ldg(mrow + j0 + i), kLog2e, v[i] * sl2) : -INFINITY;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = (j0 + i < kv_len) ? v[i] * sl2 : -INFINITY;
+        }
+    };
+    // K group g: 128 keys x 16 float4 = 8 float4 per thread
+    auto load_k_group = [&](int g, float4* kr) {
+#pragma unroll
+        for (int it = 0; it < 8; ++it) {
+            const int r = (it * TC_THREADS + tid) >> 4, key = g * TC_KG + r;
+            kr[it] = ldg_row4(p.k, hbase + (long long)key * p.sr, tid & 15, key < kv_len);
+        }
+    };
+    // V chunk c: 64 keys x 16 float4 = 4 float4 per thread; a warp covers 32 keys of one float4 column
+    auto load_v_chunk = [&](int c, float4* vr) {
+#pragma unroll
+        for (int it = 0; it < 4; ++it) {
+            const int idx = it * TC_THREADS + tid;
+            const int jj = (idx & 31) + 32 * (idx >> 9), c4 = (idx >> 5) & 15, key = c * TC_K + jj;
+            vr[it] = ldg_row4(p.v, hbase + (long long)key * p.sr, c4, key < kv_len);
+        }
+    };
+
+    // every load of Q and of the first K group is issued before any is stored
+    float4 qr[8], kr[8];
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+        const int r = (it * TC_THREADS + tid) >> 4;
+        qr[it] = ldg_row4(p.q, hbase + (long long)(q0 + r) * p.sr, tid & 15, q0 + r < S);
+    }
+    load_k_group(0, kr);
+#pragma unroll
+    for (int it = 0; it < 8; ++it)
+        split_store4(base + SQH, base + SQL, sw128_off((it * TC_THREADS + tid) >> 4, (tid & 15) * 4, TC_Q), qr[it]);
+
+    bool ok = true;
+    for (int g = 0; g < n_kg && ok; ++g) {
+        if (g > 0) {
+            if (!(ok = wait_mma())) break;  // group g-1 has read KH/KL
+            load_k_group(g, kr);
+        }
+#pragma unroll
+        for (int it = 0; it < 8; ++it)
+            split_store4(base + SKH, base + SKL, sw128_off((it * TC_THREADS + tid) >> 4, (tid & 15) * 4, TC_KG),
+                         kr[it]);
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        if (tid == 0) {
+            tc_fence_after();
+            mma_3xtf32<TC_KG>(tmem + (uint32_t)(g * TC_KG), base_addr + SQH, base_addr + SQL, base_addr + SKH,
+                              base_addr + SKL, false);
+            tc_commit(mma_bar);
+        }
+    }
+    // the first two V chunks travel while the score MMAs run
+    float4 vr0[4], vr1[4];
+    load_v_chunk(0, vr0);
+    if (n_kc > 1) load_v_chunk(1, vr1);
+    if (ok) ok = wait_mma();
+    tc_fence_after();
+
+    // pass 1: row max (this thread: columns half*32 + 64c .. +31 of every chunk)
+    float mx = -INFINITY;
+    if (ok) {
+        for (int kc = 0; kc < n_kc; ++kc) {
+            float v[32];
+            scores32(kc * TC_K + half * 32, v);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) mx = fmaxf(mx, v[i]);
+        }
+        s_red[tid] = mx;
+    }
+    __syncthreads();
+    if (ok) mx = fmaxf(mx, s_red[tid ^ 128]);
+
+    // pass 2: P chunk by chunk, O += P . V_chunk
+    float sum = 0.f;
+    for (int kc = 0; kc < n_kc && ok; ++kc) {
+        if (kc > 0 && !(ok = wait_mma())) break;  // previous chunk's MMAs have read P and V^T
+        {
+            float v[32];
+            scores32(kc * TC_K + half * 32, v);
+#pragma unroll
+            for (int c4 = 0; c4 < 8; ++c4) {
+                float e[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    e[i] = ex2_approx(v[c4 * 4 + i] - mx);
+                    sum += e[i];
+                }
+                split_store4(base + SPH, base + SPL, sw128_off(rloc, half * 32 + c4 * 4, TC_Q),
+                             make_float4(e[0], e[1], e[2], e[3]));
+            }
+        }
+        // V chunk kc (in vr0 for even kc, vr1 for odd), transposed: row = head dim, column = key
+        float4* vr = (kc & 1) ? vr1 : vr0;
+#pragma unroll
+        for (int it = 0; it < 4; ++it) {
+            const int idx = it * TC_THREADS + tid;
+            const int jj = (idx & 31) + 32 * (idx >> 9), c4 = (idx >> 5) & 15;
+            const float xs[4] = {vr[it].x, vr[it].y, vr[it].z, vr[it].w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t off = sw128_off(c4 * 4 + i, jj, 64);
+                const float hv = tf32_hi(xs[i]);
+                *reinterpret_cast<float*>(base + SVH + off) = hv;
+                *reinterpret_cast<float*>(base + SVL + off) = xs[i] - hv;
+            }
+        }
+        if (kc + 2 < n_kc) load_v_chunk(kc + 2, vr);  // two chunks ahead
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        if (tid == 0) {
+            tc_fence_after();
+            mma_3xtf32<TC_K>(tmem + TC_MAX_S, base_addr + SPH, base_addr + SPL, base_addr + SVH, base_addr + SVL,
+                             kc > 0);
+            tc_commit(mma_bar);
+        }
+    }
+    if (ok) ok = wait_mma();
+    tc_fence_after();
+
+    if (ok) {
+        s_red[tid] = sum;  // wait_mma ended with a barrier, pass-1 values are consumed
+        __syncthreads();
+        sum += s_red[tid ^ 128];
+        float o[32];
+        tmem_ld32(tO + (uint32_t)(half * 32), o);
+        if (row < S) {
+            const float inv = 1.0f / sum;
+            float4* dst = reinterpret_cast<float4*>(p.out + hbase + (long long)row * p.sr) + half * 8;
+#pragma unroll
+            for (int c4 = 0; c4 < 8; ++c4)
+                dst[c4] = make_float4(o[4 * c4] * inv, o[4 * c4 + 1] * inv, o[4 * c4 + 2] * inv, o[4 * c4 + 3] * inv);
+        }
+    } else if (tid == 0) {
+        atomicOr(p.err, NLLB_DEV_ERR_TIMEOUT);
+        (void)mbar_wait_bounded(mma_bar, phase & 1u);  // last chance for MMAs in flight
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, TC_TMEM_COLS);
+    }
+}
+
 }  // namespace
 
 cudaError_t configure_prefill_kernels() {
     const int smem = 4 * BQ * LDS * (int)sizeof(float);
-    return cudaFuncSetAttribute(prefill_ffma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(prefill_ffma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM);
 }
 
+bool prefill_uses_tensor_cores(int seq_len) { return seq_len > 32 && seq_len <= TC_MAX_S; }
+
 cudaError_t launch_prefill(const PrefillParams& p, cudaStream_t st) {
-    const int smem = 4 * BQ * LDS * (int)sizeof(float);
-    dim3 grid((p.S + BQ - 1) / BQ, p.H, p.B);
-    prefill_ffma_kernel<<<grid, kThreads, smem, st>>>(p);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    cfg.stream = st;
+    cfg.blockDim = dim3(128, 1, 1);
+    if (prefill_uses_tensor_cores(p.S)) {
+        cfg.blockDim = dim3(TC_THREADS, 1, 1);
+        cfg.gridDim = dim3((p.S + TC_Q - 1) / TC_Q, p.H, p.B);
+        cfg.dynamicSmemBytes = TC_SMEM;
+        return cudaLaunchKernelEx(&cfg, prefill_tc_kernel, p);
+    }
+    cfg.gridDim = dim3((p.S + BQ - 1) / BQ, p.H, p.B);
+    cfg.dynamicSmemBytes = 4 * BQ * LDS * sizeof(float);
+    return cudaLaunchKernelEx(&cfg, prefill_ffma_kernel, p);
 }
 
 }  // namespace nllb

@@ -56,7 +56,7 @@ def test_prefill_config1_full():
     assert_attn_close(out, po.prefill(q, k, v, vl), "config1")
 
 
-@pytest.mark.parametrize("S", [1, 2, 63, 64, 65, 130, 300, 512])
+@pytest.mark.parametrize("S", [1, 2, 32, 33, 63, 64, 65, 128, 129, 130, 255, 256, 257, 300, 512])
 def test_prefill_lengths(ctx, S):
     rng = np.random.default_rng(S)
     q, k, v = (rng.standard_normal((2, 3, S, 64), dtype=np.float32) for _ in range(3))
@@ -92,13 +92,24 @@ def test_prefill_additive_mask_per_head(ctx):
     assert_attn_close(out, ref, "mask")
 
 
-def test_prefill_all_keys_masked_is_mean_of_v(ctx):
-    """valid_len 0: the reference's -1e9 on every key gives equal weights."""
+@pytest.mark.parametrize("S", [9, 100])
+def test_prefill_all_keys_masked_is_mean_of_v(ctx, S):
+    """valid_len 0: the reference's -1e9 on every key gives equal weights
+    (S=9 runs on the FFMA kernel, S=100 on the tensor-core kernel)."""
     rng = np.random.default_rng(12)
-    q, k, v = (rng.standard_normal((1, 1, 9, 64), dtype=np.float32) for _ in range(3))
-    out = run_prefill(ctx, q, k, v, np.array([0], np.int32))
-    assert_attn_close(out, po.prefill(q, k, v, np.array([0], np.int32)), "all masked")
+    q, k, v = (rng.standard_normal((2, 1, S, 64), dtype=np.float32) for _ in range(3))
+    vl = np.array([0, S - 3], np.int32)
+    out = run_prefill(ctx, q, k, v, vl)
+    assert_attn_close(out, po.prefill(q, k, v, vl), "all masked")
     assert_attn_close(out[0, 0, 3], v[0, 0].mean(axis=0), "mean")
+
+
+def test_prefill_large_values_keep_fp32_accuracy(ctx):
+    """Scores far from zero (|q.k/8| ~ 30): the 3xTF32 split keeps softmax
+    weights at fp32 accuracy where single-pass TF32 would not."""
+    rng = np.random.default_rng(13)
+    q, k, v = (3.0 * rng.standard_normal((1, 4, 128, 64), dtype=np.float32) for _ in range(3))
+    assert_attn_close(run_prefill(ctx, q, k, v), po.prefill(q, k, v), "large")
 
 
 def test_prefill_host_variant(ctx):
