@@ -288,7 +288,7 @@ def run_ours(args, rank, world, local_rank):
         "peak_kind": peak_kind, "e2e": e2e,
     }
     ops = None
-    if not args.no_ops and rank == 0:
+    if not args.no_ops and rank == 0 and world == 1:
         ops = measure_ops(ctx_factory=lambda **kw: na.Context(local_rank, **kw), dev=dev,
                           hbm_peak=hbm_peak)
     ctx.close()
@@ -554,7 +554,7 @@ def main():
                                 "back to back on the launching stream (CUDA events around 3 sweeps)"},
             "cpu_baseline": cpu,
             "e2e": res["e2e"],
-            "gpu_launches": 2 * T * args.steps,
+            "gpu_launches": world * 2 * T * args.steps,
             "clocks": res["clocks"],
         }
         if ops:
