@@ -1,0 +1,31 @@
+// attn_internal.h -- the attention context, shared by the C ABI (nllb_attn.cu)
+// and the translation engine (engine.cu), which writes the encoder memory of
+// many sentences in one launch.
+#pragma once
+#include <cstddef>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "nllb_attn.h"
+
+struct nllb_attn_ctx {
+    int device = 0;
+    int num_sms = 148;
+    nllb_attn_dims d{};
+    int Tp = 0;  // beam-history rows per sentence (max_tgt rounded up, +2 for 16-B copies)
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    float* kc = nullptr;  // [L][S][H][T][NB][64]
+    float* vc = nullptr;
+    unsigned char* hist = nullptr;  // [S][Tp][8]
+    float* km = nullptr;  // [L][S][H][max_src][64]
+    float* vm = nullptr;
+    int* n_src_dev = nullptr;  // [L][S]
+    std::vector<int> n_src_host;
+    int* err = nullptr;
+    // staging for *_host calls, grown on demand
+    void* stg[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+    size_t stg_bytes[6] = {0, 0, 0, 0, 0, 0};
+};
+

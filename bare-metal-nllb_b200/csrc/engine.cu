@@ -1,0 +1,790 @@
+// engine.cu -- sentence-batched translation on one GPU (include/nllb_translate.h).
+//
+// Host side: safetensors loading, the forward passes as kernel sequences and
+// the beam search bookkeeping, restating the reference engine's control flow
+// (main.c:294-528, encoder.c:250-287, decoder.c:156-233) for many sentences
+// in lockstep.  Device side: engine_kernels.cu plus the attention kernels.
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "attn_internal.h"
+#include "engine_kernels.h"
+#include "nllb_translate.h"
+
+using namespace nllb;
+
+namespace nllb {
+int set_error(int status, const std::string& msg);  // nllb_attn.cu
+}
+
+namespace {
+
+constexpr int D = 1024, H = 16, FFN = 4096, LAYERS = 12, VOCAB = 256206, NB = 4;
+constexpr int LANG_START = 256000;
+
+#define ENG_CK(call)                                                                              \
+    do {                                                                                          \
+        cudaError_t e_ = (call);                                                                  \
+        if (e_ != cudaSuccess)                                                                    \
+            return nllb::set_error(NLLB_ATTN_ECUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+#define ENG_RC(call)                 \
+    do {                             \
+        int r_ = (call);             \
+        if (r_ != NLLB_ATTN_OK) return r_; \
+    } while (0)
+
+// ---- safetensors header: {"name": {"dtype": .., "shape": [..], "data_offsets": [a, b]}, ...}
+struct TensorInfo {
+    std::string dtype;
+    std::vector<long long> shape;
+    long long begin = 0, end = 0;
+};
+
+class HeaderParser {
+  public:
+    explicit HeaderParser(const std::string& s) : s_(s) {}
+    bool parse(std::map<std::string, TensorInfo>* out) {
+        skip();
+        if (!eat('{')) return false;
+        skip();
+        if (peek() == '}') return true;
+        for (;;) {
+            std::string name;
+            if (!str(&name)) return false;
+            skip();
+            if (!eat(':')) return false;
+            TensorInfo ti;
+            bool is_tensor = false;
+            if (!object(&ti, &is_tensor)) return false;
+            if (is_tensor) (*out)[name] = ti;
+            skip();
+            if (eat(',')) {
+                skip();
+                continue;
+            }
+            return eat('}');
+        }
+    }
+
+  private:
+    const std::string& s_;
+    size_t i_ = 0;
+    char peek() const { return i_ < s_.size() ? s_[i_] : '\0'; }
+    void skip() {
+        while (i_ < s_.size() && (s_[i_] == ' ' || s_[i_] == '\n' || s_[i_] == '\t' || s_[i_] == '\r')) ++i_;
+    }
+    bool eat(char c) {
+        skip();
+        if (peek() != c) return false;
+        ++i_;
+        return true;
+    }
+    bool str(std::string* o) {
+        skip();
+        if (!eat('"')) return false;
+        while (i_ < s_.size() && s_[i_] != '"') {
+            if (s_[i_] == '\\' && i_ + 1 < s_.size()) ++i_;
+            o->push_back(s_[i_++]);
+        }
+        return eat('"');
+    }
+    bool number(long long* v) {
+        skip();
+        size_t j = i_;
+        if (peek() == '-') ++i_;
+        while (i_ < s_.size() && (isdigit((unsigned char)s_[i_]) || s_[i_] == '.' || s_[i_] == 'e' ||
+                                  s_[i_] == 'E' || s_[i_] == '+' || s_[i_] == '-'))
+            ++i_;
+        if (j == i_) return false;
+        *v = std::stoll(s_.substr(j, i_ - j));
+        return true;
+    }
+    bool int_list(std::vector<long long>* o) {
+        if (!eat('[')) return false;
+        skip();
+        if (eat(']')) return true;
+        for (;;) {
+            long long v;
+            if (!number(&v)) return false;
+            o->push_back(v);
+            if (eat(',')) continue;
+            return eat(']');
+        }
+    }
+    bool skip_value() {  // strings, numbers, flat objects/arrays of those
+        skip();
+        const char c = peek();
+        if (c == '"') {
+            std::string t;
+            return str(&t);
+        }
+        if (c == '{' || c == '[') {
+            const char close = (c == '{') ? '}' : ']';
+            ++i_;
+            int depth = 1;
+            bool in_str = false;
+            while (i_ < s_.size() && depth > 0) {
+                const char d = s_[i_++];
+                if (in_str) {
+                    if (d == '\\') ++i_;
+                    else if (d == '"') in_str = false;
+                } else if (d == '"') {
+                    in_str = true;
+                } else if (d == '{' || d == '[') {
+                    ++depth;
+                } else if (d == '}' || d == ']') {
+                    --depth;
+                }
+            }
+            (void)close;
+            return depth == 0;
+        }
+        long long v;
+        return number(&v);
+    }
+    bool object(TensorInfo* ti, bool* is_tensor) {
+        skip();
+        if (peek() != '{') return skip_value();
+        ++i_;
+        skip();
+        if (eat('}')) return true;
+        for (;;) {
+            std::string key;
+            if (!str(&key)) return false;
+            if (!eat(':')) return false;
+            if (key == "dtype") {
+                if (!str(&ti->dtype)) return false;
+            } else if (key == "shape") {
+                if (!int_list(&ti->shape)) return false;
+            } else if (key == "data_offsets") {
+                std::vector<long long> o;
+                if (!int_list(&o) || o.size() != 2) return false;
+                ti->begin = o[0];
+                ti->end = o[1];
+                *is_tensor = true;
+            } else if (!skip_value()) {
+                return false;
+            }
+            if (eat(',')) continue;
+            return eat('}');
+        }
+    }
+};
+
+struct Lin {
+    int8_t* w = nullptr;
+    float* inv = nullptr;
+    float* b = nullptr;
+    int out = 0, in = 0;
+};
+
+}  // namespace
+
+struct nllb_model {
+    int device = 0;
+    int max_sentences = 0, max_src = 0, max_gen = 0;
+    cudaStream_t stream = nullptr;
+    std::vector<void*> allocs;
+    int8_t* emb = nullptr;
+    float* emb_inv = nullptr;
+    struct Enc {
+        Lin qkv, out, fc1, fc2;
+        float *ln1g, *ln1b, *ln2g, *ln2b;
+    } enc[LAYERS];
+    struct Dec {
+        Lin qkv, out, xq, xkv, xout, fc1, fc2;
+        float *ln1g, *ln1b, *ln2g, *ln2b, *ln3g, *ln3b;
+    } dec[LAYERS];
+    float *enc_lng = nullptr, *enc_lnb = nullptr, *dec_lng = nullptr, *dec_lnb = nullptr;
+    float* pos_table = nullptr;  // row p: sinusoid of actual position p (encoder.c:27-36)
+    int pos_rows = 0;
+    nllb_attn_ctx* attn = nullptr;
+    // decision margins of the last translate call, [sentence][step]
+    std::vector<std::vector<float>> margins;
+};
+
+namespace {
+
+template <typename T>
+int dev_alloc(nllb_model* m, T** p, size_t count) {
+    void* v = nullptr;
+    ENG_CK(cudaMalloc(&v, std::max<size_t>(count, 1) * sizeof(T)));
+    m->allocs.push_back(v);
+    *p = static_cast<T*>(v);
+    return NLLB_ATTN_OK;
+}
+
+struct Loader {
+    nllb_model* m;
+    const uint8_t* data;
+    std::map<std::string, TensorInfo> tensors;
+
+    int find(const std::string& name, const char* dtype, long long elems, const TensorInfo** out) {
+        auto it = tensors.find(name);
+        if (it == tensors.end()) return nllb::set_error(NLLB_ATTN_EINVAL, "tensor missing: " + name);
+        long long n = 1;
+        for (long long s : it->second.shape) n *= s;
+        if (it->second.dtype != dtype || n != elems)
+            return nllb::set_error(NLLB_ATTN_EINVAL, "unexpected dtype/shape: " + name);
+        *out = &it->second;
+        return NLLB_ATTN_OK;
+    }
+    template <typename T>
+    int upload(const std::string& name, const char* dtype, long long elems, T** dst) {
+        const TensorInfo* ti;
+        ENG_RC(find(name, dtype, elems, &ti));
+        ENG_RC(dev_alloc(m, dst, (size_t)elems));
+        ENG_CK(cudaMemcpy(*dst, data + ti->begin, (size_t)elems * sizeof(T), cudaMemcpyHostToDevice));
+        return NLLB_ATTN_OK;
+    }
+    // weight, 1/weight_scale (tensor.c:75) and bias of an INT8 linear layer
+    int linear(const std::string& prefix, int out_f, int in_f, Lin* L) {
+        L->out = out_f;
+        L->in = in_f;
+        ENG_RC(upload(prefix + "/weight", "I8", (long long)out_f * in_f, &L->w));
+        float* scale = nullptr;
+        ENG_RC(upload(prefix + "/weight_scale", "F32", out_f, &scale));
+        ENG_RC(dev_alloc(m, &L->inv, out_f));
+        ENG_CK(launch_reciprocal(L->inv, scale, out_f, m->stream));
+        if (tensors.count(prefix + "/bias")) ENG_RC(upload(prefix + "/bias", "F32", out_f, &L->b));
+        return NLLB_ATTN_OK;
+    }
+    int norm(const std::string& prefix, float** g, float** b) {
+        *g = *b = nullptr;
+        if (tensors.count(prefix + "/gamma")) ENG_RC(upload(prefix + "/gamma", "F32", D, g));
+        if (tensors.count(prefix + "/beta")) ENG_RC(upload(prefix + "/beta", "F32", D, b));
+        return NLLB_ATTN_OK;
+    }
+};
+
+// Sinusoidal table with the reference's float expressions (encoder.c:27-36).
+std::vector<float> position_table(int rows) {
+    std::vector<float> t((size_t)rows * D);
+    const int half = D / 2;
+    for (int p = 0; p < rows; ++p) {
+        for (int i = 0; i < half; ++i) {
+            const float freq = expf(-(float)i * logf(10000.0f) / (float)(half - 1));
+            const float angle = (float)p * freq;
+            t[(size_t)p * D + i] = sinf(angle);
+            t[(size_t)p * D + i + half] = cosf(angle);
+        }
+    }
+    return t;
+}
+
+struct Beam {
+    std::vector<int> tokens;
+    int n = 0;
+    float score = 0.f, eos_score = 0.f;
+    bool finished = false;
+};
+struct Cand {
+    int beam, token;
+    float score;
+};
+
+}  // namespace
+
+extern "C" {
+
+void nllb_model_free(nllb_model* m) {
+    if (!m) return;
+    cudaSetDevice(m->device);
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    if (m->attn) nllb_attn_destroy(m->attn);
+    for (void* p : m->allocs) cudaFree(p);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+}
+
+int nllb_model_load(const char* path, int device, int max_sentences, int max_src, int max_gen, nllb_model** out) {
+    if (!path || !out) return nllb::set_error(NLLB_ATTN_EINVAL, "path and out are required");
+    *out = nullptr;
+    if (max_sentences < 1 || max_src < 2 || max_gen < 6)
+        return nllb::set_error(NLLB_ATTN_EINVAL, "max_sentences >= 1, max_src >= 2, max_gen >= 6 required");
+    nllb_attn_dims dims{LAYERS, H, 64, max_sentences, NB, max_gen, max_src};
+    nllb_attn_ctx* attn = nullptr;
+    int rc = nllb_attn_create(device, &dims, &attn);
+    if (rc) return rc;
+    nllb_model* m = new nllb_model();
+    m->device = device;
+    m->attn = attn;
+    m->max_sentences = max_sentences;
+    m->max_src = max_src;
+    m->max_gen = max_gen;
+    auto fail = [&](int r) {
+        nllb_model_free(m);
+        return r;
+    };
+    if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess)
+        return fail(nllb::set_error(NLLB_ATTN_ECUDA, "cudaStreamCreate failed"));
+    nllb_attn_set_stream(attn, m->stream);
+
+    const int fd = open(path, O_RDONLY);
+    if (fd < 0) return fail(nllb::set_error(NLLB_ATTN_EINVAL, std::string("cannot open ") + path));
+    struct stat st;
+    fstat(fd, &st);
+    const size_t size = (size_t)st.st_size;
+    void* map = mmap(nullptr, size, PROT_READ, MAP_PRIVATE, fd, 0);
+    close(fd);
+    if (map == MAP_FAILED) return fail(nllb::set_error(NLLB_ATTN_EINVAL, "mmap failed"));
+    const uint8_t* base = static_cast<const uint8_t*>(map);
+    uint64_t hlen = 0;
+    memcpy(&hlen, base, 8);
+    Loader L{m, base + 8 + hlen, {}};
+    int r = NLLB_ATTN_OK;
+    if (8 + hlen > size) r = nllb::set_error(NLLB_ATTN_EINVAL, "truncated safetensors header");
+    if (!r) {
+        std::string header(reinterpret_cast<const char*>(base + 8), (size_t)hlen);
+        HeaderParser hp(header);
+        if (!hp.parse(&L.tensors)) r = nllb::set_error(NLLB_ATTN_EINVAL, "cannot parse safetensors header");
+    }
+    auto load_all = [&]() -> int {
+        // shared embedding (loader.c:327-335): one device copy serves both stacks
+        ENG_RC(L.upload("decoder/embeddings/weight", "I8", (long long)VOCAB * D, &m->emb));
+        float* es = nullptr;
+        ENG_RC(L.upload("decoder/embeddings/weight_scale", "F32", VOCAB, &es));
+        ENG_RC(dev_alloc(m, &m->emb_inv, VOCAB));
+        ENG_CK(launch_reciprocal(m->emb_inv, es, VOCAB, m->stream));
+        for (int i = 0; i < LAYERS; ++i) {
+            const std::string p = "encoder/layer_" + std::to_string(i);
+            auto& E = m->enc[i];
+            ENG_RC(L.linear(p + "/self_attention/linear_0", 3 * D, D, &E.qkv));
+            ENG_RC(L.linear(p + "/self_attention/linear_1", D, D, &E.out));
+            ENG_RC(L.linear(p + "/ffn/linear_0", FFN, D, &E.fc1));
+            ENG_RC(L.linear(p + "/ffn/linear_1", D, FFN, &E.fc2));
+            ENG_RC(L.norm(p + "/self_attention/layer_norm", &E.ln1g, &E.ln1b));
+            ENG_RC(L.norm(p + "/ffn/layer_norm", &E.ln2g, &E.ln2b));
+        }
+        ENG_RC(L.norm("encoder/layer_norm", &m->enc_lng, &m->enc_lnb));
+        for (int i = 0; i < LAYERS; ++i) {
+            const std::string p = "decoder/layer_" + std::to_string(i);
+            auto& Dl = m->dec[i];
+            ENG_RC(L.linear(p + "/self_attention/linear_0", 3 * D, D, &Dl.qkv));
+            ENG_RC(L.linear(p + "/self_attention/linear_1", D, D, &Dl.out));
+            ENG_RC(L.linear(p + "/attention/linear_0", D, D, &Dl.xq));
+            ENG_RC(L.linear(p + "/attention/linear_1", 2 * D, D, &Dl.xkv));
+            ENG_RC(L.linear(p + "/attention/linear_2", D, D, &Dl.xout));
+            ENG_RC(L.linear(p + "/ffn/linear_0", FFN, D, &Dl.fc1));
+            ENG_RC(L.linear(p + "/ffn/linear_1", D, FFN, &Dl.fc2));
+            ENG_RC(L.norm(p + "/self_attention/layer_norm", &Dl.ln1g, &Dl.ln1b));
+            ENG_RC(L.norm(p + "/attention/layer_norm", &Dl.ln2g, &Dl.ln2b));
+            ENG_RC(L.norm(p + "/ffn/layer_norm", &Dl.ln3g, &Dl.ln3b));
+        }
+        ENG_RC(L.norm("decoder/layer_norm", &m->dec_lng, &m->dec_lnb));
+        m->pos_rows = std::max(max_src, max_gen) + 4;
+        const std::vector<float> pt = position_table(m->pos_rows);
+        ENG_RC(dev_alloc(m, &m->pos_table, pt.size()));
+        ENG_CK(cudaMemcpy(m->pos_table, pt.data(), pt.size() * sizeof(float), cudaMemcpyHostToDevice));
+        ENG_CK(cudaStreamSynchronize(m->stream));
+        return NLLB_ATTN_OK;
+    };
+    if (!r) r = load_all();
+    munmap(map, size);
+    if (r) return fail(r);
+    *out = m;
+    return NLLB_ATTN_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+int run_linear(nllb_model* m, const Lin& L, const float* x, int M, float* out, const float* residual, int relu,
+               int cblock, int mask_from = -1) {
+    LinearArgs a;
+    a.x = x;
+    a.ldx = L.in;
+    a.w = L.w;
+    a.inv_scale = L.inv;
+    a.bias = L.b;
+    a.out = out;
+    a.residual = residual;
+    a.M = M;
+    a.N = L.out;
+    a.K = L.in;
+    a.cblock = cblock;
+    a.relu = relu;
+    a.mask_from = mask_from;
+    ENG_CK(launch_linear(a, m->stream));
+    return NLLB_ATTN_OK;
+}
+
+// Buffers of one translate call.
+struct Work {
+    int n_sent = 0, S = 0, rows_enc = 0, rows = 0;
+    float *ex = nullptr, *eh = nullptr, *eqkv = nullptr, *eattn = nullptr, *effn = nullptr, *ekv = nullptr;
+    int *etok = nullptr, *epos = nullptr, *evalid = nullptr;
+    float *x = nullptr, *h = nullptr, *qkv = nullptr, *qx = nullptr, *attn = nullptr, *ffn = nullptr;
+    float* logits = nullptr;
+    int *tok = nullptr, *hist = nullptr, *ntok = nullptr, *parent = nullptr, *top_tok = nullptr;
+    float* top_lp = nullptr;
+    unsigned char* active = nullptr;
+    std::vector<void*> allocs;
+    ~Work() {
+        for (void* p : allocs) cudaFree(p);
+    }
+    template <typename T>
+    int alloc(T** p, size_t n) {
+        void* v = nullptr;
+        ENG_CK(cudaMalloc(&v, std::max<size_t>(n, 1) * sizeof(T)));
+        allocs.push_back(v);
+        *p = static_cast<T*>(v);
+        return NLLB_ATTN_OK;
+    }
+};
+
+int encode(nllb_model* m, Work& w, const std::vector<int>& n_src) {
+    const int R = w.rows_enc;
+    ENG_CK(launch_embed_pos(w.ex, w.etok, w.epos, 0, m->emb, m->emb_inv, m->pos_table, 32.0f, R, VOCAB, m->stream));
+    for (int l = 0; l < LAYERS; ++l) {
+        auto& E = m->enc[l];
+        ENG_CK(launch_layernorm(w.eh, w.ex, nullptr, E.ln1g, E.ln1b, R, m->stream));
+        ENG_RC(run_linear(m, E.qkv, w.eh, R, w.eqkv, nullptr, 0, D));
+        nllb_attn_prefill_args a{};
+        a.q = w.eqkv;
+        a.k = w.eqkv + (size_t)R * D;
+        a.v = w.eqkv + (size_t)2 * R * D;
+        a.out = w.eattn;
+        a.batch = w.n_sent;
+        a.n_heads = H;
+        a.seq_len = w.S;
+        a.head_dim = 64;
+        a.stride_batch = (int64_t)w.S * D;
+        a.stride_head = 64;
+        a.stride_row = D;
+        a.valid_len = w.evalid;
+        a.scale = 1.0f / sqrtf(64.0f);
+        ENG_RC(nllb_attn_prefill(m->attn, &a));
+        ENG_RC(run_linear(m, E.out, w.eattn, R, w.ex, w.ex, 0, D));
+        ENG_CK(launch_layernorm(w.eh, w.ex, nullptr, E.ln2g, E.ln2b, R, m->stream));
+        ENG_RC(run_linear(m, E.fc1, w.eh, R, w.effn, nullptr, 1, FFN));
+        ENG_RC(run_linear(m, E.fc2, w.effn, R, w.ex, w.ex, 0, D));
+    }
+    ENG_CK(launch_layernorm(w.eh, w.ex, nullptr, m->enc_lng, m->enc_lnb, R, m->stream));  // encoder_out
+    // cross-attention memory of every layer (decoder.c:118-125, projected once)
+    nllb_attn_ctx* c = m->attn;
+    const size_t layer_floats = (size_t)c->d.max_sentences * H * (size_t)c->d.max_src * 64;
+    for (int l = 0; l < LAYERS; ++l) {
+        ENG_RC(run_linear(m, m->dec[l].xkv, w.eh, R, w.ekv, nullptr, 0, D));
+        ENG_CK(launch_set_memory_batched(c->km + l * layer_floats, c->vm + l * layer_floats,
+                                         c->n_src_dev + (size_t)l * c->d.max_sentences, c->d.max_src, H, w.ekv,
+                                         w.ekv + (size_t)R * D, (long long)w.S * D, w.evalid, w.n_sent, w.S,
+                                         m->stream));
+        for (int s = 0; s < w.n_sent; ++s) c->n_src_host[(size_t)l * c->d.max_sentences + s] = n_src[s];
+    }
+    return NLLB_ATTN_OK;
+}
+
+// One decoder step for every row (decoder.c:199-233): token w.tok[row] at
+// position `step`; leaves the final-LayerNorm output in w.h.
+int decode_step(nllb_model* m, Work& w, int step) {
+    const int R = w.rows;
+    ENG_CK(launch_embed_pos(w.x, w.tok, nullptr, step + 2, m->emb, m->emb_inv, m->pos_table, 32.0f, R, VOCAB, m->stream));
+    for (int l = 0; l < LAYERS; ++l) {
+        auto& Dl = m->dec[l];
+        ENG_CK(launch_layernorm(w.h, w.x, nullptr, Dl.ln1g, Dl.ln1b, R, m->stream));
+        ENG_RC(run_linear(m, Dl.qkv, w.h, R, w.qkv, nullptr, 0, D));
+        ENG_RC(nllb_attn_decode_self(m->attn, l, step, w.n_sent, w.qkv, w.qkv + (size_t)R * D,
+                                     w.qkv + (size_t)2 * R * D, w.attn));
+        ENG_RC(run_linear(m, Dl.out, w.attn, R, w.x, w.x, 0, D));
+        ENG_CK(launch_layernorm(w.h, w.x, nullptr, Dl.ln2g, Dl.ln2b, R, m->stream));
+        ENG_RC(run_linear(m, Dl.xq, w.h, R, w.qx, nullptr, 0, D));
+        ENG_RC(nllb_attn_cross(m->attn, l, w.n_sent, w.qx, w.attn));
+        ENG_RC(run_linear(m, Dl.xout, w.attn, R, w.x, w.x, 0, D));
+        ENG_CK(launch_layernorm(w.h, w.x, nullptr, Dl.ln3g, Dl.ln3b, R, m->stream));
+        ENG_RC(run_linear(m, Dl.fc1, w.h, R, w.ffn, nullptr, 1, FFN));
+        ENG_RC(run_linear(m, Dl.fc2, w.ffn, R, w.x, w.x, 0, D));
+    }
+    ENG_CK(launch_layernorm(w.h, w.x, nullptr, m->dec_lng, m->dec_lnb, R, m->stream));
+    return NLLB_ATTN_OK;
+}
+
+// Tied vocabulary projection with language rows masked (decoder.c:319-354),
+// penalties (main.c:186-213) and log-softmax + top-k (main.c:154-182).
+int vocab_topk(nllb_model* m, Work& w, int k, bool penalties, const nllb_translate_opts& o) {
+    Lin E;
+    E.w = m->emb;
+    E.inv = m->emb_inv;
+    E.b = nullptr;
+    E.out = VOCAB;
+    E.in = D;
+    ENG_RC(run_linear(m, E, w.h, w.rows, w.logits, nullptr, 0, VOCAB, LANG_START));
+    if (penalties)
+        ENG_CK(launch_penalties(w.logits, VOCAB, w.hist, m->max_gen, w.ntok, w.active, w.rows,
+                                o.repetition_penalty, o.no_repeat_ngram, m->stream));
+    ENG_CK(launch_logsoftmax_topk(w.logits, VOCAB, VOCAB, w.rows, w.active, k, w.top_tok, w.top_lp, m->stream));
+    return NLLB_ATTN_OK;
+}
+
+double ms_since(std::chrono::steady_clock::time_point t0) {
+    return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+}
+
+}  // namespace
+
+extern "C" int nllb_translate(nllb_model* m, int n_sent, const int* src_tokens, const int* src_offsets,
+                              int tgt_lang, const nllb_translate_opts* opts, int* out_tokens, int* out_len,
+                              float* out_score, nllb_translate_stats* stats) {
+    if (!m || !src_tokens || !src_offsets) return nllb::set_error(NLLB_ATTN_EINVAL, "model and sources required");
+    if (n_sent < 1 || n_sent > m->max_sentences)
+        return nllb::set_error(NLLB_ATTN_ECAPACITY, "n_sentences outside [1, max_sentences]");
+    if (tgt_lang < 0 || tgt_lang >= VOCAB) return nllb::set_error(NLLB_ATTN_EINVAL, "tgt_lang out of range");
+    nllb_translate_opts o{m->max_gen, 1.2f, 2};
+    if (opts) o = *opts;
+    if (o.max_gen < 6 || o.max_gen > m->max_gen)
+        return nllb::set_error(NLLB_ATTN_ECAPACITY, "opts.max_gen outside [6, model max_gen]");
+    if (!(o.no_repeat_ngram == 0 || o.no_repeat_ngram == 2))
+        return nllb::set_error(NLLB_ATTN_EINVAL, "no_repeat_ngram must be 0 or 2");
+    ENG_CK(cudaSetDevice(m->device));
+    const auto t_start = std::chrono::steady_clock::now();
+
+    Work w;
+    w.n_sent = n_sent;
+    std::vector<int> n_src(n_sent), max_out(n_sent);
+    int S = 0;
+    for (int s = 0; s < n_sent; ++s) {
+        n_src[s] = src_offsets[s + 1] - src_offsets[s];
+        if (n_src[s] < 1 || n_src[s] > m->max_src)
+            return nllb::set_error(NLLB_ATTN_ECAPACITY, "a source length is outside [1, max_src]");
+        for (int i = src_offsets[s]; i < src_offsets[s + 1]; ++i)
+            if (src_tokens[i] < 0 || src_tokens[i] >= VOCAB)
+                return nllb::set_error(NLLB_ATTN_EINVAL, "source token id out of range");
+        S = std::max(S, n_src[s]);
+        max_out[s] = std::min(3 * n_src[s] + 10, o.max_gen - 4);  // main.c:315-316
+    }
+    w.S = S;
+    w.rows_enc = n_sent * S;
+    w.rows = n_sent * NB;
+    const size_t RE = (size_t)w.rows_enc, R = (size_t)w.rows;
+    ENG_RC(w.alloc(&w.ex, RE * D));
+    ENG_RC(w.alloc(&w.eh, RE * D));
+    ENG_RC(w.alloc(&w.eqkv, RE * 3 * D));
+    ENG_RC(w.alloc(&w.eattn, RE * D));
+    ENG_RC(w.alloc(&w.effn, RE * FFN));
+    ENG_RC(w.alloc(&w.ekv, RE * 2 * D));
+    ENG_RC(w.alloc(&w.etok, RE));
+    ENG_RC(w.alloc(&w.epos, RE));
+    ENG_RC(w.alloc(&w.evalid, n_sent));
+    ENG_RC(w.alloc(&w.x, R * D));
+    ENG_RC(w.alloc(&w.h, R * D));
+    ENG_RC(w.alloc(&w.qkv, R * 3 * D));
+    ENG_RC(w.alloc(&w.qx, R * D));
+    ENG_RC(w.alloc(&w.attn, R * D));
+    ENG_RC(w.alloc(&w.ffn, R * FFN));
+    ENG_RC(w.alloc(&w.logits, R * VOCAB));
+    ENG_RC(w.alloc(&w.tok, R));
+    ENG_RC(w.alloc(&w.hist, R * m->max_gen));
+    ENG_RC(w.alloc(&w.ntok, R));
+    ENG_RC(w.alloc(&w.parent, R));
+    ENG_RC(w.alloc(&w.top_tok, R * 8));
+    ENG_RC(w.alloc(&w.top_lp, R * 8));
+    ENG_RC(w.alloc(&w.active, R));
+
+    // ---- encoder (padded to the longest source; keys beyond n_src masked)
+    {
+        std::vector<int> tok(RE, 1), pos(RE);
+        for (int s = 0; s < n_sent; ++s)
+            for (int t = 0; t < S; ++t) {
+                if (t < n_src[s]) tok[(size_t)s * S + t] = src_tokens[src_offsets[s] + t];
+                pos[(size_t)s * S + t] = t + 2;  // NLLB position offset (encoder.c:29)
+            }
+        ENG_CK(cudaMemcpyAsync(w.etok, tok.data(), RE * sizeof(int), cudaMemcpyHostToDevice, m->stream));
+        ENG_CK(cudaMemcpyAsync(w.epos, pos.data(), RE * sizeof(int), cudaMemcpyHostToDevice, m->stream));
+        ENG_CK(cudaMemcpyAsync(w.evalid, n_src.data(), n_sent * sizeof(int), cudaMemcpyHostToDevice, m->stream));
+        ENG_RC(nllb_attn_reset(m->attn));
+        ENG_RC(encode(m, w, n_src));
+        ENG_CK(cudaStreamSynchronize(m->stream));
+        ENG_RC(nllb_attn_sync(m->attn));
+    }
+    const double t_enc = ms_since(t_start);
+    const auto t_dec0 = std::chrono::steady_clock::now();
+
+    // ---- beam state (main.c:317-330)
+    const int G = o.max_gen;
+    std::vector<Beam> beams((size_t)n_sent * NB);
+    std::vector<std::vector<Beam>> completed(n_sent);
+    std::vector<char> done(n_sent, 0);
+    for (auto& b : beams) {
+        b.tokens.assign(G, 0);
+        b.tokens[0] = 2;  // NLLB decoder start token (main.c:324)
+        b.n = 1;
+    }
+    m->margins.assign(n_sent, {});
+    std::vector<int> tok_h(R), parent_h(R), ntok_h(R), hist_h(R * (size_t)m->max_gen, 0);
+    std::vector<unsigned char> active_h(R);
+    std::vector<int> top_tok_h(R * 8);
+    std::vector<float> top_lp_h(R * 8);
+
+    auto upload_tokens = [&]() -> int {
+        ENG_CK(cudaMemcpyAsync(w.tok, tok_h.data(), R * sizeof(int), cudaMemcpyHostToDevice, m->stream));
+        return NLLB_ATTN_OK;
+    };
+
+    // step 0: decoder start token on every beam (main.c:331-333; all beams start equal)
+    std::fill(tok_h.begin(), tok_h.end(), 2);
+    ENG_RC(upload_tokens());
+    ENG_RC(decode_step(m, w, 0));
+    // step 1: target language token, top-4 of beam 0 seeds the beams (main.c:343-392)
+    std::fill(tok_h.begin(), tok_h.end(), tgt_lang);
+    ENG_RC(upload_tokens());
+    ENG_RC(decode_step(m, w, 1));
+    for (size_t r = 0; r < R; ++r) active_h[r] = (r % NB) == 0;
+    ENG_CK(cudaMemcpyAsync(w.active, active_h.data(), R, cudaMemcpyHostToDevice, m->stream));
+    ENG_RC(vocab_topk(m, w, NB, false, o));
+    ENG_CK(cudaMemcpyAsync(top_tok_h.data(), w.top_tok, R * NB * sizeof(int), cudaMemcpyDeviceToHost, m->stream));
+    ENG_CK(cudaMemcpyAsync(top_lp_h.data(), w.top_lp, R * NB * sizeof(float), cudaMemcpyDeviceToHost, m->stream));
+    ENG_CK(cudaStreamSynchronize(m->stream));
+    for (int s = 0; s < n_sent; ++s)
+        for (int b = 0; b < NB; ++b) {
+            Beam& bm = beams[(size_t)s * NB + b];
+            const size_t r0 = (size_t)s * NB;  // beam 0's row
+            bm.tokens[1] = tgt_lang;
+            bm.tokens[2] = top_tok_h[r0 * NB + b];
+            bm.n = 3;
+            bm.score = top_lp_h[r0 * NB + b];
+            bm.eos_score = 0.f;
+            bm.finished = bm.tokens[2] == 2;
+        }
+    int steps_run = 2;
+
+    // ---- steps 2 .. max_out+1 (main.c:411-511)
+    for (int step = 2;; ++step) {
+        bool any = false;
+        for (int s = 0; s < n_sent; ++s) {
+            if (done[s]) continue;
+            int n_active = 0;
+            for (int b = 0; b < NB; ++b) n_active += !beams[(size_t)s * NB + b].finished;
+            if (step >= max_out[s] + 2 || n_active == 0) {
+                done[s] = 1;
+                continue;
+            }
+            any = true;
+        }
+        if (!any) break;
+        if (step >= m->max_gen) return nllb::set_error(NLLB_ATTN_ECAPACITY, "decode ran past max_gen");
+        for (int s = 0; s < n_sent; ++s)
+            for (int b = 0; b < NB; ++b) {
+                const size_t r = (size_t)s * NB + b;
+                const Beam& bm = beams[r];
+                tok_h[r] = bm.tokens[bm.n - 1];
+                ntok_h[r] = bm.n;
+                active_h[r] = (!done[s] && !bm.finished) ? 1 : 0;
+                std::copy(bm.tokens.begin(), bm.tokens.begin() + bm.n, hist_h.begin() + r * m->max_gen);
+            }
+        ENG_RC(upload_tokens());
+        ENG_CK(cudaMemcpyAsync(w.ntok, ntok_h.data(), R * sizeof(int), cudaMemcpyHostToDevice, m->stream));
+        ENG_CK(cudaMemcpyAsync(w.active, active_h.data(), R, cudaMemcpyHostToDevice, m->stream));
+        ENG_CK(cudaMemcpyAsync(w.hist, hist_h.data(), hist_h.size() * sizeof(int), cudaMemcpyHostToDevice,
+                               m->stream));
+        ENG_RC(decode_step(m, w, step));
+        ENG_RC(vocab_topk(m, w, 8, true, o));
+        ENG_CK(cudaMemcpyAsync(top_tok_h.data(), w.top_tok, R * 8 * sizeof(int), cudaMemcpyDeviceToHost, m->stream));
+        ENG_CK(cudaMemcpyAsync(top_lp_h.data(), w.top_lp, R * 8 * sizeof(float), cudaMemcpyDeviceToHost, m->stream));
+        ENG_CK(cudaStreamSynchronize(m->stream));
+        ++steps_run;
+
+        // candidate selection per sentence (main.c:413-488)
+        for (int s = 0; s < n_sent; ++s) {
+            Beam* bs = &beams[(size_t)s * NB];
+            if (done[s]) {
+                for (int b = 0; b < NB; ++b) parent_h[(size_t)s * NB + b] = b;
+                continue;
+            }
+            std::vector<Cand> cands;
+            cands.reserve(NB * 8 + NB);
+            for (int b = 0; b < NB; ++b)
+                if (bs[b].finished) cands.push_back({b, 2, bs[b].score});
+            for (int b = 0; b < NB; ++b) {
+                if (bs[b].finished) continue;
+                const size_t r = (size_t)s * NB + b;
+                for (int k = 0; k < 8; ++k) cands.push_back({b, top_tok_h[r * 8 + k], bs[b].score + top_lp_h[r * 8 + k]});
+            }
+            // the reference's exchange sort, descending (main.c:456-460)
+            const int nc = (int)cands.size();
+            for (int i = 0; i < nc - 1; ++i)
+                for (int j = i + 1; j < nc; ++j)
+                    if (cands[j].score > cands[i].score) std::swap(cands[i], cands[j]);
+            float gap = INFINITY;
+            for (int i = 0; i + 1 < std::min(nc, NB + 1); ++i) gap = std::min(gap, cands[i].score - cands[i + 1].score);
+            m->margins[s].push_back(gap);
+            Beam nb[NB];
+            for (int i = 0; i < NB; ++i) {
+                const int par = cands[i].beam;
+                nb[i].tokens = bs[par].tokens;
+                nb[i].n = bs[par].n;
+                nb[i].tokens[nb[i].n++] = cands[i].token;
+                nb[i].score = cands[i].score;
+                nb[i].finished = cands[i].token == 2;
+                nb[i].eos_score = nb[i].finished ? cands[i].score - bs[par].score : bs[par].eos_score;
+                parent_h[(size_t)s * NB + i] = par;
+                if (nb[i].finished && completed[s].size() < (size_t)(2 * NB)) completed[s].push_back(nb[i]);
+            }
+            for (int i = 0; i < NB; ++i) bs[i] = nb[i];
+        }
+        ENG_CK(cudaMemcpyAsync(w.parent, parent_h.data(), R * sizeof(int), cudaMemcpyHostToDevice, m->stream));
+        ENG_RC(nllb_attn_reorder(m->attn, n_sent, w.parent));
+    }
+    ENG_RC(nllb_attn_sync(m->attn));
+    const double t_dec = ms_since(t_dec0);
+
+    // ---- final choice (main.c:511-546)
+    long long total_out = 0;
+    for (int s = 0; s < n_sent; ++s) {
+        std::vector<Beam>& cp = completed[s];
+        for (int b = 0; b < NB; ++b) {
+            const Beam& bm = beams[(size_t)s * NB + b];
+            if (bm.finished && cp.size() < (size_t)(2 * NB)) cp.push_back(bm);
+        }
+        if (cp.empty()) cp.push_back(beams[(size_t)s * NB]);
+        int bi = 0;
+        float bn = -1e30f;
+        for (int c = 0; c < (int)cp.size(); ++c) {
+            const int cl = cp[c].n - 2;
+            const float ns = (cp[c].score - cp[c].eos_score) / (float)(cl + 1);
+            if (ns > bn) {
+                bn = ns;
+                bi = c;
+            }
+        }
+        const Beam& best = cp[bi];
+        int n_out = 0;
+        for (int i = 2; i < best.n; ++i) {
+            if (best.tokens[i] == 2) break;
+            if (out_tokens) out_tokens[(size_t)s * G + n_out] = best.tokens[i];
+            ++n_out;
+        }
+        if (out_tokens)
+            for (int i = n_out; i < G; ++i) out_tokens[(size_t)s * G + i] = -1;
+        if (out_len) out_len[s] = n_out;
+        if (out_score) out_score[s] = bn;
+        total_out += n_out;
+    }
+    if (stats) {
+        stats->encode_ms = t_enc;
+        stats->decode_ms = t_dec;
+        stats->steps = steps_run;
+        stats->tokens_out = total_out;
+    }
+    return NLLB_ATTN_OK;
+}
+
+extern "C" int nllb_translate_margins(const nllb_model* m, int sentence, float* out, int max_steps) {
+    if (!m || sentence < 0 || sentence >= (int)m->margins.size() || !out) return 0;
+    const auto& v = m->margins[sentence];
+    const int n = std::min<int>((int)v.size(), max_steps);
+    for (int i = 0; i < n; ++i) out[i] = v[i];
+    return n;
+}

@@ -1,0 +1,432 @@
+// engine_kernels.cu -- the non-attention kernels of the GPU translation engine
+// (sm_100a): embedding + positions, LayerNorm, INT8-weight linear layers,
+// vocabulary penalties, log-softmax with top-k, and the batched store of the
+// cross-attention memory.  Each restates the arithmetic of the reference
+// routine named in its comment; fp32 throughout.
+#include <cfloat>
+#include <cstdint>
+
+#include "device_common.cuh"
+#include "engine_kernels.h"
+
+namespace nllb {
+
+namespace {
+
+// ---------------------------------------------------------------------------
+// embedding * sqrt(d_model) + sinusoidal position
+// encoder.c:262-270 / decoder.c:208-223, tensor.c:29-53, encoder.c:27-36
+// ---------------------------------------------------------------------------
+__global__ void embed_pos_kernel(float* x, const int* tokens, const int* positions, int pos_const,
+                                 const int8_t* emb, const float* emb_inv_scale, const float* pos_table,
+                                 float embed_scale, int rows, int vocab) {
+    const int r = blockIdx.x;
+    if (r >= rows) return;
+    const int tok = min(max(tokens[r], 0), vocab - 1);
+    const int pos = positions ? positions[r] : pos_const;  // table row = position + 2 offset applied on host
+    const float inv = emb_inv_scale[tok];
+    const int8_t* w = emb + (size_t)tok * 1024;
+    const float* pe = pos_table + (size_t)pos * 1024;
+    for (int i = threadIdx.x; i < 1024; i += blockDim.x) {
+        const float e = __fmul_rn(__fmul_rn((float)w[i], inv), embed_scale);
+        x[(size_t)r * 1024 + i] = __fadd_rn(e, pe[i]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// LayerNorm over 1024 (tensor.c:198-223), optionally adding a residual first:
+// x = x + res (residual_add, tensor.c:249-251), out = LN(x).  One CTA per row.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float block_sum_256(float v, float* sh) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) sh[w] = v;
+    __syncthreads();
+    float t = (l < (int)(blockDim.x >> 5)) ? sh[l] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    return t;
+}
+
+__global__ void __launch_bounds__(256) layernorm_kernel(float* out, float* x, const float* res,
+                                                         const float* gamma, const float* beta, int rows) {
+    __shared__ float sh[8];
+    const int r = blockIdx.x;
+    if (r >= rows) return;
+    float4* xr = reinterpret_cast<float4*>(x + (size_t)r * 1024);
+    float4 v = xr[threadIdx.x];
+    if (res) {
+        const float4 a = reinterpret_cast<const float4*>(res + (size_t)r * 1024)[threadIdx.x];
+        v = make_float4(v.x + a.x, v.y + a.y, v.z + a.z, v.w + a.w);
+        xr[threadIdx.x] = v;
+    }
+    const float mean = block_sum_256(v.x + v.y + v.z + v.w, sh) / 1024.0f;
+    const float4 d = make_float4(v.x - mean, v.y - mean, v.z - mean, v.w - mean);
+    const float var = block_sum_256(d.x * d.x + d.y * d.y + d.z * d.z + d.w * d.w, sh) / 1024.0f;
+    const float inv_std = 1.0f / sqrtf(var + 1e-5f);
+    const float4 g = gamma ? reinterpret_cast<const float4*>(gamma)[threadIdx.x] : make_float4(1.f, 1.f, 1.f, 1.f);
+    const float4 b = beta ? reinterpret_cast<const float4*>(beta)[threadIdx.x] : make_float4(0.f, 0.f, 0.f, 0.f);
+    reinterpret_cast<float4*>(out + (size_t)r * 1024)[threadIdx.x] =
+        make_float4(d.x * inv_std * g.x + b.x, d.y * inv_std * g.y + b.y, d.z * inv_std * g.z + b.z,
+                    d.w * inv_std * g.w + b.w);
+}
+
+// ---------------------------------------------------------------------------
+// INT8-weight linear layer: out[m][n] = (sum_k x[m][k] * w[n][k]) / scale[n]
+// + bias[n], then ReLU and/or + residual (mat_vec_int8, tensor.c:70-138 per
+// row of x; relu tensor.c:242-245; residual_add tensor.c:249-251).  Output
+// column n of row m goes to out + (n / cblock) * (M * cblock) + m * cblock +
+// n % cblock: cblock = N is plain row-major, cblock = 1024 stores a fused
+// [q|k|v] projection as three stacked [M][1024] matrices.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void linear_store(const LinearArgs& a, int m, int n, float acc) {
+    float y = acc * a.inv_scale[n];
+    if (a.bias) y += a.bias[n];
+    if (a.relu) y = fmaxf(y, 0.f);
+    if (a.mask_from >= 0 && n >= a.mask_from) y = -1e30f;
+    const size_t o = (size_t)(n / a.cblock) * ((size_t)a.M * a.cblock) + (size_t)m * a.cblock + (n % a.cblock);
+    if (a.residual) y += a.residual[o];
+    a.out[o] = y;
+}
+
+// Skinny shape (M <= MT rows): a warp owns RPW output rows; lane l reads 4
+// consecutive weights of a row at k = 128 j + 4 l (a warp reads 128 B of a
+// row per load); the rows' activations for the current 512-wide K chunk sit
+// in shared memory and are read once per 4 weights for all RPW rows.
+template <int MT, int RPW>
+__global__ void __launch_bounds__(256) linear_skinny_kernel(const LinearArgs a) {
+    constexpr int KC = 512;
+    __shared__ __align__(16) float xs[MT][KC];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = (blockIdx.x * 8 + warp) * RPW;
+    float acc[RPW][MT];
+#pragma unroll
+    for (int r = 0; r < RPW; ++r)
+#pragma unroll
+        for (int m = 0; m < MT; ++m) acc[r][m] = 0.f;
+    for (int k0 = 0; k0 < a.K; k0 += KC) {
+        const int kc = min(KC, a.K - k0);
+        __syncthreads();
+        for (int i = threadIdx.x; i < MT * (KC / 4); i += 256) {
+            const int m = i / (KC / 4), c4 = i % (KC / 4);
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (m < a.M && c4 * 4 < kc) v = *reinterpret_cast<const float4*>(a.x + (size_t)m * a.ldx + k0 + c4 * 4);
+            reinterpret_cast<float4*>(xs[m])[c4] = v;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < KC / 128; ++j) {
+            const int k = j * 128 + lane * 4;
+            if (k >= kc) break;
+            char4 w[RPW];
+#pragma unroll
+            for (int r = 0; r < RPW; ++r) {
+                const int n = n0 + r;
+                w[r] = (n < a.N) ? *reinterpret_cast<const char4*>(a.w + (size_t)n * a.K + k0 + k)
+                                 : make_char4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                if (m >= a.M) break;
+                const float4 xv = reinterpret_cast<const float4*>(xs[m])[k >> 2];
+#pragma unroll
+                for (int r = 0; r < RPW; ++r) {
+                    acc[r][m] = fmaf((float)w[r].x, xv.x, acc[r][m]);
+                    acc[r][m] = fmaf((float)w[r].y, xv.y, acc[r][m]);
+                    acc[r][m] = fmaf((float)w[r].z, xv.z, acc[r][m]);
+                    acc[r][m] = fmaf((float)w[r].w, xv.w, acc[r][m]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            float v = acc[r][m];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0 && m < a.M && n0 + r < a.N) linear_store(a, m, n0 + r, v);
+        }
+    }
+}
+
+// General shape: 64 x 64 output tile per CTA, 256 threads with 4 x 4
+// outputs each, K in steps of 32 through shared memory (x transposed to
+// k-major, weights converted to fp32).
+__global__ void __launch_bounds__(256) linear_tiled_kernel(const LinearArgs a) {
+    constexpr int BM = 64, BN = 64, BK = 32;
+    __shared__ __align__(16) float xs[BK][BM + 4];
+    __shared__ __align__(16) float ws[BK][BN + 4];
+    const int tid = threadIdx.x, tm = tid >> 4, tn = tid & 15;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+    for (int k0 = 0; k0 < a.K; k0 += BK) {
+        __syncthreads();
+        // x tile: 64 rows x 32 k = 512 float4, 2 per thread
+#pragma unroll
+        for (int it = 0; it < 2; ++it) {
+            const int i = it * 256 + tid, r = i >> 3, c4 = i & 7;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (m0 + r < a.M) v = *reinterpret_cast<const float4*>(a.x + (size_t)(m0 + r) * a.ldx + k0 + c4 * 4);
+            xs[c4 * 4 + 0][r] = v.x;
+            xs[c4 * 4 + 1][r] = v.y;
+            xs[c4 * 4 + 2][r] = v.z;
+            xs[c4 * 4 + 3][r] = v.w;
+        }
+        // weight tile: 64 rows x 32 k int8 = 128 x 16 B
+        if (tid < 128) {
+            const int r = tid >> 1, h = tid & 1;
+            int4 raw = make_int4(0, 0, 0, 0);
+            if (n0 + r < a.N) raw = *reinterpret_cast<const int4*>(a.w + (size_t)(n0 + r) * a.K + k0 + h * 16);
+            const int8_t* b = reinterpret_cast<const int8_t*>(&raw);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) ws[h * 16 + e][r] = (float)b[e];
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int k = 0; k < BK; ++k) {
+            const float4 xv = *reinterpret_cast<const float4*>(&xs[k][tm * 4]);
+            const float4 wv = *reinterpret_cast<const float4*>(&ws[k][tn * 4]);
+            const float xa[4] = {xv.x, xv.y, xv.z, xv.w}, wa[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(xa[i], wa[j], acc[i][j]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int m = m0 + tm * 4 + i, n = n0 + tn * 4 + j;
+            if (m < a.M && n < a.N) linear_store(a, m, n, acc[i][j]);
+        }
+}
+
+// ---------------------------------------------------------------------------
+// Penalties on one beam's logits (main.c:186-213): repetition penalty over
+// tokens[2..n) (skipping EOS 2), compounding for repeated tokens, then the
+// no-repeat-bigram ban.  One thread per row: the updates are sequential.
+// ---------------------------------------------------------------------------
+__global__ void penalties_kernel(float* logits, size_t ld, const int* hist, int hist_ld, const int* n_tokens,
+                                 const unsigned char* active, int rows, float penalty, int ngram) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= rows || (active && !active[r])) return;
+    float* lg = logits + (size_t)r * ld;
+    const int* tk = hist + (size_t)r * hist_ld;
+    const int n = n_tokens[r];
+    for (int g = 2; g < n; ++g) {
+        const int t = tk[g];
+        if (t == 2) continue;
+        const float v = lg[t];
+        lg[t] = (v > 0.f) ? v / penalty : v * penalty;
+    }
+    if (ngram == 2 && n >= 2) {
+        const int cur = tk[n - 1];
+        for (int i = 0; i <= n - 2; ++i)
+            if (tk[i] == cur && tk[i + 1] != 2) lg[tk[i + 1]] = -1e30f;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// log-softmax over the vocabulary and the K best entries (main.c:154-182):
+// one CTA per row; max and sum of exp by block reduction, top-K kept per
+// thread (greater value first, lower index first among equals, as
+// find_topk's strict comparison does) and merged across the CTA.
+// ---------------------------------------------------------------------------
+struct Cand {
+    float v;
+    int i;
+};
+__device__ __forceinline__ bool better(float va, int ia, float vb, int ib) {
+    return va > vb || (va == vb && ia < ib);
+}
+
+template <int K>
+__device__ __forceinline__ void topk_insert(float (&tv)[K], int (&ti)[K], float v, int i) {
+    if (!better(v, i, tv[K - 1], ti[K - 1])) return;
+    int j = K - 1;
+#pragma unroll
+    for (int q = K - 1; q > 0; --q) {
+        if (j == q && better(v, i, tv[q - 1], ti[q - 1])) {
+            tv[q] = tv[q - 1];
+            ti[q] = ti[q - 1];
+            j = q - 1;
+        }
+    }
+    tv[j] = v;
+    ti[j] = i;
+}
+
+template <int K>
+__global__ void __launch_bounds__(256) logsoftmax_topk_kernel(const float* logits, size_t ld, int V, int rows,
+                                                               const unsigned char* active, int* out_tok,
+                                                               float* out_logp) {
+    __shared__ float sh_f[8];
+    __shared__ float cv[256 * K];
+    __shared__ int ci[256 * K];
+    const int r = blockIdx.x;
+    if (r >= rows) return;
+    if (active && !active[r]) return;  // uniform per CTA
+    const float* lg = logits + (size_t)r * ld;
+    float tv[K];
+    int ti[K];
+#pragma unroll
+    for (int q = 0; q < K; ++q) {
+        tv[q] = -FLT_MAX;
+        ti[q] = 0x7fffffff;
+    }
+    float mx = -FLT_MAX;
+    for (int i = threadIdx.x; i < V; i += 256) {
+        const float v = lg[i];
+        mx = fmaxf(mx, v);
+        topk_insert<K>(tv, ti, v, i);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) sh_f[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    mx = sh_f[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) mx = fmaxf(mx, sh_f[w]);
+    float se = 0.f;
+    for (int i = threadIdx.x; i < V; i += 256) se += expf(lg[i] - mx);
+    se = block_sum_256(se, sh_f);
+    const float ln = mx + logf(se);
+#pragma unroll
+    for (int q = 0; q < K; ++q) {
+        cv[threadIdx.x * K + q] = tv[q];
+        ci[threadIdx.x * K + q] = ti[q];
+    }
+    __syncthreads();
+    // tree merge of sorted lists: 256 -> 1
+    for (int width = 1; width < 256; width <<= 1) {
+        if ((threadIdx.x & (2 * width - 1)) == 0) {
+            const int a0 = threadIdx.x * K, b0 = (threadIdx.x + width) * K;
+            float mv[K];
+            int mi[K];
+            int ia = 0, ib = 0;
+#pragma unroll
+            for (int q = 0; q < K; ++q) {
+                const bool take_a =
+                    ib >= K || (ia < K && better(cv[a0 + ia], ci[a0 + ia], cv[b0 + ib], ci[b0 + ib]));
+                mv[q] = take_a ? cv[a0 + ia] : cv[b0 + ib];
+                mi[q] = take_a ? ci[a0 + ia] : ci[b0 + ib];
+                ia += take_a;
+                ib += !take_a;
+            }
+#pragma unroll
+            for (int q = 0; q < K; ++q) {
+                cv[a0 + q] = mv[q];
+                ci[a0 + q] = mi[q];
+            }
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x < K) {
+        out_tok[(size_t)r * K + threadIdx.x] = ci[threadIdx.x];
+        out_logp[(size_t)r * K + threadIdx.x] = cv[threadIdx.x] - ln;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// cross-attention memory of many sentences for one layer: rows of sentence s
+// at kv + s * row_stride_sent (K) and + v_off (V), [n][1024] head-interleaved,
+// into the context's head-major [sentence][head][max_src][64]
+// ---------------------------------------------------------------------------
+__global__ void set_memory_batched_kernel(float* km, float* vm, int* n_src_slots, int max_src, int H,
+                                          const float* k, const float* v, long long sent_stride,
+                                          const int* n_src, int n_sent) {
+    const int s = blockIdx.y;
+    const int n = n_src[s];
+    if (blockIdx.x == 0 && threadIdx.x == 0) n_src_slots[s] = n;
+    const size_t total = (size_t)H * n * 16;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int q4 = (int)(i & 15);
+        const size_t hr = i >> 4;
+        const int r = (int)(hr % n), h = (int)(hr / n);
+        const size_t src = (size_t)s * sent_stride + (size_t)r * (H * 64) + (size_t)h * 64;
+        const size_t dst = (((size_t)s * H + h) * max_src + r) * 64;
+        reinterpret_cast<float4*>(km + dst)[q4] = reinterpret_cast<const float4*>(k + src)[q4];
+        reinterpret_cast<float4*>(vm + dst)[q4] = reinterpret_cast<const float4*>(v + src)[q4];
+    }
+}
+
+__global__ void reciprocal_kernel(float* out, const float* in, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = 1.0f / in[i];
+}
+
+}  // namespace
+
+cudaError_t launch_embed_pos(float* x, const int* tokens, const int* positions, int pos_const, const int8_t* emb,
+                             const float* emb_inv_scale, const float* pos_table, float embed_scale, int rows,
+                             int vocab, cudaStream_t st) {
+    if (rows <= 0) return cudaSuccess;
+    embed_pos_kernel<<<rows, 256, 0, st>>>(x, tokens, positions, pos_const, emb, emb_inv_scale, pos_table,
+                                           embed_scale, rows, vocab);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_layernorm(float* out, float* x, const float* res, const float* gamma, const float* beta,
+                             int rows, cudaStream_t st) {
+    if (rows <= 0) return cudaSuccess;
+    layernorm_kernel<<<rows, 256, 0, st>>>(out, x, res, gamma, beta, rows);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_linear(const LinearArgs& a, cudaStream_t st) {
+    if (a.M <= 0) return cudaSuccess;
+    if ((a.K & 3) || (a.ldx & 3)) return cudaErrorInvalidValue;
+    if (a.M <= 4) {
+        linear_skinny_kernel<4, 2><<<(a.N + 15) / 16, 256, 0, st>>>(a);
+    } else if (a.M <= 16) {
+        linear_skinny_kernel<16, 2><<<(a.N + 15) / 16, 256, 0, st>>>(a);
+    } else {
+        if (a.K % 32) return cudaErrorInvalidValue;
+        dim3 grid((a.N + 63) / 64, (a.M + 63) / 64);
+        linear_tiled_kernel<<<grid, 256, 0, st>>>(a);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_penalties(float* logits, size_t ld, const int* hist, int hist_ld, const int* n_tokens,
+                             const unsigned char* active, int rows, float penalty, int ngram, cudaStream_t st) {
+    if (rows <= 0) return cudaSuccess;
+    penalties_kernel<<<(rows + 127) / 128, 128, 0, st>>>(logits, ld, hist, hist_ld, n_tokens, active, rows,
+                                                          penalty, ngram);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_logsoftmax_topk(const float* logits, size_t ld, int V, int rows, const unsigned char* active,
+                                   int k, int* out_tok, float* out_logp, cudaStream_t st) {
+    if (rows <= 0) return cudaSuccess;
+    if (k == 8) logsoftmax_topk_kernel<8><<<rows, 256, 0, st>>>(logits, ld, V, rows, active, out_tok, out_logp);
+    else if (k == 4) logsoftmax_topk_kernel<4><<<rows, 256, 0, st>>>(logits, ld, V, rows, active, out_tok, out_logp);
+    else return cudaErrorInvalidValue;
+    return cudaGetLastError();
+}
+
+cudaError_t launch_set_memory_batched(float* km, float* vm, int* n_src_slots, int max_src, int H, const float* k,
+                                      const float* v, long long sent_stride, const int* n_src, int n_sent,
+                                      int max_n, cudaStream_t st) {
+    if (n_sent <= 0) return cudaSuccess;
+    const int bx = (int)(((size_t)H * max_n * 16 + 255) / 256);
+    set_memory_batched_kernel<<<dim3(bx < 64 ? bx : 64, n_sent), 256, 0, st>>>(km, vm, n_src_slots, max_src, H, k,
+                                                                                v, sent_stride, n_src, n_sent);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_reciprocal(float* out, const float* in, size_t n, cudaStream_t st) {
+    reciprocal_kernel<<<256, 256, 0, st>>>(out, in, n);
+    return cudaGetLastError();
+}
+
+}  // namespace nllb

@@ -1,0 +1,39 @@
+// engine_kernels.h -- launchers of the translation engine's non-attention kernels.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace nllb {
+
+// out = epilogue(x[M][K] . (w[N][K] / scale[N])^T + bias), see engine_kernels.cu
+struct LinearArgs {
+    const float* x;
+    int ldx;                 // row stride of x (elements)
+    const int8_t* w;         // [N][K] int8
+    const float* inv_scale;  // [N] 1 / weight_scale
+    const float* bias;       // [N] or null
+    float* out;
+    const float* residual;   // same addressing as out, or null
+    int M, N, K;
+    int cblock;              // output column block (N for row-major)
+    int relu;
+    int mask_from;           // columns >= mask_from are set to -1e30 (-1: none)
+};
+
+cudaError_t launch_embed_pos(float* x, const int* tokens, const int* positions, int pos_const, const int8_t* emb,
+                             const float* emb_inv_scale, const float* pos_table, float embed_scale, int rows,
+                             int vocab, cudaStream_t st);
+cudaError_t launch_layernorm(float* out, float* x, const float* res, const float* gamma, const float* beta,
+                             int rows, cudaStream_t st);
+cudaError_t launch_linear(const LinearArgs& a, cudaStream_t st);
+cudaError_t launch_penalties(float* logits, size_t ld, const int* hist, int hist_ld, const int* n_tokens,
+                             const unsigned char* active, int rows, float penalty, int ngram, cudaStream_t st);
+cudaError_t launch_logsoftmax_topk(const float* logits, size_t ld, int V, int rows, const unsigned char* active,
+                                   int k, int* out_tok, float* out_logp, cudaStream_t st);
+cudaError_t launch_set_memory_batched(float* km, float* vm, int* n_src_slots, int max_src, int H, const float* k,
+                                      const float* v, long long sent_stride, const int* n_src, int n_sent,
+                                      int max_n, cudaStream_t st);
+cudaError_t launch_reciprocal(float* out, const float* in, size_t n, cudaStream_t st);
+
+}  // namespace nllb

@@ -10,6 +10,7 @@
 #include <string>
 #include <vector>
 
+#include "attn_internal.h"
 #include "device_common.cuh"
 #include "kernels.h"
 
@@ -40,25 +41,12 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 }  // namespace
 
-struct nllb_attn_ctx {
-    int device = 0;
-    int num_sms = 148;
-    nllb_attn_dims d{};
-    int Tp = 0;  // beam-history rows per sentence (max_tgt rounded up, +2 for 16-B copies)
-    cudaStream_t own_stream = nullptr;
-    cudaStream_t stream = nullptr;
-    float* kc = nullptr;  // [L][S][H][T][NB][64]
-    float* vc = nullptr;
-    unsigned char* hist = nullptr;  // [S][Tp][8]
-    float* km = nullptr;  // [L][S][H][max_src][64]
-    float* vm = nullptr;
-    int* n_src_dev = nullptr;  // [L][S]
-    std::vector<int> n_src_host;
-    int* err = nullptr;
-    // staging for *_host calls, grown on demand
-    void* stg[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
-    size_t stg_bytes[6] = {0, 0, 0, 0, 0, 0};
-};
+namespace nllb {
+// Status + message for the engine translation unit (engine.cu).
+int set_error(int status, const std::string& msg) { return fail(status, msg); }
+}  // namespace nllb
+
+
 
 namespace {
 

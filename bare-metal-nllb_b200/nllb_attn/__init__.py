@@ -40,6 +40,16 @@ class PrefillArgs(ctypes.Structure):
     ]
 
 
+class TranslateOpts(ctypes.Structure):
+    _fields_ = [("max_gen", ctypes.c_int), ("repetition_penalty", ctypes.c_float),
+                ("no_repeat_ngram", ctypes.c_int)]
+
+
+class TranslateStats(ctypes.Structure):
+    _fields_ = [("encode_ms", ctypes.c_double), ("decode_ms", ctypes.c_double),
+                ("steps", ctypes.c_int), ("tokens_out", ctypes.c_longlong)]
+
+
 SIGNATURES = {
     "nllb_attn_create": (_c_int, [_c_int, ctypes.POINTER(Dims), ctypes.POINTER(_c_void_p)]),
     "nllb_attn_destroy": (None, [_c_void_p]),
@@ -65,6 +75,13 @@ SIGNATURES = {
     "nllb_attention_head": (None, [_fp, _fp, _fp, _fp, _fp, _fp, _c_int, _c_int]),
     "nllb_attention_head_flash": (None, [_fp, _fp, _fp, _fp, _fp, _c_int, _c_int]),
     "nllb_attn_last_status": (_c_int, []),
+    # include/nllb_translate.h
+    "nllb_model_load": (_c_int, [ctypes.c_char_p, _c_int, _c_int, _c_int, _c_int,
+                                 ctypes.POINTER(_c_void_p)]),
+    "nllb_model_free": (None, [_c_void_p]),
+    "nllb_translate": (_c_int, [_c_void_p, _c_int, _fp, _fp, _c_int, ctypes.POINTER(TranslateOpts),
+                                _fp, _fp, _fp, ctypes.POINTER(TranslateStats)]),
+    "nllb_translate_margins": (_c_int, [_c_void_p, _c_int, _fp, _c_int]),
 }
 
 _LIB: Optional[ctypes.CDLL] = None
@@ -224,6 +241,55 @@ def attention_head(Q, K, V, mask, out, scores_buf, seq_len: int, head_dim: int =
     lib.nllb_attention_head(ptr(Q), ptr(K), ptr(V), ptr(mask), ptr(out), ptr(scores_buf),
                             seq_len, head_dim)
     return lib.nllb_attn_last_status()
+
+
+class Model:
+    """A synthetic-or-real NLLB INT8 model on one GPU (include/nllb_translate.h)."""
+
+    def __init__(self, path: str, device: int = 0, max_sentences: int = 1, max_src: int = 256,
+                 max_gen: int = 36, lib: Optional[ctypes.CDLL] = None):
+        self.lib = lib or load()
+        h = ctypes.c_void_p()
+        _check(self.lib, self.lib.nllb_model_load(path.encode(), device, max_sentences, max_src,
+                                                  max_gen, ctypes.byref(h)), "nllb_model_load")
+        self.handle, self.max_gen = h, max_gen
+
+    def close(self) -> None:
+        if self.handle:
+            self.lib.nllb_model_free(self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def translate(self, sources, tgt_lang: int, max_gen: Optional[int] = None,
+                  repetition_penalty: float = 1.2, no_repeat_ngram: int = 2):
+        """sources: list of token-id lists ([src_lang] ... [2]).  Returns
+        (list of output token lists, normalised scores, TranslateStats)."""
+        import numpy as np
+        flat = np.ascontiguousarray(np.concatenate([np.asarray(x, np.int32) for x in sources]))
+        offs = np.zeros(len(sources) + 1, np.int32)
+        offs[1:] = np.cumsum([len(x) for x in sources])
+        G = max_gen or self.max_gen
+        out = np.full((len(sources), self.max_gen), -1, np.int32)
+        lens = np.zeros(len(sources), np.int32)
+        scores = np.zeros(len(sources), np.float32)
+        opts = TranslateOpts(G, repetition_penalty, no_repeat_ngram)
+        st = TranslateStats()
+        _check(self.lib, self.lib.nllb_translate(self.handle, len(sources), ptr(flat), ptr(offs), tgt_lang,
+                                                 ctypes.byref(opts), ptr(out), ptr(lens), ptr(scores),
+                                                 ctypes.byref(st)), "nllb_translate")
+        toks = [out[i, :lens[i]].tolist() for i in range(len(sources))]
+        return toks, scores, st
+
+    def margins(self, sentence: int, max_steps: int = 1024):
+        import numpy as np
+        buf = np.zeros(max_steps, np.float32)
+        n = self.lib.nllb_translate_margins(self.handle, sentence, ptr(buf), max_steps)
+        return buf[:n]
 
 
 def exported_symbols(header_path: str) -> Sequence[str]:

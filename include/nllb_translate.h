@@ -1,0 +1,73 @@
+/*  nllb_translate.h -- sentence-batched NLLB translation on one B200.
+ *
+ *  The engine around the attention path: it runs the reference engine's
+ *  whole forward pass and beam search on the GPU for many sentences at once.
+ *
+ *    weights      loader.c:287-372 (CTranslate2-named INT8 safetensors file)
+ *    encoder      pico_encode, encoder.c:250-287
+ *    decoder      pico_decode_forward / decoder_layer_step, decoder.c:156-233
+ *    vocabulary   pico_vocab_project, decoder.c:319-354 (language rows masked)
+ *    beam search  main.c:294-528: steps 0 and 1 seed the beams, then per step
+ *                 repetition penalty 1.2, no-repeat bigram, log-softmax, top-8
+ *                 per beam, candidate sort, EOS bookkeeping, final choice by
+ *                 length-normalised score; max_out = min(3*n_src+10, max_gen-4)
+ *
+ *  The attention runs through libnllb_attn's kernels; the rest (INT8 linear
+ *  layers, LayerNorm, embeddings, vocabulary projection, penalties, top-k) are
+ *  this library's kernels too.  The candidate selection of each step runs on
+ *  the host from the per-beam top-8 (a few KB per step).
+ *
+ *  Returns NLLB_ATTN_* status codes (nllb_attn.h).
+ */
+#ifndef NLLB_TRANSLATE_H
+#define NLLB_TRANSLATE_H
+
+#include "nllb_attn.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct nllb_model nllb_model;
+
+typedef struct {
+    int max_gen;                /* MAX_GEN_LEN (pico.h:19): caps the target at max_gen - 4 tokens */
+    float repetition_penalty;   /* REPETITION_PENALTY (pico.h:100), 1.2 */
+    int no_repeat_ngram;        /* NO_REPEAT_NGRAM_SIZE (pico.h:101): 2, or 0 to disable */
+} nllb_translate_opts;
+
+typedef struct {
+    double encode_ms;           /* encoder + cross-attention memory, all sentences */
+    double decode_ms;           /* decoder steps and beam search */
+    int steps;                  /* decoder steps run (including the two seeding steps) */
+    long long tokens_out;       /* emitted target tokens, EOS excluded (main.c:534-546) */
+} nllb_translate_stats;
+
+/* Upload the model in `path` to `device`.  max_sentences / max_src bound the
+ * batch a later nllb_translate may pass. */
+NLLB_ATTN_API int nllb_model_load(const char* path, int device, int max_sentences, int max_src,
+                                  int max_gen, nllb_model** out);
+NLLB_ATTN_API void nllb_model_free(nllb_model* m);
+
+/* Translate n_sentences sources.  Sentence i is src_tokens[src_offsets[i] ..
+ * src_offsets[i+1]) and must already be [src_lang] ... [2] as main.c:274-290
+ * builds it.  out_tokens: [n_sentences][max_gen] (the best hypothesis's
+ * tokens, EOS excluded, then -1), out_len: [n_sentences], out_score:
+ * [n_sentences] length-normalised score (main.c:519-528).  Any output pointer
+ * may be NULL.  Host pointers. */
+NLLB_ATTN_API int nllb_translate(nllb_model* m, int n_sentences, const int* src_tokens,
+                                 const int* src_offsets, int tgt_lang, const nllb_translate_opts* opts,
+                                 int* out_tokens, int* out_len, float* out_score,
+                                 nllb_translate_stats* stats);
+
+/* Decision margins of the last nllb_translate call for sentence `sentence`:
+ * out[t] = smallest gap between consecutive candidate scores among the best
+ * n_beams+1 after the sort of step t+2 (main.c:455-460), i.e. how close the
+ * beam choice of that step came to a tie.  Returns the number of steps
+ * written (at most max_steps). */
+NLLB_ATTN_API int nllb_translate_margins(const nllb_model* m, int sentence, float* out, int max_steps);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NLLB_TRANSLATE_H */

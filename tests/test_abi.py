@@ -9,10 +9,11 @@ import nllb_attn as na
 
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 HEADER = os.path.join(REPO, "include", "nllb_attn.h")
+HEADERS = [HEADER, os.path.join(REPO, "include", "nllb_translate.h")]
 
 
 def test_library_exports_every_declared_symbol():
-    declared = na.exported_symbols(HEADER)
+    declared = sorted(set().union(*(na.exported_symbols(h) for h in HEADERS)))
     assert len(declared) >= 20
     lib = ctypes.CDLL(na.LIB_PATH)
     missing = [n for n in declared if not hasattr(lib, n)]
@@ -26,12 +27,15 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_binding_declares_every_header_function():
-    assert set(na.exported_symbols(HEADER)) == set(na.SIGNATURES)
+    declared = set().union(*(na.exported_symbols(h) for h in HEADERS))
+    assert declared == set(na.SIGNATURES)
 
 
 def test_header_compiles_as_c11(tmp_path):
     src = tmp_path / "t.c"
-    src.write_text('#include "nllb_attn.h"\nint main(void){nllb_attn_dims d={12,16,64,1,4,256,512};'
+    src.write_text('#include "nllb_attn.h"\n#include "nllb_translate.h"\n'
+                   'int main(void){nllb_attn_dims d={12,16,64,1,4,256,512};'
+                   'nllb_translate_opts o={36,1.2f,2};(void)o;'
                    'return nllb_attn_device_bytes(&d) == 0;}\n')
     subprocess.run(["gcc", "-std=c11", "-Wall", "-Werror", "-I", os.path.join(REPO, "include"),
                     "-c", str(src), "-o", str(tmp_path / "t.o")], check=True)
