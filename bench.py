@@ -125,6 +125,8 @@ def parse_args():
     ap.add_argument("--max-len", type=int, default=256, help="decode steps per sweep")
     ap.add_argument("--no-ops", action="store_true", help="skip the per-config op measurements")
     ap.add_argument("--cpu-sample-s", type=float, default=10.0)
+    ap.add_argument("--translate-sentences", type=int, default=1024,
+                    help="sentences of the sentence-batched translation (0: skip translation)")
     ap.add_argument("--ncu-case", choices=("decode", "decode1", "cross", "prefill"),
                     help="run one small fixed case for an ncu capture and exit")
     return ap.parse_args()
@@ -426,6 +428,100 @@ def measure_ops(ctx_factory, dev, hbm_peak, tflops_note=""):
     return res
 
 
+SYNTH_MODEL = os.environ.get("NLLB_SYNTH_MODEL", "/tmp/nllb_synth/synth_nllb600m_seed0.safetensors")
+
+
+def config4_sources(n: int = 1024, seed: int = 4):
+    """Sentence-batched translation workload: n sources of U[16,128] tokens
+    (ids U[4,256000)), each [eng_Latn] ... [2]."""
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import pyoracle as po
+    from nllb_attn import synth_model as sm
+    lengths = po.det_ints(seed, n, 16, 129)
+    return [sm.source_ids(seed * 1000003 + i, int(lengths[i])) for i in range(n)]
+
+
+def reference_translate_rate(model_path: str):
+    """The reference engine (its own main.c, compiled from its sources) on the
+    single-sentence configuration: tokens/s as it reports them (decode time)."""
+    import re
+    from nllb_attn import synth_model as sm
+    exe = os.path.join(REPO, "oracle", "_ref", "pico_nllb_g36")
+    if not os.path.exists(exe):
+        return None
+    src = sm.source_ids(0, 16)
+    out = subprocess.run([exe, model_path, "eng_Latn", "fra_Latn"] + [str(t) for t in src[1:-1]],
+                         capture_output=True, text=True, timeout=600).stdout
+    m = re.search(r"^best: (\d+) tokens, score=[-0-9.]+, enc=(\d+)ms, dec=(\d+)ms, ([0-9.]+) tok/s", out, re.M)
+    if not m:
+        return None
+    n, enc, dec = int(m.group(1)), int(m.group(2)), int(m.group(3))
+    return {"tok_s_decode": float(m.group(4)), "tok_s_total": round(n / ((enc + dec) / 1e3), 3),
+            "tokens": n, "cores": 4, "kind": "reference",
+            "sample": "one 16-token sentence, beam 4, 32 target tokens, NUM_THREADS=4 (the reference's default)"}
+
+
+def measure_translation(args, rank, world, local_rank):
+    """Translated tokens/s through nllb_translate (host sources in, host
+    tokens out), config 0 (one sentence) at N=1 and config 4 (sentences
+    sharded over the ranks, no collective until the final counts)."""
+    import torch
+    import torch.distributed as dist
+    import nllb_attn as na
+    from nllb_attn import sharding, synth_model as sm
+
+    if local_rank == 0:
+        sm.ensure_model(SYNTH_MODEL, seed=0)
+    if world > 1:
+        dist.barrier()
+    sources = config4_sources(args.translate_sentences)
+    shards = sharding.plan_shards([len(x) for x in sources], world, max_gen=132)
+    mine = [sources[i] for i in shards[rank]]
+    res = {}
+    max_sent = max(1, len(mine))
+    with na.Model(SYNTH_MODEL, device=local_rank, max_sentences=max_sent, max_src=132, max_gen=132) as m:
+        tgt = sm.LANG["fra_Latn"]
+        if world == 1:
+            src0 = sm.source_ids(0, 16)
+            m.translate([src0], tgt, max_gen=36)  # warm-up
+            best = None
+            for _ in range(3):
+                toks, _, st = m.translate([src0], tgt, max_gen=36)
+                if best is None or st.decode_ms < best.decode_ms:
+                    best = st
+            res["config0"] = {
+                "workload": "one 16-token sentence, beam 4, 32 target tokens (main.c rules)",
+                "tokens": int(best.tokens_out),
+                "tok_s_decode": round(best.tokens_out / (best.decode_ms / 1e3), 1),
+                "tok_s_total": round(best.tokens_out / ((best.encode_ms + best.decode_ms) / 1e3), 1),
+                "ms_encode": round(best.encode_ms, 2), "ms_decode": round(best.decode_ms, 2)}
+        if mine:
+            m.translate(mine[:min(4, len(mine))], tgt, max_gen=132)  # warm-up
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        tokens = 0
+        if mine:
+            _, _, st = m.translate(mine, tgt, max_gen=132)
+            tokens = int(st.tokens_out)
+        dt = time.perf_counter() - t0
+    dev = torch.device("cuda", local_rank)
+    t = torch.tensor([dt], dtype=torch.float64, device=dev)
+    n = torch.tensor([tokens], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(n, op=dist.ReduceOp.SUM)
+    res["config4"] = {
+        "workload": f"{len(sources)} sentences, sources U[16,128] tokens (seed 4), beam 4, max 128 target tokens, "
+                    f"sharded by sentence over {world} GPU(s) (LPT plan, no collective on the data path)",
+        "sentences": len(sources), "tokens": int(n.item()), "seconds": round(float(t.item()), 3),
+        "tok_s": round(float(n.item()) / float(t.item()), 1), "n_gpus": world, "scaling": "strong",
+        "how": "wall clock around nllb_translate (host sources in, host token ids out), max over ranks"}
+    if rank == 0 and world == 1:
+        res["reference_cpu"] = reference_translate_rate(SYNTH_MODEL)
+    return res
+
+
 def ncu_case(which: str) -> None:
     """Small, fixed cases for ncu captures (a few launches of one kernel each)."""
     import torch
@@ -524,6 +620,9 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     res, ops = run_ours(args, rank, world, local_rank)
+    translation = None
+    if args.translate_sentences > 0:
+        translation = measure_translation(args, rank, world, local_rank)
     cpu = None
     if rank == 0 and world == 1:
         try:
@@ -559,6 +658,8 @@ def main():
         }
         if ops:
             line["ops"] = ops
+        if translation:
+            line["translation"] = translation
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
