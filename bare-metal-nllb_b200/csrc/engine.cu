@@ -185,7 +185,7 @@ class HeaderParser {
 
 struct Lin {
     int8_t* w = nullptr;
-    float* inv = nullptr;
+    float* scale = nullptr;  // CT2 weight_scale (weight = int8 / scale)
     float* b = nullptr;
     int out = 0, in = 0;
 };
@@ -198,7 +198,8 @@ struct nllb_model {
     cudaStream_t stream = nullptr;
     std::vector<void*> allocs;
     int8_t* emb = nullptr;
-    float* emb_inv = nullptr;
+    float* emb_scale = nullptr;  // per-row weight_scale of the shared embedding
+    float* emb_inv = nullptr;    // 1 / emb_scale, for the embedding lookup (tensor.c:37-40)
     struct Enc {
         Lin qkv, out, fc1, fc2;
         float *ln1g, *ln1b, *ln2g, *ln2b;
@@ -211,6 +212,8 @@ struct nllb_model {
     float* pos_table = nullptr;  // row p: sinusoid of actual position p (encoder.c:27-36)
     int pos_rows = 0;
     nllb_attn_ctx* attn = nullptr;
+    LinearWorkspace lws;  // split-K workspace of the tensor-core linear kernel
+    int num_sms = 148;
     // decision margins of the last translate call, [sentence][step]
     std::vector<std::vector<float>> margins;
 };
@@ -249,15 +252,12 @@ struct Loader {
         ENG_CK(cudaMemcpy(*dst, data + ti->begin, (size_t)elems * sizeof(T), cudaMemcpyHostToDevice));
         return NLLB_ATTN_OK;
     }
-    // weight, 1/weight_scale (tensor.c:75) and bias of an INT8 linear layer
+    // weight, weight_scale (dequantised as int8 * (1/scale), tensor.c:75) and bias
     int linear(const std::string& prefix, int out_f, int in_f, Lin* L) {
         L->out = out_f;
         L->in = in_f;
         ENG_RC(upload(prefix + "/weight", "I8", (long long)out_f * in_f, &L->w));
-        float* scale = nullptr;
-        ENG_RC(upload(prefix + "/weight_scale", "F32", out_f, &scale));
-        ENG_RC(dev_alloc(m, &L->inv, out_f));
-        ENG_CK(launch_reciprocal(L->inv, scale, out_f, m->stream));
+        ENG_RC(upload(prefix + "/weight_scale", "F32", out_f, &L->scale));
         if (tensors.count(prefix + "/bias")) ENG_RC(upload(prefix + "/bias", "F32", out_f, &L->b));
         return NLLB_ATTN_OK;
     }
@@ -330,6 +330,15 @@ int nllb_model_load(const char* path, int device, int max_sentences, int max_src
     };
     if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess)
         return fail(nllb::set_error(NLLB_ATTN_ECUDA, "cudaStreamCreate failed"));
+    if (configure_linear_tc() != cudaSuccess)
+        return fail(nllb::set_error(NLLB_ATTN_ECUDA, "cannot configure the tensor-core linear kernel"));
+    m->num_sms = attn->num_sms;
+    // split-K: at most 2*SMs*8 partial 128x128 tiles, one counter per tile of the largest output
+    m->lws.ws_floats = (size_t)2 * m->num_sms * 8 * 128 * 128;
+    m->lws.n_counters = (size_t)((VOCAB + 127) / 128) * ((std::max(max_sentences * NB, max_sentences * max_src) + 127) / 128);
+    if (dev_alloc(m, &m->lws.ws, m->lws.ws_floats) || dev_alloc(m, &m->lws.tile_count, m->lws.n_counters) ||
+        cudaMemset(m->lws.tile_count, 0, m->lws.n_counters * sizeof(int)) != cudaSuccess)
+        return fail(nllb::set_error(NLLB_ATTN_ECUDA, "cannot allocate the linear-layer workspace"));
     nllb_attn_set_stream(attn, m->stream);
 
     const int fd = open(path, O_RDONLY);
@@ -354,10 +363,9 @@ int nllb_model_load(const char* path, int device, int max_sentences, int max_src
     auto load_all = [&]() -> int {
         // shared embedding (loader.c:327-335): one device copy serves both stacks
         ENG_RC(L.upload("decoder/embeddings/weight", "I8", (long long)VOCAB * D, &m->emb));
-        float* es = nullptr;
-        ENG_RC(L.upload("decoder/embeddings/weight_scale", "F32", VOCAB, &es));
+        ENG_RC(L.upload("decoder/embeddings/weight_scale", "F32", VOCAB, &m->emb_scale));
         ENG_RC(dev_alloc(m, &m->emb_inv, VOCAB));
-        ENG_CK(launch_reciprocal(m->emb_inv, es, VOCAB, m->stream));
+        ENG_CK(launch_reciprocal(m->emb_inv, m->emb_scale, VOCAB, m->stream));
         for (int i = 0; i < LAYERS; ++i) {
             const std::string p = "encoder/layer_" + std::to_string(i);
             auto& E = m->enc[i];
@@ -408,7 +416,7 @@ int run_linear(nllb_model* m, const Lin& L, const float* x, int M, float* out, c
     a.x = x;
     a.ldx = L.in;
     a.w = L.w;
-    a.inv_scale = L.inv;
+    a.scale = L.scale;
     a.bias = L.b;
     a.out = out;
     a.residual = residual;
@@ -418,7 +426,7 @@ int run_linear(nllb_model* m, const Lin& L, const float* x, int M, float* out, c
     a.cblock = cblock;
     a.relu = relu;
     a.mask_from = mask_from;
-    ENG_CK(launch_linear(a, m->stream));
+    ENG_CK(launch_linear(a, &m->lws, m->num_sms, m->attn->err, m->stream));
     return NLLB_ATTN_OK;
 }
 
@@ -517,7 +525,7 @@ int decode_step(nllb_model* m, Work& w, int step) {
 int vocab_topk(nllb_model* m, Work& w, int k, bool penalties, const nllb_translate_opts& o) {
     Lin E;
     E.w = m->emb;
-    E.inv = m->emb_inv;
+    E.scale = m->emb_scale;
     E.b = nullptr;
     E.out = VOCAB;
     E.in = D;
@@ -787,4 +795,63 @@ extern "C" int nllb_translate_margins(const nllb_model* m, int sentence, float* 
     const int n = std::min<int>((int)v.size(), max_steps);
     for (int i = 0; i < n; ++i) out[i] = v[i];
     return n;
+}
+
+extern "C" int nllb_linear_int8(const float* x, int M, int K, const int8_t* w, const float* weight_scale,
+                                const float* bias, int N, float* out, const float* residual, int flags,
+                                void* stream) {
+    if (!x || !w || !weight_scale || !out) return nllb::set_error(NLLB_ATTN_EINVAL, "x, w, weight_scale, out required");
+    if (M < 0 || K < 4 || N < 1 || (K & 3)) return nllb::set_error(NLLB_ATTN_EINVAL, "M >= 0, N >= 1, K a multiple of 4");
+    if (M > 0 && M > 16 && K % 32) return nllb::set_error(NLLB_ATTN_EINVAL, "K must be a multiple of 32 beyond 16 rows");
+    LinearArgs a;
+    a.x = x;
+    a.ldx = K;
+    a.w = w;
+    a.scale = weight_scale;
+    a.bias = bias;
+    a.out = out;
+    a.residual = residual;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.cblock = N;
+    a.relu = (flags & NLLB_LINEAR_RELU) ? 1 : 0;
+    a.mask_from = -1;
+    // bounded-wait error word of the current device for callers without a context
+    static int* err_words[64] = {nullptr};
+    int dev = 0;
+    ENG_CK(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return nllb::set_error(NLLB_ATTN_ENODEV, "device ordinal beyond 63");
+    if (!err_words[dev]) {
+        ENG_CK(cudaMalloc(&err_words[dev], sizeof(int)));
+        ENG_CK(cudaMemset(err_words[dev], 0, sizeof(int)));
+    }
+    int* err_word = err_words[dev];
+    // split-K workspace of the current device, grown on demand
+    static LinearWorkspace wss[64];
+    LinearWorkspace& W = wss[dev];
+    int nsm = 148;
+    ENG_CK(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+    if (M > 16 && linear_tc_supports(a)) {
+        const int splits = linear_tc_splits(a, nsm);
+        const size_t need = linear_tc_workspace_floats(a, splits), tiles = linear_tc_tiles(a);
+        if (need > W.ws_floats) {
+            if (W.ws) cudaFree(W.ws);
+            W.ws = nullptr;
+            W.ws_floats = 0;
+            ENG_CK(cudaMalloc(&W.ws, need * sizeof(float)));
+            W.ws_floats = need;
+        }
+        if (tiles > W.n_counters) {
+            if (W.tile_count) cudaFree(W.tile_count);
+            W.tile_count = nullptr;
+            W.n_counters = 0;
+            ENG_CK(cudaMalloc(&W.tile_count, tiles * sizeof(int)));
+            ENG_CK(cudaMemset(W.tile_count, 0, tiles * sizeof(int)));
+            W.n_counters = tiles;
+        }
+    }
+    if (configure_linear_tc() != cudaSuccess) return nllb::set_error(NLLB_ATTN_ECUDA, "configure failed");
+    ENG_CK(launch_linear(a, &W, nsm, err_word, static_cast<cudaStream_t>(stream)));
+    return NLLB_ATTN_OK;
 }

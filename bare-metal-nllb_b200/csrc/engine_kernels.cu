@@ -82,7 +82,7 @@ __global__ void __launch_bounds__(256) layernorm_kernel(float* out, float* x, co
 // [q|k|v] projection as three stacked [M][1024] matrices.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void linear_store(const LinearArgs& a, int m, int n, float acc) {
-    float y = acc * a.inv_scale[n];
+    float y = acc * (1.0f / a.scale[n]);
     if (a.bias) y += a.bias[n];
     if (a.relu) y = fmaxf(y, 0.f);
     if (a.mask_from >= 0 && n >= a.mask_from) y = -1e30f;
@@ -382,13 +382,18 @@ cudaError_t launch_layernorm(float* out, float* x, const float* res, const float
     return cudaGetLastError();
 }
 
-cudaError_t launch_linear(const LinearArgs& a, cudaStream_t st) {
+cudaError_t launch_linear(const LinearArgs& a, const LinearWorkspace* wsp, int num_sms, int* err, cudaStream_t st) {
     if (a.M <= 0) return cudaSuccess;
     if ((a.K & 3) || (a.ldx & 3)) return cudaErrorInvalidValue;
     if (a.M <= 4) {
         linear_skinny_kernel<4, 2><<<(a.N + 15) / 16, 256, 0, st>>>(a);
     } else if (a.M <= 16) {
         linear_skinny_kernel<16, 2><<<(a.N + 15) / 16, 256, 0, st>>>(a);
+    } else if (linear_tc_supports(a)) {
+        int splits = linear_tc_splits(a, num_sms);
+        if (!wsp || linear_tc_workspace_floats(a, splits) > wsp->ws_floats || linear_tc_tiles(a) > wsp->n_counters)
+            splits = 1;
+        return launch_linear_tc(a, splits, wsp ? wsp->ws : nullptr, wsp ? wsp->tile_count : nullptr, err, st);
     } else {
         if (a.K % 32) return cudaErrorInvalidValue;
         dim3 grid((a.N + 63) / 64, (a.M + 63) / 64);

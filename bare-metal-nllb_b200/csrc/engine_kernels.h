@@ -11,7 +11,7 @@ struct LinearArgs {
     const float* x;
     int ldx;                 // row stride of x (elements)
     const int8_t* w;         // [N][K] int8
-    const float* inv_scale;  // [N] 1 / weight_scale
+    const float* scale;      // [N] CT2 weight_scale: weight = int8 * (1.0f / scale)
     const float* bias;       // [N] or null
     float* out;
     const float* residual;   // same addressing as out, or null
@@ -26,7 +26,26 @@ cudaError_t launch_embed_pos(float* x, const int* tokens, const int* positions, 
                              int vocab, cudaStream_t st);
 cudaError_t launch_layernorm(float* out, float* x, const float* res, const float* gamma, const float* beta,
                              int rows, cudaStream_t st);
-cudaError_t launch_linear(const LinearArgs& a, cudaStream_t st);
+// Split-K workspace of the tensor-core linear kernel: partial tiles and one
+// arrival counter per output tile (zero between calls).
+struct LinearWorkspace {
+    float* ws = nullptr;
+    size_t ws_floats = 0;
+    int* tile_count = nullptr;
+    size_t n_counters = 0;
+};
+
+// Dispatch: <= 16 rows skinny SIMT kernel, else the tcgen05 kernel (K % 64 == 0;
+// split-K when the output has fewer tiles than twice the SMs and the workspace
+// is large enough) or the tiled SIMT kernel.  err: device error word.
+cudaError_t launch_linear(const LinearArgs& a, const LinearWorkspace* wsp, int num_sms, int* err, cudaStream_t st);
+cudaError_t configure_linear_tc();
+bool linear_tc_supports(const LinearArgs& a);
+int linear_tc_splits(const LinearArgs& a, int num_sms);
+size_t linear_tc_workspace_floats(const LinearArgs& a, int splits);
+size_t linear_tc_tiles(const LinearArgs& a);
+cudaError_t launch_linear_tc(const LinearArgs& a, int splits, float* ws, int* tile_count, int* err,
+                             cudaStream_t st);
 cudaError_t launch_penalties(float* logits, size_t ld, const int* hist, int hist_ld, const int* n_tokens,
                              const unsigned char* active, int rows, float penalty, int ngram, cudaStream_t st);
 cudaError_t launch_logsoftmax_topk(const float* logits, size_t ld, int V, int rows, const unsigned char* active,

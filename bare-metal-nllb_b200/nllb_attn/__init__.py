@@ -82,6 +82,7 @@ SIGNATURES = {
     "nllb_translate": (_c_int, [_c_void_p, _c_int, _fp, _fp, _c_int, ctypes.POINTER(TranslateOpts),
                                 _fp, _fp, _fp, ctypes.POINTER(TranslateStats)]),
     "nllb_translate_margins": (_c_int, [_c_void_p, _c_int, _fp, _c_int]),
+    "nllb_linear_int8": (_c_int, [_fp, _c_int, _c_int, _fp, _fp, _fp, _c_int, _fp, _fp, _c_int, _c_void_p]),
 }
 
 _LIB: Optional[ctypes.CDLL] = None
@@ -290,6 +291,22 @@ class Model:
         buf = np.zeros(max_steps, np.float32)
         n = self.lib.nllb_translate_margins(self.handle, sentence, ptr(buf), max_steps)
         return buf[:n]
+
+
+LINEAR_RELU = 1
+
+
+def linear_int8(x, w, weight_scale, bias=None, out=None, residual=None, relu=False, stream=None):
+    """nllb_linear_int8 on torch CUDA tensors: x [M][K] fp32, w [N][K] int8."""
+    lib = load()
+    M, K = x.shape
+    N = w.shape[0]
+    if out is None:
+        import torch
+        out = torch.empty((M, N), dtype=torch.float32, device=x.device)
+    _check(lib, lib.nllb_linear_int8(ptr(x), M, K, ptr(w), ptr(weight_scale), ptr(bias), N, ptr(out),
+                                     ptr(residual), LINEAR_RELU if relu else 0, stream), "nllb_linear_int8")
+    return out
 
 
 def exported_symbols(header_path: str) -> Sequence[str]:

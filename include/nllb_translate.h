@@ -67,6 +67,21 @@ NLLB_ATTN_API int nllb_translate(nllb_model* m, int n_sentences, const int* src_
  * written (at most max_steps). */
 NLLB_ATTN_API int nllb_translate_margins(const nllb_model* m, int sentence, float* out, int max_steps);
 
+/* ---- INT8-weight linear layer -------------------------------------------
+ * out[m][n] = sum_k x[m][k] * (w[n][k] * (1.0f / weight_scale[n])) + bias[n]
+ * for M rows at once: mat_vec_int8 (tensor.c:144-196) batched, with the
+ * CTranslate2 scale convention (the int8 value is DIVIDED by weight_scale).
+ * With NLLB_LINEAR_RELU the result is clamped at 0 (relu, tensor.c:242-245);
+ * a non-NULL residual (same layout as out) is added last (residual_add,
+ * tensor.c:249-251).  Device pointers, row-major x [M][K], w [N][K],
+ * out [M][N]; asynchronous on `stream` (a cudaStream_t, NULL = default).
+ * More than 16 rows run on the tensor cores (int8 weights exact in bf16,
+ * activations split into three bf16 parts, fp32 accumulation). */
+#define NLLB_LINEAR_RELU 1
+NLLB_ATTN_API int nllb_linear_int8(const float* x, int M, int K, const int8_t* w, const float* weight_scale,
+                                   const float* bias, int N, float* out, const float* residual, int flags,
+                                   void* stream);
+
 #ifdef __cplusplus
 }
 #endif
