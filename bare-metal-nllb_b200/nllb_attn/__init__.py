@@ -83,6 +83,8 @@ SIGNATURES = {
                                 _fp, _fp, _fp, ctypes.POINTER(TranslateStats)]),
     "nllb_translate_margins": (_c_int, [_c_void_p, _c_int, _fp, _c_int]),
     "nllb_linear_int8": (_c_int, [_fp, _c_int, _c_int, _fp, _fp, _fp, _c_int, _fp, _fp, _c_int, _c_void_p]),
+    "nllb_linear_int8_noalloc": (_c_int, [_fp, _c_int, _c_int, _fp, _fp, _fp, _c_int, _fp, _fp, _c_int,
+                                          _c_void_p]),
 }
 
 _LIB: Optional[ctypes.CDLL] = None
@@ -306,6 +308,18 @@ def linear_int8(x, w, weight_scale, bias=None, out=None, residual=None, relu=Fal
         out = torch.empty((M, N), dtype=torch.float32, device=x.device)
     _check(lib, lib.nllb_linear_int8(ptr(x), M, K, ptr(w), ptr(weight_scale), ptr(bias), N, ptr(out),
                                      ptr(residual), LINEAR_RELU if relu else 0, stream), "nllb_linear_int8")
+    return out
+
+
+def linear_int8_noalloc(x, w, weight_scale, out, bias=None, residual=None, relu=False, stream=None):
+    """nllb_linear_int8_noalloc on torch CUDA tensors; `out` must be given
+    (the call allocates nothing, the caller owns every buffer)."""
+    lib = load()
+    M, K = x.shape
+    N = w.shape[0]
+    _check(lib, lib.nllb_linear_int8_noalloc(ptr(x), M, K, ptr(w), ptr(weight_scale), ptr(bias), N, ptr(out),
+                                             ptr(residual), LINEAR_RELU if relu else 0, stream),
+           "nllb_linear_int8_noalloc")
     return out
 
 

@@ -82,6 +82,25 @@ NLLB_ATTN_API int nllb_linear_int8(const float* x, int M, int K, const int8_t* w
                                    const float* bias, int N, float* out, const float* residual, int flags,
                                    void* stream);
 
+/* Same computation as nllb_linear_int8, for callers that cannot have a
+ * library allocate device memory while they run -- a serving process that
+ * hands out all device memory from its own pool reserved at start-up, or a
+ * loop with a fixed memory plan that must not pay cudaMalloc's implicit
+ * device synchronisation.  No counterpart in the reference (its mat-vec
+ * needs no scratch).  Allocates nothing: the split-K scratch is a fixed
+ * 8 MB array inside the library that every GPU loading the library holds
+ * until exit.  The first call on a device looks that array up (device
+ * current); make it before any stream capture.  Calls share the array:
+ * calls whose kernels overlap on the GPU race.  At most
+ * NLLB_LINEAR_NOALLOC_MAX_ROWS rows, _MAX_OUT outputs, _MAX_IN inputs;
+ * larger shapes return NLLB_ATTN_ECAPACITY. */
+#define NLLB_LINEAR_NOALLOC_MAX_ROWS 256
+#define NLLB_LINEAR_NOALLOC_MAX_OUT 4096
+#define NLLB_LINEAR_NOALLOC_MAX_IN 4096
+NLLB_ATTN_API int nllb_linear_int8_noalloc(const float* x, int M, int K, const int8_t* w,
+                                           const float* weight_scale, const float* bias, int N, float* out,
+                                           const float* residual, int flags, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
