@@ -18,6 +18,8 @@
 #include <string>
 #include <vector>
 
+#include <cuda_bf16.h>
+
 #include "attn_internal.h"
 #include "engine_kernels.h"
 #include "nllb_translate.h"
@@ -188,6 +190,8 @@ struct Lin {
     float* scale = nullptr;  // CT2 weight_scale (weight = int8 / scale)
     float* b = nullptr;
     int out = 0, in = 0;
+    void* wb = nullptr;  // bf16 copy of w (exact), operand of the TMA-fed tensor-core kernel
+    CUtensorMap tm{};    // tensor map of wb: [out][in], box 64 x 128, 128-byte swizzle
 };
 
 }  // namespace
@@ -213,6 +217,12 @@ struct nllb_model {
     int pos_rows = 0;
     nllb_attn_ctx* attn = nullptr;
     LinearWorkspace lws;  // split-K workspace of the tensor-core linear kernel
+    Lin vocab;            // tied output projection: the shared embedding (decoder.c:319-354)
+    // activations split into bf16 planes for the TMA-fed linear kernel ([3][M][K]),
+    // grow-only, with its tensor maps per (M, K)
+    void* planes = nullptr;
+    size_t planes_elems = 0;
+    std::map<std::pair<int, int>, CUtensorMap> plane_maps;
     int num_sms = 148;
     // decision margins of the last translate call, [sentence][step]
     std::vector<std::vector<float>> margins;
@@ -259,6 +269,16 @@ struct Loader {
         ENG_RC(upload(prefix + "/weight", "I8", (long long)out_f * in_f, &L->w));
         ENG_RC(upload(prefix + "/weight_scale", "F32", out_f, &L->scale));
         if (tensors.count(prefix + "/bias")) ENG_RC(upload(prefix + "/bias", "F32", out_f, &L->b));
+        return bf16_copy(L);
+    }
+    // bf16 copy of the int8 weight (every int8 is exact in bf16) and its tensor map
+    int bf16_copy(Lin* L) {
+        if (L->in % 64) return NLLB_ATTN_OK;  // the TMA kernel takes K % 64 == 0 only
+        __nv_bfloat16* wb = nullptr;
+        ENG_RC(dev_alloc(m, &wb, (size_t)L->out * L->in));
+        ENG_CK(launch_int8_to_bf16(L->w, wb, (size_t)L->out * L->in, m->stream));
+        ENG_CK(encode_bf16_map(&L->tm, wb, L->in, L->out, 1));
+        L->wb = wb;
         return NLLB_ATTN_OK;
     }
     int norm(const std::string& prefix, float** g, float** b) {
@@ -305,6 +325,7 @@ void nllb_model_free(nllb_model* m) {
     if (m->stream) cudaStreamSynchronize(m->stream);
     if (m->attn) nllb_attn_destroy(m->attn);
     for (void* p : m->allocs) cudaFree(p);
+    if (m->planes) cudaFree(m->planes);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
 }
@@ -330,8 +351,8 @@ int nllb_model_load(const char* path, int device, int max_sentences, int max_src
     };
     if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess)
         return fail(nllb::set_error(NLLB_ATTN_ECUDA, "cudaStreamCreate failed"));
-    if (configure_linear_tc() != cudaSuccess)
-        return fail(nllb::set_error(NLLB_ATTN_ECUDA, "cannot configure the tensor-core linear kernel"));
+    if (configure_linear_tc() != cudaSuccess || configure_linear_tma() != cudaSuccess)
+        return fail(nllb::set_error(NLLB_ATTN_ECUDA, "cannot configure the tensor-core linear kernels"));
     m->num_sms = attn->num_sms;
     // split-K: at most 2*SMs*8 partial 128x128 tiles, one counter per tile of the largest output
     m->lws.ws_floats = (size_t)2 * m->num_sms * 8 * 128 * 128;
@@ -366,6 +387,11 @@ int nllb_model_load(const char* path, int device, int max_sentences, int max_src
         ENG_RC(L.upload("decoder/embeddings/weight_scale", "F32", VOCAB, &m->emb_scale));
         ENG_RC(dev_alloc(m, &m->emb_inv, VOCAB));
         ENG_CK(launch_reciprocal(m->emb_inv, m->emb_scale, VOCAB, m->stream));
+        m->vocab.w = m->emb;
+        m->vocab.scale = m->emb_scale;
+        m->vocab.out = VOCAB;
+        m->vocab.in = D;
+        ENG_RC(L.bf16_copy(&m->vocab));
         for (int i = 0; i < LAYERS; ++i) {
             const std::string p = "encoder/layer_" + std::to_string(i);
             auto& E = m->enc[i];
@@ -426,7 +452,33 @@ int run_linear(nllb_model* m, const Lin& L, const float* x, int M, float* out, c
     a.cblock = cblock;
     a.relu = relu;
     a.mask_from = mask_from;
+    if (M > 16 && L.wb && (size_t)M * L.in * 3 <= m->planes_elems) {
+        // x -> three bf16 planes, then the TMA-fed tensor-core GEMM
+        ENG_CK(launch_split3(x, L.in, M, L.in, m->planes, m->stream));
+        auto it = m->plane_maps.find({M, L.in});
+        if (it == m->plane_maps.end()) {
+            CUtensorMap tx;
+            ENG_CK(encode_bf16_map(&tx, m->planes, L.in, M, 3));
+            it = m->plane_maps.emplace(std::make_pair(M, L.in), tx).first;
+        }
+        const int splits = linear_tma_splits(M, L.out, L.in, m->num_sms);
+        ENG_CK(launch_linear_tma(a, &it->second, &L.tm, splits, m->attn->err, m->stream));
+        return NLLB_ATTN_OK;
+    }
     ENG_CK(launch_linear(a, &m->lws, m->num_sms, m->attn->err, m->stream));
+    return NLLB_ATTN_OK;
+}
+
+// Grow the activation-plane buffer to `elems` bf16 values.
+int ensure_planes(nllb_model* m, size_t elems) {
+    if (elems <= m->planes_elems) return NLLB_ATTN_OK;
+    ENG_CK(cudaStreamSynchronize(m->stream));
+    if (m->planes) cudaFree(m->planes);
+    m->planes = nullptr;
+    m->planes_elems = 0;
+    m->plane_maps.clear();
+    ENG_CK(cudaMalloc(&m->planes, elems * sizeof(__nv_bfloat16)));
+    m->planes_elems = elems;
     return NLLB_ATTN_OK;
 }
 
@@ -523,13 +575,7 @@ int decode_step(nllb_model* m, Work& w, int step) {
 // Tied vocabulary projection with language rows masked (decoder.c:319-354),
 // penalties (main.c:186-213) and log-softmax + top-k (main.c:154-182).
 int vocab_topk(nllb_model* m, Work& w, int k, bool penalties, const nllb_translate_opts& o) {
-    Lin E;
-    E.w = m->emb;
-    E.scale = m->emb_scale;
-    E.b = nullptr;
-    E.out = VOCAB;
-    E.in = D;
-    ENG_RC(run_linear(m, E, w.h, w.rows, w.logits, nullptr, 0, VOCAB, LANG_START));
+    ENG_RC(run_linear(m, m->vocab, w.h, w.rows, w.logits, nullptr, 0, VOCAB, LANG_START));
     if (penalties)
         ENG_CK(launch_penalties(w.logits, VOCAB, w.hist, m->max_gen, w.ntok, w.active, w.rows,
                                 o.repetition_penalty, o.no_repeat_ngram, m->stream));
@@ -577,6 +623,7 @@ extern "C" int nllb_translate(nllb_model* m, int n_sent, const int* src_tokens, 
     w.rows_enc = n_sent * S;
     w.rows = n_sent * NB;
     const size_t RE = (size_t)w.rows_enc, R = (size_t)w.rows;
+    ENG_RC(ensure_planes(m, std::max(RE, R) * FFN * 3));
     ENG_RC(w.alloc(&w.ex, RE * D));
     ENG_RC(w.alloc(&w.eh, RE * D));
     ENG_RC(w.alloc(&w.eqkv, RE * 3 * D));

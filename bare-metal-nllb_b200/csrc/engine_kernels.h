@@ -2,6 +2,7 @@
 #pragma once
 #include <cstddef>
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace nllb {
@@ -46,6 +47,16 @@ size_t linear_tc_workspace_floats(const LinearArgs& a, int splits);
 size_t linear_tc_tiles(const LinearArgs& a);
 cudaError_t launch_linear_tc(const LinearArgs& a, int splits, float* ws, int* tile_count, int* err,
                              cudaStream_t st);
+// TMA-fed tcgen05 linear layer over bf16 operands (linear_tma.cu): weights
+// kept as a bf16 copy of the int8 matrix, activations split into three bf16
+// planes [3][M][K] by launch_split3.  K % 64 == 0, K >= 64.
+cudaError_t configure_linear_tma();
+cudaError_t encode_bf16_map(CUtensorMap* map, const void* base, int cols, int rows, int planes);
+int linear_tma_splits(int M, int N, int K, int num_sms);
+cudaError_t launch_split3(const float* x, int ldx, int M, int K, void* planes, cudaStream_t st);
+cudaError_t launch_int8_to_bf16(const int8_t* w, void* out, size_t n, cudaStream_t st);
+cudaError_t launch_linear_tma(const LinearArgs& a, const CUtensorMap* tx, const CUtensorMap* tw, int splits, int* err,
+                              cudaStream_t st);
 cudaError_t launch_penalties(float* logits, size_t ld, const int* hist, int hist_ld, const int* n_tokens,
                              const unsigned char* active, int rows, float penalty, int ngram, cudaStream_t st);
 cudaError_t launch_logsoftmax_topk(const float* logits, size_t ld, int V, int rows, const unsigned char* active,

@@ -1,0 +1,342 @@
+// linear_tma.cu -- INT8-weight linear layer for the translation engine on
+// tcgen05 tensor cores, fed by TMA (sm_100a).
+//
+// Same arithmetic as linear_tc.cu (int8 weights exact in bf16, fp32
+// activations as three bf16 parts x1 + x2 + x3, three MMAs per k-step, fp32
+// accumulation in TMEM), with the conversions moved out of the GEMM: the
+// engine keeps a bf16 copy of every weight matrix (converted once at load)
+// and splits each activation matrix into its three planes once per GEMM
+// (split3_kernel), so the GEMM's operands are plain bf16 matrices that TMA
+// tensor maps load straight into 128-byte-swizzled shared memory.
+//
+// CTA: warps 0-7 epilogue, warp 8 lane 0 TMA producer, warp 9 lane 0 MMA
+// issuer; 128 x 128 output tile; K in stages of 64 (3 X planes + W = 64 KB
+// per stage, 3 stages).  Split-K over a thread-block cluster along x: the S
+// CTAs of a tile each leave their 128 x 128 partial sum in shared memory and
+// cluster rank z reduces rows [z*128/S, (z+1)*128/S) over all S partials in
+// rank order (distributed shared memory; deterministic; no workspace).
+// Grid x = (row tile, split) fastest, so the row tiles that share a weight
+// tile run together and the weight tile is read from DRAM once.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "device_common.cuh"
+#include "engine_kernels.h"
+
+namespace nllb {
+
+namespace {
+
+constexpr int TM = 128, TN = 128, TK = 64, STAGES = 3;
+constexpr int EPI_WARPS = 8, THREADS = (EPI_WARPS + 2) * 32;
+constexpr uint32_t PLANE = TM * TK * 2;      // 16 KB
+constexpr uint32_t STAGE_BYTES = 4 * PLANE;  // x1, x2, x3, w
+constexpr uint32_t SMEM_BAR = STAGES * STAGE_BYTES;
+constexpr uint32_t SMEM_TOTAL = SMEM_BAR + 128 + 1024;
+constexpr uint32_t TMEM_COLS = 128;
+constexpr int PART_STRIDE = TN + 4;  // floats per row of the partial tile in shared memory
+
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// y = accumulator / scale[n] (the per-column dequantisation factor of tensor.c:75)
+__device__ __forceinline__ void epilogue_store(const LinearArgs& a, int m, int n, float y) {
+    if (a.bias) y += a.bias[n];
+    if (a.relu) y = fmaxf(y, 0.f);
+    if (a.mask_from >= 0 && n >= a.mask_from) y = -1e30f;
+    const size_t o = (size_t)(n / a.cblock) * ((size_t)a.M * a.cblock) + (size_t)m * a.cblock + (n % a.cblock);
+    if (a.residual) y += a.residual[o];
+    a.out[o] = y;
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    linear_tma_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw,
+                      const LinearArgs a, int splits, int* err) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base_addr = (raw + 1023u) & ~1023u;
+    unsigned char* base = smem_raw + (base_addr - raw);
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + SMEM_BAR);
+    uint64_t* empty = full + STAGES;
+    uint64_t* done = empty + STAGES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    int* s_abort = reinterpret_cast<int*>(tmem_slot + 1);
+    __shared__ float s_inv[TN];
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int S = splits, z = blockIdx.x % S, mt = blockIdx.x / S;
+    const int m0 = mt * TM, n0 = blockIdx.y * TN;
+    const int nk_all = a.K / TK;
+    const int kc0 = (int)((long long)z * nk_all / S), kc1 = (int)((long long)(z + 1) * nk_all / S);
+    const int nk = kc1 - kc0;
+
+    if (warp == 0) tmem_alloc(tmem_slot, TMEM_COLS);
+    if (tid == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(done, 1);
+        fence_barrier_init();
+        *s_abort = 0;
+    }
+    if (tid < TN) s_inv[tid] = (n0 + tid < a.N) ? 1.0f / a.scale[n0 + tid] : 0.f;  // 1/scale as tensor.c:75
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == EPI_WARPS && lane == 0) {
+        // ---- TMA producer
+        for (int c = 0; c < nk; ++c) {
+            const int s = c % STAGES;
+            if (c >= STAGES && !mbar_wait_bounded(&empty[s], (uint32_t)((c / STAGES - 1) & 1))) {
+                atomicExch(s_abort, 1);
+                break;
+            }
+            unsigned char* st = base + s * STAGE_BYTES;
+            const int k = (kc0 + c) * TK;
+            mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+            tma_load_3d(st, &tx, k, m0, 0, &full[s]);  // box 64 x 128 x 3: the three planes
+            tma_load_2d(st + 3 * PLANE, &tw, k, n0, &full[s]);
+        }
+    } else if (warp == EPI_WARPS + 1 && lane == 0) {
+        // ---- MMA issuer
+        constexpr uint32_t idesc = idesc_bf16(TM, TN);
+        for (int c = 0; c < nk; ++c) {
+            const int s = c % STAGES;
+            if (!mbar_wait_bounded(&full[s], (uint32_t)((c / STAGES) & 1))) {
+                atomicExch(s_abort, 1);
+                break;
+            }
+            tc_fence_after();
+            const uint32_t st = base_addr + s * STAGE_BYTES;
+#pragma unroll
+            for (int ks = 0; ks < TK / 16; ++ks) {
+                const uint64_t bw = umma_desc_k_sw128(st + 3 * PLANE + ks * 32);
+                mma_bf16(tmem, umma_desc_k_sw128(st + 0 * PLANE + ks * 32), bw, idesc, (c > 0 || ks > 0) ? 1u : 0u);
+                mma_bf16(tmem, umma_desc_k_sw128(st + 1 * PLANE + ks * 32), bw, idesc, 1u);
+                mma_bf16(tmem, umma_desc_k_sw128(st + 2 * PLANE + ks * 32), bw, idesc, 1u);
+            }
+            tc_commit(&empty[s]);
+        }
+        tc_commit(done);
+    }
+
+    // ---- accumulator -> shared memory (two threads per row, 64 columns each)
+    float* part = reinterpret_cast<float*>(base);  // the stage ring is idle once `done` has fired
+    if (warp < EPI_WARPS) {
+        const int quarter = warp & 3, half = (warp >> 2) & 1;
+        const int rloc = quarter * 32 + lane;
+        const bool ok = mbar_wait_bounded(done, 0u);
+        tc_fence_after();
+        if (!ok) {
+            atomicExch(s_abort, 1);
+        } else {
+            float v[64];
+            tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(half * 64), v);
+            tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(half * 64 + 32), v + 32);
+            float4* row = reinterpret_cast<float4*>(part + rloc * PART_STRIDE + half * 64);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) row[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        }
+    }
+    if (S == 1) __syncthreads();
+    else cluster_sync_all();
+
+    // ---- rank z finishes rows [z*R, (z+1)*R) of the tile: sum of the S partials
+    // in rank order, epilogue, coalesced stores (one warp per 128-column row)
+    int aborted = 0;
+    if (S == 1) aborted = *(volatile int*)s_abort;
+    else
+        for (int r = 0; r < S; ++r) aborted |= ld_cluster_s32(map_rank(s_abort, r));
+    if (aborted) {
+        if (tid == 0) atomicOr(err, NLLB_DEV_ERR_TIMEOUT);
+    } else {
+        const int R = TM / S;
+        const bool vec = (a.cblock % 4 == 0) && ((reinterpret_cast<uintptr_t>(a.out) & 15) == 0) &&
+                         ((reinterpret_cast<uintptr_t>(a.residual) & 15) == 0) &&
+                         ((reinterpret_cast<uintptr_t>(a.bias) & 15) == 0);
+        for (int item = tid; item < R * (TN / 4); item += THREADS) {
+            const int rr = z * R + item / (TN / 4), c4 = item % (TN / 4);
+            const int m = m0 + rr;
+            if (m >= a.M) break;  // rows grow with item
+            const float* src = part + rr * PART_STRIDE + c4 * 4;
+            float4 acc;
+            if (S == 1) {
+                acc = *reinterpret_cast<const float4*>(src);
+            } else {
+                acc = ld_cluster_f4(map_rank(src, 0));
+                for (int r = 1; r < S; ++r) {
+                    const float4 p = ld_cluster_f4(map_rank(src, r));
+                    acc.x += p.x;
+                    acc.y += p.y;
+                    acc.z += p.z;
+                    acc.w += p.w;
+                }
+            }
+            const int nl = c4 * 4, n = n0 + nl;
+            float y[4] = {acc.x * s_inv[nl], acc.y * s_inv[nl + 1], acc.z * s_inv[nl + 2], acc.w * s_inv[nl + 3]};
+            if (vec && n + 3 < a.N) {
+                if (a.bias) {
+                    const float4 b = *reinterpret_cast<const float4*>(a.bias + n);
+                    y[0] += b.x, y[1] += b.y, y[2] += b.z, y[3] += b.w;
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    if (a.relu) y[j] = fmaxf(y[j], 0.f);
+                    if (a.mask_from >= 0 && n + j >= a.mask_from) y[j] = -1e30f;
+                }
+                const size_t o =
+                    (size_t)(n / a.cblock) * ((size_t)a.M * a.cblock) + (size_t)m * a.cblock + (n % a.cblock);
+                if (a.residual) {
+                    const float4 r = *reinterpret_cast<const float4*>(a.residual + o);
+                    y[0] += r.x, y[1] += r.y, y[2] += r.z, y[3] += r.w;
+                }
+                *reinterpret_cast<float4*>(a.out + o) = make_float4(y[0], y[1], y[2], y[3]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (n + j < a.N) epilogue_store(a, m, n + j, y[j]);
+            }
+        }
+    }
+    if (S > 1) cluster_sync_all();  // partners keep their partials until every rank is done reading
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+// x [M][ldx] fp32 -> planes [3][M][K] bf16 with x = p0 + p1 + p2 (to 24 bits)
+__global__ void split3_kernel(const float* x, int ldx, int M, int K, __nv_bfloat16* planes) {
+    const size_t n4 = (size_t)M * (K / 4);
+    const size_t plane = (size_t)M * K;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+        const int m = (int)(i / (K / 4)), k = (int)(i % (K / 4)) * 4;
+        const float4 v = *reinterpret_cast<const float4*>(x + (size_t)m * ldx + k);
+        const float f[4] = {v.x, v.y, v.z, v.w};
+        __nv_bfloat16 p[3][4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            p[0][e] = __float2bfloat16_rn(f[e]);
+            const float r1 = f[e] - __bfloat162float(p[0][e]);
+            p[1][e] = __float2bfloat16_rn(r1);
+            p[2][e] = __float2bfloat16_rn(r1 - __bfloat162float(p[1][e]));
+        }
+        const size_t o = (size_t)m * K + k;
+#pragma unroll
+        for (int q = 0; q < 3; ++q) *reinterpret_cast<uint2*>(planes + q * plane + o) = *reinterpret_cast<const uint2*>(p[q]);
+    }
+}
+
+__global__ void int8_to_bf16_kernel(const int8_t* w, __nv_bfloat16* out, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = __float2bfloat16_rn((float)w[i]);
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+}  // namespace
+
+cudaError_t configure_linear_tma() {
+    cudaError_t e = cudaFuncSetAttribute(linear_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_TOTAL);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(linear_tma_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+}
+
+// Tensor map of a row-major bf16 matrix stack: `planes` matrices of
+// [rows][cols] (K-major), box 64 columns x 128 rows, 128-byte swizzle.
+cudaError_t encode_bf16_map(CUtensorMap* map, const void* base, int cols, int rows, int planes) {
+    std::call_once(g_encode_once, [] {
+        cudaDriverEntryPointQueryResult q;
+        void* fn = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    if (!g_encode) return cudaErrorNotSupported;
+    const cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)planes};
+    const cuuint64_t strides[2] = {(cuuint64_t)cols * 2, (cuuint64_t)cols * rows * 2};
+    const cuuint32_t box[3] = {(cuuint32_t)TK, (cuuint32_t)TM, (cuuint32_t)planes};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, planes > 1 ? 3 : 2, const_cast<void*>(base),
+                                dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+int linear_tma_splits(int M, int N, int K, int num_sms) {
+    const int tiles = ((N + TN - 1) / TN) * ((M + TM - 1) / TM);
+    const int nk = K / TK;
+    int S = 1;
+    while (S < 8 && tiles * S < 2 * num_sms && nk / (2 * S) >= 2) S *= 2;  // 1, 2, 4, 8: divides 128 rows
+    return S;
+}
+
+cudaError_t launch_split3(const float* x, int ldx, int M, int K, void* planes, cudaStream_t st) {
+    const size_t n4 = (size_t)M * (K / 4);
+    int blocks = (int)((n4 + 255) / 256);
+    blocks = blocks < 4096 ? blocks : 4096;
+    if (blocks < 1) return cudaSuccess;
+    split3_kernel<<<blocks, 256, 0, st>>>(x, ldx, M, K, static_cast<__nv_bfloat16*>(planes));
+    return cudaGetLastError();
+}
+
+cudaError_t launch_int8_to_bf16(const int8_t* w, void* out, size_t n, cudaStream_t st) {
+    int blocks = (int)((n + 255) / 256);
+    blocks = blocks < 8192 ? blocks : 8192;
+    int8_to_bf16_kernel<<<blocks, 256, 0, st>>>(w, static_cast<__nv_bfloat16*>(out), n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_linear_tma(const LinearArgs& a, const CUtensorMap* tx, const CUtensorMap* tw, int splits, int* err,
+                              cudaStream_t st) {
+    const int mt = (a.M + TM - 1) / TM, nt = (a.N + TN - 1) / TN;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(mt * splits, nt, 1);
+    cfg.blockDim = dim3(THREADS, 1, 1);
+    cfg.dynamicSmemBytes = SMEM_TOTAL;
+    cfg.stream = st;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = (unsigned)splits;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, linear_tma_kernel, *tx, *tw, a, splits, err);
+}
+
+}  // namespace nllb

@@ -85,6 +85,10 @@ SIGNATURES = {
     "nllb_linear_int8": (_c_int, [_fp, _c_int, _c_int, _fp, _fp, _fp, _c_int, _fp, _fp, _c_int, _c_void_p]),
     "nllb_linear_int8_noalloc": (_c_int, [_fp, _c_int, _c_int, _fp, _fp, _fp, _c_int, _fp, _fp, _c_int,
                                           _c_void_p]),
+    "nllb_linear_prepare": (_c_int, [_fp, _fp, _fp, _c_int, _c_int, _c_void_p, ctypes.POINTER(_c_void_p)]),
+    "nllb_linear_run": (_c_int, [_c_void_p, _fp, _c_int, _fp, _fp, _c_int, _c_void_p]),
+    "nllb_linear_status": (_c_int, [_c_void_p]),
+    "nllb_linear_free": (None, [_c_void_p]),
 }
 
 _LIB: Optional[ctypes.CDLL] = None
@@ -321,6 +325,49 @@ def linear_int8_noalloc(x, w, weight_scale, out, bias=None, residual=None, relu=
                                              ptr(residual), LINEAR_RELU if relu else 0, stream),
            "nllb_linear_int8_noalloc")
     return out
+
+
+class PreparedLinear:
+    """nllb_linear_prepare / nllb_linear_run: one LinearInt8 resident on the
+    GPU.  Keeps references to the weight tensors, which the layer reads."""
+
+    def __init__(self, w, weight_scale, bias=None, stream=None):
+        self._lib = load()
+        self._keep = (w, weight_scale, bias)
+        self.N, self.K = w.shape
+        h = _c_void_p()
+        _check(self._lib, self._lib.nllb_linear_prepare(ptr(w), ptr(weight_scale), ptr(bias), self.N, self.K,
+                                                         stream, ctypes.byref(h)), "nllb_linear_prepare")
+        self._h = h
+
+    def __call__(self, x, out=None, residual=None, relu=False, stream=None):
+        M = x.shape[0]
+        if out is None:
+            import torch
+            out = torch.empty((M, self.N), dtype=torch.float32, device=x.device)
+        _check(self._lib, self._lib.nllb_linear_run(self._h, ptr(x), M, ptr(out), ptr(residual),
+                                                     LINEAR_RELU if relu else 0, stream), "nllb_linear_run")
+        return out
+
+    def status(self) -> int:
+        return self._lib.nllb_linear_status(self._h)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self._lib.nllb_linear_free(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def exported_symbols(header_path: str) -> Sequence[str]:

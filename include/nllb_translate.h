@@ -101,6 +101,29 @@ NLLB_ATTN_API int nllb_linear_int8_noalloc(const float* x, int M, int K, const i
                                            const float* weight_scale, const float* bias, int N, float* out,
                                            const float* residual, int flags, void* stream);
 
+/* ---- INT8 linear layer with weights prepared once --------------------------
+ * A LinearInt8 (pico.h:26-32) made resident on the current GPU: the layer
+ * keeps the caller's device pointers w [N][K], weight_scale [N] and bias [N]
+ * (NULL: none) -- they must stay valid until nllb_linear_free -- plus its own
+ * bf16 copy of w (exact) with a TMA tensor map.  nllb_linear_run computes
+ * what nllb_linear_int8 computes for those weights: more than 16 rows run on
+ * the TMA-fed tcgen05 kernel over the bf16 copy, fewer on the SIMT kernel
+ * over the int8 matrix.  K must be a positive multiple of 64.  The reference
+ * dequantises inside every mat_vec_int8 (tensor.c:144-196) and has no
+ * prepared form; this is the form the translation engine keeps its layers in.
+ * A layer owns a grow-only activation buffer: runs of one layer whose kernels
+ * overlap on the GPU (different streams, no ordering) race on it.  The first
+ * run with more rows than before allocates (and synchronises `stream`).
+ * nllb_linear_status synchronises the device and reports a bounded device
+ * wait that gave up (NLLB_ATTN_ETIMEOUT). */
+typedef struct nllb_linear nllb_linear;
+NLLB_ATTN_API int nllb_linear_prepare(const int8_t* w, const float* weight_scale, const float* bias, int N, int K,
+                                      void* stream, nllb_linear** out);
+NLLB_ATTN_API int nllb_linear_run(nllb_linear* layer, const float* x, int M, float* out, const float* residual,
+                                  int flags, void* stream);
+NLLB_ATTN_API int nllb_linear_status(nllb_linear* layer);
+NLLB_ATTN_API void nllb_linear_free(nllb_linear* layer);
+
 #ifdef __cplusplus
 }
 #endif
