@@ -491,6 +491,7 @@ struct Work {
     float* logits = nullptr;
     int *tok = nullptr, *hist = nullptr, *ntok = nullptr, *parent = nullptr, *top_tok = nullptr;
     float* top_lp = nullptr;
+    float* topk_ws = nullptr;  // partials of the vocabulary log-softmax / top-k
     unsigned char* active = nullptr;
     std::vector<void*> allocs;
     ~Work() {
@@ -579,7 +580,8 @@ int vocab_topk(nllb_model* m, Work& w, int k, bool penalties, const nllb_transla
     if (penalties)
         ENG_CK(launch_penalties(w.logits, VOCAB, w.hist, m->max_gen, w.ntok, w.active, w.rows,
                                 o.repetition_penalty, o.no_repeat_ngram, m->stream));
-    ENG_CK(launch_logsoftmax_topk(w.logits, VOCAB, VOCAB, w.rows, w.active, k, w.top_tok, w.top_lp, m->stream));
+    ENG_CK(launch_logsoftmax_topk(w.logits, VOCAB, VOCAB, w.rows, w.active, k, w.top_tok, w.top_lp, w.topk_ws,
+                                  m->stream));
     return NLLB_ATTN_OK;
 }
 
@@ -645,6 +647,7 @@ extern "C" int nllb_translate(nllb_model* m, int n_sent, const int* src_tokens, 
     ENG_RC(w.alloc(&w.ntok, R));
     ENG_RC(w.alloc(&w.parent, R));
     ENG_RC(w.alloc(&w.top_tok, R * 8));
+    ENG_RC(w.alloc(&w.topk_ws, vocab_topk_ws_floats(VOCAB, w.rows, 8)));
     ENG_RC(w.alloc(&w.top_lp, R * 8));
     ENG_RC(w.alloc(&w.active, R));
 

@@ -237,9 +237,10 @@ __global__ void penalties_kernel(float* logits, size_t ld, const int* hist, int 
 
 // ---------------------------------------------------------------------------
 // log-softmax over the vocabulary and the K best entries (main.c:154-182):
-// one CTA per row; max and sum of exp by block reduction, top-K kept per
-// thread (greater value first, lower index first among equals, as
-// find_topk's strict comparison does) and merged across the CTA.
+// each row split into C column chunks (about 8 CTAs per SM in all); one
+// streaming pass per chunk keeps an online max and sum of exp and a per-thread
+// top-K (greater value first, lower index first among equals, as find_topk's
+// strict comparison does); a warp per row then merges the C partials.
 // ---------------------------------------------------------------------------
 struct Cand {
     float v;
@@ -252,88 +253,169 @@ __device__ __forceinline__ bool better(float va, int ia, float vb, int ib) {
 template <int K>
 __device__ __forceinline__ void topk_insert(float (&tv)[K], int (&ti)[K], float v, int i) {
     if (!better(v, i, tv[K - 1], ti[K - 1])) return;
-    int j = K - 1;
+    // the candidate sinks to its place, each displaced entry moves one down
 #pragma unroll
-    for (int q = K - 1; q > 0; --q) {
-        if (j == q && better(v, i, tv[q - 1], ti[q - 1])) {
-            tv[q] = tv[q - 1];
-            ti[q] = ti[q - 1];
-            j = q - 1;
+    for (int q = 0; q < K; ++q) {
+        if (better(v, i, tv[q], ti[q])) {
+            const float tvq = tv[q];
+            const int tiq = ti[q];
+            tv[q] = v;
+            ti[q] = i;
+            v = tvq;
+            i = tiq;
         }
     }
-    tv[j] = v;
-    ti[j] = i;
+}
+
+// (max, sum of exp relative to max) of two parts
+__device__ __forceinline__ void lse_combine(float& m, float& s, float mo, float so) {
+    const float mn = fmaxf(m, mo);
+    s = s * expf(m - mn) + so * expf(mo - mn);
+    m = mn;
+}
+
+// Warp-wide merge of the lanes' sorted K-lists into the K best (every lane
+// gets the result in rv/ri; lanes that hold nothing pass -FLT_MAX lists).
+template <int K>
+__device__ __forceinline__ void warp_merge_topk(float (&tv)[K], int (&ti)[K], float (&rv)[K], int (&ri)[K]) {
+#pragma unroll
+    for (int q = 0; q < K; ++q) {
+        float bv = tv[0];
+        int bi = ti[0];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (better(ov, oi, bv, bi)) bv = ov, bi = oi;
+        }
+        rv[q] = bv;
+        ri[q] = bi;
+        if (ti[0] == bi && tv[0] == bv) {  // the owner of the head advances (indices are unique)
+#pragma unroll
+            for (int j = 0; j < K - 1; ++j) tv[j] = tv[j + 1], ti[j] = ti[j + 1];
+            tv[K - 1] = -FLT_MAX;
+            ti[K - 1] = 0x7fffffff;
+        }
+    }
 }
 
 template <int K>
-__global__ void __launch_bounds__(256) logsoftmax_topk_kernel(const float* logits, size_t ld, int V, int rows,
-                                                               const unsigned char* active, int* out_tok,
-                                                               float* out_logp) {
-    __shared__ float sh_f[8];
-    __shared__ float cv[256 * K];
-    __shared__ int ci[256 * K];
-    const int r = blockIdx.x;
-    if (r >= rows) return;
+__device__ __forceinline__ void visit(float v, int i, float& m, float& s, float (&tv)[K], int (&ti)[K]) {
+    if (v > m) {
+        s = s * expf(m - v) + 1.f;  // m = -FLT_MAX at the start: 0 * 0 + 1
+        m = v;
+    } else {
+        s += expf(v - m);
+    }
+    topk_insert<K>(tv, ti, v, i);
+}
+
+// Partial over columns [c*chunk, (c+1)*chunk) of row r (grid: chunks x rows):
+// online max and sum of exp, K best; written to ws[r][c] = {m, s, v[K], i[K]}.
+template <int K>
+__global__ void __launch_bounds__(256) vocab_partial_kernel(const float* logits, size_t ld, int V, int chunk,
+                                                            const unsigned char* active, float* ws) {
+    __shared__ float sh_m[8], sh_s[8], sh_v[8 * K];
+    __shared__ int sh_i[8 * K];
+    const int r = blockIdx.y, c = blockIdx.x, C = gridDim.x;
     if (active && !active[r]) return;  // uniform per CTA
     const float* lg = logits + (size_t)r * ld;
+    const int lo = c * chunk, hi = min(V, lo + chunk);
+    float m = -FLT_MAX, s = 0.f;
     float tv[K];
     int ti[K];
 #pragma unroll
-    for (int q = 0; q < K; ++q) {
-        tv[q] = -FLT_MAX;
-        ti[q] = 0x7fffffff;
+    for (int q = 0; q < K; ++q) tv[q] = -FLT_MAX, ti[q] = 0x7fffffff;
+    // scalar head up to a 16-byte boundary, float4 body, scalar tail
+    const int head = min(hi - lo, (int)(((16u - (uint32_t)(reinterpret_cast<uintptr_t>(lg + lo) & 15u)) & 15u) >> 2));
+    const int b0 = lo + head, nb4 = (hi - b0) >> 2, t0 = b0 + 4 * nb4;
+    if ((int)threadIdx.x < head) visit<K>(lg[lo + threadIdx.x], lo + threadIdx.x, m, s, tv, ti);
+    const float4* body = reinterpret_cast<const float4*>(lg + b0);
+#pragma unroll 4
+    for (int j = threadIdx.x; j < nb4; j += 256) {
+        const float4 v = __ldcs(body + j);
+        const int i = b0 + 4 * j;
+        visit<K>(v.x, i, m, s, tv, ti);
+        visit<K>(v.y, i + 1, m, s, tv, ti);
+        visit<K>(v.z, i + 2, m, s, tv, ti);
+        visit<K>(v.w, i + 3, m, s, tv, ti);
     }
-    float mx = -FLT_MAX;
-    for (int i = threadIdx.x; i < V; i += 256) {
-        const float v = lg[i];
-        mx = fmaxf(mx, v);
-        topk_insert<K>(tv, ti, v, i);
-    }
+    if (t0 + (int)threadIdx.x < hi) visit<K>(lg[t0 + threadIdx.x], t0 + threadIdx.x, m, s, tv, ti);
+    // warp, then block
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if ((threadIdx.x & 31) == 0) sh_f[threadIdx.x >> 5] = mx;
+    for (int o = 16; o > 0; o >>= 1) {
+        const float mo = __shfl_xor_sync(0xffffffffu, m, o), so = __shfl_xor_sync(0xffffffffu, s, o);
+        lse_combine(m, s, mo, so);
+    }
+    float rv[K];
+    int ri[K];
+    warp_merge_topk<K>(tv, ti, rv, ri);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        sh_m[warp] = m;
+        sh_s[warp] = s;
+#pragma unroll
+        for (int q = 0; q < K; ++q) sh_v[warp * K + q] = rv[q], sh_i[warp * K + q] = ri[q];
+    }
     __syncthreads();
-    mx = sh_f[0];
+    if (warp == 0) {
+        m = lane < 8 ? sh_m[lane] : -FLT_MAX;
+        s = lane < 8 ? sh_s[lane] : 0.f;
 #pragma unroll
-    for (int w = 1; w < 8; ++w) mx = fmaxf(mx, sh_f[w]);
-    float se = 0.f;
-    for (int i = threadIdx.x; i < V; i += 256) se += expf(lg[i] - mx);
-    se = block_sum_256(se, sh_f);
-    const float ln = mx + logf(se);
-#pragma unroll
-    for (int q = 0; q < K; ++q) {
-        cv[threadIdx.x * K + q] = tv[q];
-        ci[threadIdx.x * K + q] = ti[q];
-    }
-    __syncthreads();
-    // tree merge of sorted lists: 256 -> 1
-    for (int width = 1; width < 256; width <<= 1) {
-        if ((threadIdx.x & (2 * width - 1)) == 0) {
-            const int a0 = threadIdx.x * K, b0 = (threadIdx.x + width) * K;
-            float mv[K];
-            int mi[K];
-            int ia = 0, ib = 0;
-#pragma unroll
-            for (int q = 0; q < K; ++q) {
-                const bool take_a =
-                    ib >= K || (ia < K && better(cv[a0 + ia], ci[a0 + ia], cv[b0 + ib], ci[b0 + ib]));
-                mv[q] = take_a ? cv[a0 + ia] : cv[b0 + ib];
-                mi[q] = take_a ? ci[a0 + ia] : ci[b0 + ib];
-                ia += take_a;
-                ib += !take_a;
-            }
-#pragma unroll
-            for (int q = 0; q < K; ++q) {
-                cv[a0 + q] = mv[q];
-                ci[a0 + q] = mi[q];
-            }
+        for (int o = 4; o > 0; o >>= 1) {
+            const float mo = __shfl_xor_sync(0xffffffffu, m, o), so = __shfl_xor_sync(0xffffffffu, s, o);
+            lse_combine(m, s, mo, so);
         }
-        __syncthreads();
+#pragma unroll
+        for (int q = 0; q < K; ++q) {
+            tv[q] = lane < 8 ? sh_v[lane * K + q] : -FLT_MAX;
+            ti[q] = lane < 8 ? sh_i[lane * K + q] : 0x7fffffff;
+        }
+        warp_merge_topk<K>(tv, ti, rv, ri);
+        float* out = ws + ((size_t)r * C + c) * (2 + 2 * K);
+        if (lane == 0) out[0] = m, out[1] = s;
+#pragma unroll
+        for (int q = 0; q < K; ++q)
+            if (lane == q) out[2 + q] = rv[q], out[2 + K + q] = __int_as_float(ri[q]);
     }
-    if (threadIdx.x < K) {
-        out_tok[(size_t)r * K + threadIdx.x] = ci[threadIdx.x];
-        out_logp[(size_t)r * K + threadIdx.x] = cv[threadIdx.x] - ln;
+}
+
+// One warp per row: combine the C partials, write the K best as
+// (token, log-probability = logit - (max + log(sum of exp))).
+template <int K>
+__global__ void __launch_bounds__(256) vocab_merge_kernel(const float* ws, int C, int rows,
+                                                          const unsigned char* active, int* out_tok,
+                                                          float* out_logp) {
+    const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (r >= rows || (active && !active[r])) return;  // uniform per warp
+    const float* p = ws + (size_t)r * C * (2 + 2 * K);
+    float m = -FLT_MAX, s = 0.f;
+    float tv[K];
+    int ti[K];
+#pragma unroll
+    for (int q = 0; q < K; ++q) tv[q] = -FLT_MAX, ti[q] = 0x7fffffff;
+    if (lane < C) {
+        const float* e = p + (size_t)lane * (2 + 2 * K);
+        m = e[0];
+        s = e[1];
+#pragma unroll
+        for (int q = 0; q < K; ++q) tv[q] = e[2 + q], ti[q] = __float_as_int(e[2 + K + q]);
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float mo = __shfl_xor_sync(0xffffffffu, m, o), so = __shfl_xor_sync(0xffffffffu, s, o);
+        lse_combine(m, s, mo, so);
+    }
+    float rv[K];
+    int ri[K];
+    warp_merge_topk<K>(tv, ti, rv, ri);
+    const float ln = m + logf(s);
+#pragma unroll
+    for (int q = 0; q < K; ++q)
+        if (lane == q) {
+            out_tok[(size_t)r * K + q] = ri[q];
+            out_logp[(size_t)r * K + q] = rv[q] - ln;
+        }
 }
 
 // ---------------------------------------------------------------------------
@@ -410,12 +492,32 @@ cudaError_t launch_penalties(float* logits, size_t ld, const int* hist, int hist
     return cudaGetLastError();
 }
 
+int vocab_topk_chunks(int V, int rows) {
+    int C = (148 * 8 + rows - 1) / rows;  // about 8 CTAs per SM
+    C = C < 1 ? 1 : (C > 32 ? 32 : C);
+    while (C > 1 && V / C < 4096) --C;
+    return C;
+}
+
+size_t vocab_topk_ws_floats(int V, int rows, int k) {
+    return (size_t)rows * vocab_topk_chunks(V, rows) * (2 + 2 * (size_t)k);
+}
+
 cudaError_t launch_logsoftmax_topk(const float* logits, size_t ld, int V, int rows, const unsigned char* active,
-                                   int k, int* out_tok, float* out_logp, cudaStream_t st) {
+                                   int k, int* out_tok, float* out_logp, float* ws, cudaStream_t st) {
     if (rows <= 0) return cudaSuccess;
-    if (k == 8) logsoftmax_topk_kernel<8><<<rows, 256, 0, st>>>(logits, ld, V, rows, active, out_tok, out_logp);
-    else if (k == 4) logsoftmax_topk_kernel<4><<<rows, 256, 0, st>>>(logits, ld, V, rows, active, out_tok, out_logp);
-    else return cudaErrorInvalidValue;
+    const int C = vocab_topk_chunks(V, rows);
+    const int chunk = (((V + C - 1) / C) + 3) & ~3;
+    const dim3 g1(C, rows), g2((rows + 7) / 8);
+    if (k == 8) {
+        vocab_partial_kernel<8><<<g1, 256, 0, st>>>(logits, ld, V, chunk, active, ws);
+        vocab_merge_kernel<8><<<g2, 256, 0, st>>>(ws, C, rows, active, out_tok, out_logp);
+    } else if (k == 4) {
+        vocab_partial_kernel<4><<<g1, 256, 0, st>>>(logits, ld, V, chunk, active, ws);
+        vocab_merge_kernel<4><<<g2, 256, 0, st>>>(ws, C, rows, active, out_tok, out_logp);
+    } else {
+        return cudaErrorInvalidValue;
+    }
     return cudaGetLastError();
 }
 

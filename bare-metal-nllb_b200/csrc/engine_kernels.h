@@ -59,8 +59,10 @@ cudaError_t launch_linear_tma(const LinearArgs& a, const CUtensorMap* tx, const 
                               cudaStream_t st);
 cudaError_t launch_penalties(float* logits, size_t ld, const int* hist, int hist_ld, const int* n_tokens,
                              const unsigned char* active, int rows, float penalty, int ngram, cudaStream_t st);
+// ws: vocab_topk_ws_floats(V, rows, k) floats of scratch
+size_t vocab_topk_ws_floats(int V, int rows, int k);
 cudaError_t launch_logsoftmax_topk(const float* logits, size_t ld, int V, int rows, const unsigned char* active,
-                                   int k, int* out_tok, float* out_logp, cudaStream_t st);
+                                   int k, int* out_tok, float* out_logp, float* ws, cudaStream_t st);
 cudaError_t launch_set_memory_batched(float* km, float* vm, int* n_src_slots, int max_src, int H, const float* k,
                                       const float* v, long long sent_stride, const int* n_src, int n_sent,
                                       int max_n, cudaStream_t st);

@@ -194,14 +194,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (S == 1) {
                 acc = *reinterpret_cast<const float4*>(src);
             } else {
-                acc = ld_cluster_f4(map_rank(src, 0));
-                for (int r = 1; r < S; ++r) {
-                    const float4 p = ld_cluster_f4(map_rank(src, r));
-                    acc.x += p.x;
-                    acc.y += p.y;
-                    acc.z += p.z;
-                    acc.w += p.w;
-                }
+                float4 p[8];  // all remote loads in flight before the first add
+#pragma unroll
+                for (int r = 0; r < 8; ++r)
+                    if (r < S) p[r] = ld_cluster_f4(map_rank(src, r));
+                acc = p[0];
+#pragma unroll
+                for (int r = 1; r < 8; ++r)
+                    if (r < S) acc.x += p[r].x, acc.y += p[r].y, acc.z += p[r].z, acc.w += p[r].w;
             }
             const int nl = c4 * 4, n = n0 + nl;
             float y[4] = {acc.x * s_inv[nl], acc.y * s_inv[nl + 1], acc.z * s_inv[nl + 2], acc.w * s_inv[nl + 3]};
