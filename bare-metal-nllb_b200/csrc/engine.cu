@@ -33,6 +33,7 @@ int set_error(int status, const std::string& msg);  // nllb_attn.cu
 namespace {
 
 constexpr int D = 1024, H = 16, FFN = 4096, LAYERS = 12, VOCAB = 256206, NB = 4;
+constexpr int VOCAB_LD = (VOCAB + 3) & ~3;  // row stride of the logits: rows start 16-byte aligned
 constexpr int LANG_START = 256000;
 
 #define ENG_CK(call)                                                                              \
@@ -192,6 +193,7 @@ struct Lin {
     int out = 0, in = 0;
     void* wb = nullptr;  // bf16 copy of w (exact), operand of the TMA-fed tensor-core kernel
     CUtensorMap tm{};    // tensor map of wb: [out][in], box 64 x 128, 128-byte swizzle
+    CUtensorMap tm256{}; // the same, box 32 x 256, 64-byte swizzle (persistent kernel)
 };
 
 }  // namespace
@@ -222,7 +224,8 @@ struct nllb_model {
     // grow-only, with its tensor maps per (M, K)
     void* planes = nullptr;
     size_t planes_elems = 0;
-    std::map<std::pair<int, int>, CUtensorMap> plane_maps;
+    std::map<std::pair<int, int>, CUtensorMap> plane_maps;  // key (M, K): split-K kernel
+    std::map<std::pair<int, int>, CUtensorMap> plane_maps_pers;  // key (M, K): persistent kernel
     int num_sms = 148;
     // decision margins of the last translate call, [sentence][step]
     std::vector<std::vector<float>> margins;
@@ -278,6 +281,7 @@ struct Loader {
         ENG_RC(dev_alloc(m, &wb, (size_t)L->out * L->in));
         ENG_CK(launch_int8_to_bf16(L->w, wb, (size_t)L->out * L->in, m->stream));
         ENG_CK(encode_bf16_map(&L->tm, wb, L->in, L->out, 1));
+        ENG_CK(encode_bf16_maps_persistent(nullptr, nullptr, L->in, 0, &L->tm256, wb, L->out));
         L->wb = wb;
         return NLLB_ATTN_OK;
     }
@@ -455,6 +459,16 @@ int run_linear(nllb_model* m, const Lin& L, const float* x, int M, float* out, c
     if (M > 16 && L.wb && (size_t)M * L.in * 3 <= m->planes_elems) {
         // x -> three bf16 planes, then the TMA-fed tensor-core GEMM
         ENG_CK(launch_split3(x, L.in, M, L.in, m->planes, m->stream));
+        if (linear_tma_use_persistent(M, L.out, m->num_sms)) {
+            auto ip = m->plane_maps_pers.find({M, L.in});
+            if (ip == m->plane_maps_pers.end()) {
+                CUtensorMap tx;
+                ENG_CK(encode_bf16_maps_persistent(&tx, m->planes, L.in, M, nullptr, nullptr, 0));
+                ip = m->plane_maps_pers.emplace(std::make_pair(M, L.in), tx).first;
+            }
+            ENG_CK(launch_linear_tma_persistent(a, &ip->second, &L.tm256, m->num_sms, m->attn->err, m->stream));
+            return NLLB_ATTN_OK;
+        }
         auto it = m->plane_maps.find({M, L.in});
         if (it == m->plane_maps.end()) {
             CUtensorMap tx;
@@ -477,6 +491,7 @@ int ensure_planes(nllb_model* m, size_t elems) {
     m->planes = nullptr;
     m->planes_elems = 0;
     m->plane_maps.clear();
+    m->plane_maps_pers.clear();
     ENG_CK(cudaMalloc(&m->planes, elems * sizeof(__nv_bfloat16)));
     m->planes_elems = elems;
     return NLLB_ATTN_OK;
@@ -576,11 +591,11 @@ int decode_step(nllb_model* m, Work& w, int step) {
 // Tied vocabulary projection with language rows masked (decoder.c:319-354),
 // penalties (main.c:186-213) and log-softmax + top-k (main.c:154-182).
 int vocab_topk(nllb_model* m, Work& w, int k, bool penalties, const nllb_translate_opts& o) {
-    ENG_RC(run_linear(m, m->vocab, w.h, w.rows, w.logits, nullptr, 0, VOCAB, LANG_START));
+    ENG_RC(run_linear(m, m->vocab, w.h, w.rows, w.logits, nullptr, 0, VOCAB_LD, LANG_START));
     if (penalties)
-        ENG_CK(launch_penalties(w.logits, VOCAB, w.hist, m->max_gen, w.ntok, w.active, w.rows,
+        ENG_CK(launch_penalties(w.logits, VOCAB_LD, w.hist, m->max_gen, w.ntok, w.active, w.rows,
                                 o.repetition_penalty, o.no_repeat_ngram, m->stream));
-    ENG_CK(launch_logsoftmax_topk(w.logits, VOCAB, VOCAB, w.rows, w.active, k, w.top_tok, w.top_lp, w.topk_ws,
+    ENG_CK(launch_logsoftmax_topk(w.logits, VOCAB_LD, VOCAB, w.rows, w.active, k, w.top_tok, w.top_lp, w.topk_ws,
                                   m->stream));
     return NLLB_ATTN_OK;
 }
@@ -641,7 +656,7 @@ extern "C" int nllb_translate(nllb_model* m, int n_sent, const int* src_tokens, 
     ENG_RC(w.alloc(&w.qx, R * D));
     ENG_RC(w.alloc(&w.attn, R * D));
     ENG_RC(w.alloc(&w.ffn, R * FFN));
-    ENG_RC(w.alloc(&w.logits, R * VOCAB));
+    ENG_RC(w.alloc(&w.logits, R * VOCAB_LD));
     ENG_RC(w.alloc(&w.tok, R));
     ENG_RC(w.alloc(&w.hist, R * m->max_gen));
     ENG_RC(w.alloc(&w.ntok, R));

@@ -28,11 +28,12 @@ struct nllb_linear {
     int N = 0, K = 0;
     int num_sms = 148;
     void* wb = nullptr;       // [N][K] bf16
-    CUtensorMap tm{};         // of wb
+    CUtensorMap tm{};         // of wb, box 64 x 128 (split-K kernel)
+    CUtensorMap tm256{};      // of wb, box 32 x 256 (persistent kernel)
     void* planes = nullptr;   // [3][M][K] bf16, grow-only
     size_t planes_elems = 0;
-    int map_rows = -1;        // rows the plane map `tx` was encoded for
-    CUtensorMap tx{};
+    int map_rows = -1;        // rows the plane maps were encoded for
+    CUtensorMap tx{}, tx_pers{};
     int* err = nullptr;       // bounded-wait error word
 };
 
@@ -90,7 +91,8 @@ int nllb_linear_prepare(const int8_t* w, const float* weight_scale, const float*
         return fail(nllb::set_error(NLLB_ATTN_ECUDA, "cannot allocate the bf16 weight copy"));
     if (launch_int8_to_bf16(w, L->wb, (size_t)N * K, st) != cudaSuccess)
         return fail(nllb::set_error(NLLB_ATTN_ECUDA, "weight conversion launch failed"));
-    if (encode_bf16_map(&L->tm, L->wb, K, N, 1) != cudaSuccess)
+    if (encode_bf16_map(&L->tm, L->wb, K, N, 1) != cudaSuccess ||
+        encode_bf16_maps_persistent(nullptr, nullptr, K, 0, &L->tm256, L->wb, N) != cudaSuccess)
         return fail(nllb::set_error(NLLB_ATTN_ECUDA, "cuTensorMapEncodeTiled failed for the weight"));
     *out = L;
     return NLLB_ATTN_OK;
@@ -136,10 +138,14 @@ int nllb_linear_run(nllb_linear* L, const float* x, int M, float* out, const flo
     }
     if (L->map_rows != M) {
         LP_CK(encode_bf16_map(&L->tx, L->planes, L->K, M, 3));
+        LP_CK(encode_bf16_maps_persistent(&L->tx_pers, L->planes, L->K, M, nullptr, nullptr, 0));
         L->map_rows = M;
     }
     LP_CK(launch_split3(x, L->K, M, L->K, L->planes, st));
-    LP_CK(launch_linear_tma(a, &L->tx, &L->tm, linear_tma_splits(M, L->N, L->K, L->num_sms), L->err, st));
+    if (linear_tma_use_persistent(M, L->N, L->num_sms))
+        LP_CK(launch_linear_tma_persistent(a, &L->tx_pers, &L->tm256, L->num_sms, L->err, st));
+    else
+        LP_CK(launch_linear_tma(a, &L->tx, &L->tm, linear_tma_splits(M, L->N, L->K, L->num_sms), L->err, st));
     return NLLB_ATTN_OK;
 }
 

@@ -185,47 +185,74 @@ __global__ void __launch_bounds__(THREADS, 1)
         const bool vec = (a.cblock % 4 == 0) && ((reinterpret_cast<uintptr_t>(a.out) & 15) == 0) &&
                          ((reinterpret_cast<uintptr_t>(a.residual) & 15) == 0) &&
                          ((reinterpret_cast<uintptr_t>(a.bias) & 15) == 0);
-        for (int item = tid; item < R * (TN / 4); item += THREADS) {
-            const int rr = z * R + item / (TN / 4), c4 = item % (TN / 4);
-            const int m = m0 + rr;
-            if (m >= a.M) break;  // rows grow with item
-            const float* src = part + rr * PART_STRIDE + c4 * 4;
-            float4 acc;
-            if (S == 1) {
-                acc = *reinterpret_cast<const float4*>(src);
-            } else {
-                float4 p[8];  // all remote loads in flight before the first add
+        if (vec) {
+            // a warp stores one 128-column row as float4s
+            for (int item = tid; item < R * (TN / 4); item += THREADS) {
+                const int rr = z * R + item / (TN / 4), c4 = item % (TN / 4);
+                const int m = m0 + rr;
+                if (m >= a.M) break;  // rows grow with item
+                const float* src = part + rr * PART_STRIDE + c4 * 4;
+                float4 acc;
+                if (S == 1) {
+                    acc = *reinterpret_cast<const float4*>(src);
+                } else {
+                    float4 p[8];  // all remote loads in flight before the first add
 #pragma unroll
-                for (int r = 0; r < 8; ++r)
-                    if (r < S) p[r] = ld_cluster_f4(map_rank(src, r));
-                acc = p[0];
+                    for (int r = 0; r < 8; ++r)
+                        if (r < S) p[r] = ld_cluster_f4(map_rank(src, r));
+                    acc = p[0];
 #pragma unroll
-                for (int r = 1; r < 8; ++r)
-                    if (r < S) acc.x += p[r].x, acc.y += p[r].y, acc.z += p[r].z, acc.w += p[r].w;
+                    for (int r = 1; r < 8; ++r)
+                        if (r < S) acc.x += p[r].x, acc.y += p[r].y, acc.z += p[r].z, acc.w += p[r].w;
+                }
+                const int nl = c4 * 4, n = n0 + nl;
+                float y[4] = {acc.x * s_inv[nl], acc.y * s_inv[nl + 1], acc.z * s_inv[nl + 2],
+                              acc.w * s_inv[nl + 3]};
+                if (n + 3 < a.N) {
+                    if (a.bias) {
+                        const float4 b = *reinterpret_cast<const float4*>(a.bias + n);
+                        y[0] += b.x, y[1] += b.y, y[2] += b.z, y[3] += b.w;
+                    }
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        if (a.relu) y[j] = fmaxf(y[j], 0.f);
+                        if (a.mask_from >= 0 && n + j >= a.mask_from) y[j] = -1e30f;
+                    }
+                    const size_t o =
+                        (size_t)(n / a.cblock) * ((size_t)a.M * a.cblock) + (size_t)m * a.cblock + (n % a.cblock);
+                    if (a.residual) {
+                        const float4 r = *reinterpret_cast<const float4*>(a.residual + o);
+                        y[0] += r.x, y[1] += r.y, y[2] += r.z, y[3] += r.w;
+                    }
+                    *reinterpret_cast<float4*>(a.out + o) = make_float4(y[0], y[1], y[2], y[3]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        if (n + j < a.N) epilogue_store(a, m, n + j, y[j]);
+                }
             }
-            const int nl = c4 * 4, n = n0 + nl;
-            float y[4] = {acc.x * s_inv[nl], acc.y * s_inv[nl + 1], acc.z * s_inv[nl + 2], acc.w * s_inv[nl + 3]};
-            if (vec && n + 3 < a.N) {
-                if (a.bias) {
-                    const float4 b = *reinterpret_cast<const float4*>(a.bias + n);
-                    y[0] += b.x, y[1] += b.y, y[2] += b.z, y[3] += b.w;
-                }
+        } else {
+            // a warp stores 32 consecutive columns of one row per instruction
+            for (int item = tid; item < R * TN; item += THREADS) {
+                const int rr = z * R + item / TN, nl = item % TN;
+                const int m = m0 + rr, n = n0 + nl;
+                if (m >= a.M) break;
+                if (n >= a.N) continue;
+                const float* src = part + rr * PART_STRIDE + nl;
+                float acc;
+                if (S == 1) {
+                    acc = *src;
+                } else {
+                    float p[8];
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    if (a.relu) y[j] = fmaxf(y[j], 0.f);
-                    if (a.mask_from >= 0 && n + j >= a.mask_from) y[j] = -1e30f;
-                }
-                const size_t o =
-                    (size_t)(n / a.cblock) * ((size_t)a.M * a.cblock) + (size_t)m * a.cblock + (n % a.cblock);
-                if (a.residual) {
-                    const float4 r = *reinterpret_cast<const float4*>(a.residual + o);
-                    y[0] += r.x, y[1] += r.y, y[2] += r.z, y[3] += r.w;
-                }
-                *reinterpret_cast<float4*>(a.out + o) = make_float4(y[0], y[1], y[2], y[3]);
-            } else {
+                    for (int r = 0; r < 8; ++r)
+                        if (r < S) p[r] = ld_cluster_f32(map_rank(src, r));
+                    acc = p[0];
 #pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    if (n + j < a.N) epilogue_store(a, m, n + j, y[j]);
+                    for (int r = 1; r < 8; ++r)
+                        if (r < S) acc += p[r];
+                }
+                epilogue_store(a, m, n, acc * s_inv[nl]);
             }
         }
     }
@@ -236,6 +263,195 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc_fence_after();
         tmem_dealloc(tmem, TMEM_COLS);
     }
+}
+
+// ---------------------------------------------------------------------------
+// Persistent form for outputs with at least one 128 x 256 tile per SM: one CTA
+// per SM walks tiles t = blockIdx.x, + gridDim.x, ... (row tile fastest, so
+// CTAs running at the same time share a weight tile in L2).  Warp 0 lane 0
+// streams 32-wide K chunks (3 planes 8 KB + weight 16 KB, 64-byte swizzle)
+// through a 4-stage ring, warp 1 lane 0 issues 128 x 256 x 16 MMAs into one
+// of two TMEM accumulators (2 x 256 columns), and warps 2-9 drain the other
+// accumulator meanwhile: TMEM -> registers -> a per-warp transpose buffer ->
+// stores of 32 consecutive columns per row.
+// ---------------------------------------------------------------------------
+namespace pers {
+constexpr int TM = 128, TN = 256, TK = 32, STAGES = 4;
+constexpr int EPI_WARPS = 8, THREADS = (EPI_WARPS + 2) * 32;
+constexpr uint32_t A_PLANE = TM * TK * 2;                // 8 KB
+constexpr uint32_t B_BYTES = TN * TK * 2;                // 16 KB
+constexpr uint32_t STAGE_BYTES = 3 * A_PLANE + B_BYTES;  // 40 KB
+constexpr int BUF_LD = 33;                               // transpose buffer row stride (floats)
+constexpr uint32_t SMEM_EPI = STAGES * STAGE_BYTES;
+constexpr uint32_t SMEM_BAR = SMEM_EPI + EPI_WARPS * 32 * BUF_LD * 4;
+constexpr uint32_t SMEM_TOTAL = SMEM_BAR + 256 + 1024;
+constexpr uint32_t TMEM_COLS = 512;
+}  // namespace pers
+
+// K-major operand in the 64-byte swizzled layout: rows of 64 B (32 bf16),
+// 8-row atoms 512 B apart (stride byte offset), descriptor version 1.
+__device__ __forceinline__ uint64_t umma_desc_k_sw64(uint32_t smem_addr) {
+    return (uint64_t)((smem_addr >> 4) & 0x3FFFu) | ((uint64_t)1u << 16) | ((uint64_t)(512u >> 4) << 32) |
+           ((uint64_t)1u << 46) | ((uint64_t)4u << 61);
+}
+
+// Bounded wait whose outcome every lane of the warp shares (the tcgen05 loads
+// that follow are warp-collective).
+__device__ __forceinline__ bool warp_wait_bounded(uint64_t* bar, uint32_t parity) {
+    const bool ok = mbar_wait_bounded(bar, parity);
+    return __all_sync(0xffffffffu, ok);
+}
+
+__global__ void __launch_bounds__(pers::THREADS, 1)
+    linear_tma_persistent_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw,
+                                 const LinearArgs a, int* err) {
+    constexpr int TM = pers::TM, TN = pers::TN, TK = pers::TK, STAGES = pers::STAGES, EPI_WARPS = pers::EPI_WARPS;
+    constexpr int BUF_LD = pers::BUF_LD;
+    constexpr uint32_t A_PLANE = pers::A_PLANE, STAGE_BYTES = pers::STAGE_BYTES, SMEM_EPI = pers::SMEM_EPI;
+    constexpr uint32_t SMEM_BAR = pers::SMEM_BAR, TMEM_COLS = pers::TMEM_COLS;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base_addr = (raw + 1023u) & ~1023u;
+    unsigned char* base = smem_raw + (base_addr - raw);
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + SMEM_BAR);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int MT = (a.M + TM - 1) / TM, NT = (a.N + TN - 1) / TN;
+    const int tiles = MT * NT, nk = a.K / TK;
+
+    if (warp == 0) tmem_alloc(tmem_slot, TMEM_COLS);
+    if (tid == 32) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], EPI_WARPS);
+        }
+        *s_abort = 0;
+        fence_barrier_init();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {  // ---- TMA producer
+            uint32_t g = 0;
+            for (int t = blockIdx.x; t < tiles && !*s_abort; t += gridDim.x) {
+                const int m0 = (t % MT) * TM, n0 = (t / MT) * TN;
+                for (int c = 0; c < nk; ++c, ++g) {
+                    const uint32_t s = g % STAGES, use = g / STAGES;
+                    if (!mbar_wait_bounded(&empty[s], (use & 1u) ^ 1u)) {
+                        *s_abort = 1;
+                        break;
+                    }
+                    unsigned char* st = base + s * STAGE_BYTES;
+                    mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+                    tma_load_3d(st, &tx, c * TK, m0, 0, &full[s]);  // box 32 x 128 x 3: the three planes
+                    tma_load_2d(st + 3 * A_PLANE, &tw, c * TK, n0, &full[s]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {  // ---- MMA issuer
+            constexpr uint32_t idesc = idesc_bf16(TM, TN);
+            uint32_t g = 0, i = 0;
+            for (int t = blockIdx.x; t < tiles && !*s_abort; t += gridDim.x, ++i) {
+                const uint32_t acc = i & 1u;
+                if (!mbar_wait_bounded(&tempty[acc], ((i >> 1) & 1u) ^ 1u)) {
+                    *s_abort = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem + acc * TN;
+                bool ok = true;
+                for (int c = 0; c < nk; ++c, ++g) {
+                    const uint32_t s = g % STAGES, use = g / STAGES;
+                    if (!mbar_wait_bounded(&full[s], use & 1u)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = base_addr + s * STAGE_BYTES;
+#pragma unroll
+                    for (int ks = 0; ks < TK / 16; ++ks) {
+                        const uint64_t bw = umma_desc_k_sw64(sa + 3 * A_PLANE + ks * 32);
+                        mma_bf16(d, umma_desc_k_sw64(sa + 0 * A_PLANE + ks * 32), bw, idesc, (c > 0 || ks > 0) ? 1u : 0u);
+                        mma_bf16(d, umma_desc_k_sw64(sa + 1 * A_PLANE + ks * 32), bw, idesc, 1u);
+                        mma_bf16(d, umma_desc_k_sw64(sa + 2 * A_PLANE + ks * 32), bw, idesc, 1u);
+                    }
+                    tc_commit(&empty[s]);
+                }
+                if (!ok) {
+                    *s_abort = 1;
+                    break;
+                }
+                tc_commit(&tfull[acc]);
+            }
+        }
+    } else {  // ---- epilogue warps 2-9: lane quarter warp % 4, column half (warp - 2) / 4
+        const int quarter = warp & 3, half = (warp - 2) >> 2;
+        float* buf = reinterpret_cast<float*>(base + SMEM_EPI) + (warp - 2) * 32 * BUF_LD;
+        uint32_t i = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+            const uint32_t acc = i & 1u;
+            const bool go = __all_sync(0xffffffffu, *s_abort == 0);  // warp-uniform
+            if (!go || !warp_wait_bounded(&tfull[acc], (i >> 1) & 1u)) {
+                *s_abort = 1;
+                break;
+            }
+            tc_fence_after();
+            const int mrow = (t % MT) * TM + quarter * 32, n0 = (t / MT) * TN;
+#pragma unroll 1
+            for (int ch = 0; ch < 4; ++ch) {
+                const int col0 = half * 128 + ch * 32;
+                float v[32];
+                tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + acc * TN + (uint32_t)col0, v);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) buf[lane * BUF_LD + j] = v[j];
+                __syncwarp();
+                // lane = column: per-column factors once, then one row per store
+                const int n = n0 + col0 + lane;
+                const bool nok = n < a.N;
+                const float inv = nok ? 1.0f / a.scale[n] : 0.f;  // 1/scale as tensor.c:75
+                const float bias = (nok && a.bias) ? a.bias[n] : 0.f;
+                const bool masked = a.mask_from >= 0 && n >= a.mask_from;
+                const size_t colbase =
+                    nok ? (size_t)(n / a.cblock) * ((size_t)a.M * a.cblock) + (size_t)(n % a.cblock) : 0;
+                const int rows = min(32, a.M - mrow);
+                if (nok) {
+                    for (int r = 0; r < rows; ++r) {
+                        float y = buf[r * BUF_LD + lane] * inv;
+                        if (a.bias) y += bias;
+                        if (a.relu) y = fmaxf(y, 0.f);
+                        if (masked) y = -1e30f;
+                        const size_t o = colbase + (size_t)(mrow + r) * a.cblock;
+                        if (a.residual) y += a.residual[o];
+                        a.out[o] = y;
+                    }
+                }
+                __syncwarp();
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, TMEM_COLS);
+    }
+    if (tid == 0 && *s_abort) atomicOr(err, NLLB_DEV_ERR_TIMEOUT);
 }
 
 // x [M][ldx] fp32 -> planes [3][M][K] bf16 with x = p0 + p1 + p2 (to 24 bits)
@@ -273,12 +489,17 @@ std::once_flag g_encode_once;
 cudaError_t configure_linear_tma() {
     cudaError_t e = cudaFuncSetAttribute(linear_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_TOTAL);
     if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(linear_tma_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)pers::SMEM_TOTAL);
+    if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(linear_tma_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
 }
 
 // Tensor map of a row-major bf16 matrix stack: `planes` matrices of
-// [rows][cols] (K-major), box 64 columns x 128 rows, 128-byte swizzle.
-cudaError_t encode_bf16_map(CUtensorMap* map, const void* base, int cols, int rows, int planes) {
+// [rows][cols] (K-major), box box_cols x box_rows (x planes), with the
+// 128-byte swizzle (box_cols 64) or the 64-byte swizzle (box_cols 32).
+cudaError_t encode_bf16_map_box(CUtensorMap* map, const void* base, int cols, int rows, int planes, int box_cols,
+                                int box_rows) {
     std::call_once(g_encode_once, [] {
         cudaDriverEntryPointQueryResult q;
         void* fn = nullptr;
@@ -287,14 +508,42 @@ cudaError_t encode_bf16_map(CUtensorMap* map, const void* base, int cols, int ro
             g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     });
     if (!g_encode) return cudaErrorNotSupported;
+    if (box_cols != 64 && box_cols != 32) return cudaErrorInvalidValue;
     const cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)planes};
     const cuuint64_t strides[2] = {(cuuint64_t)cols * 2, (cuuint64_t)cols * rows * 2};
-    const cuuint32_t box[3] = {(cuuint32_t)TK, (cuuint32_t)TM, (cuuint32_t)planes};
+    const cuuint32_t box[3] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows, (cuuint32_t)planes};
     const cuuint32_t estr[3] = {1, 1, 1};
-    const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, planes > 1 ? 3 : 2, const_cast<void*>(base),
-                                dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    const CUresult r =
+        g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, planes > 1 ? 3 : 2, const_cast<void*>(base), dims, strides,
+                 box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                 box_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+cudaError_t encode_bf16_map(CUtensorMap* map, const void* base, int cols, int rows, int planes) {
+    return encode_bf16_map_box(map, base, cols, rows, planes, TK, TM);
+}
+
+cudaError_t encode_bf16_maps_persistent(CUtensorMap* x_map, const void* planes, int K, int M, CUtensorMap* w_map,
+                                        const void* wb, int N) {
+    cudaError_t e = cudaSuccess;
+    if (x_map) e = encode_bf16_map_box(x_map, planes, K, M, 3, pers::TK, pers::TM);
+    if (e == cudaSuccess && w_map) e = encode_bf16_map_box(w_map, wb, K, N, 1, pers::TK, pers::TN);
+    return e;
+}
+
+bool linear_tma_use_persistent(int M, int N, int num_sms) {
+    return (long long)((M + pers::TM - 1) / pers::TM) * ((N + pers::TN - 1) / pers::TN) >= num_sms;
+}
+
+cudaError_t launch_linear_tma_persistent(const LinearArgs& a, const CUtensorMap* tx, const CUtensorMap* tw,
+                                         int num_sms, int* err, cudaStream_t st) {
+    const int tiles = ((a.M + pers::TM - 1) / pers::TM) * ((a.N + pers::TN - 1) / pers::TN);
+    const int grid = tiles < num_sms ? tiles : num_sms;
+    if (grid < 1) return cudaSuccess;
+    linear_tma_persistent_kernel<<<grid, pers::THREADS, pers::SMEM_TOTAL, st>>>(*tx, *tw, a, err);
+    return cudaGetLastError();
 }
 
 int linear_tma_splits(int M, int N, int K, int num_sms) {

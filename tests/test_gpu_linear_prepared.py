@@ -6,9 +6,11 @@ Checked against a float64 evaluation of mat_vec_int8's arithmetic
 (tensor.c:144-196): out[m][n] = sum_k x[m][k] * (w[n][k] * (1/scale[n])) + bias[n],
 then relu and the residual.  Tolerance: fp32 accumulation error relative to
 the sum of |terms|, as for nllb_linear_int8.  The shapes reach every split-K
-depth of the cluster reduction (1, 2, 4, 8 CTAs per tile), row counts that
-are not multiples of the 128-row tile, output counts that are not multiples
-of 128 or of 4 (the scalar store path), and the full vocabulary projection.
+depth of the cluster reduction (1, 2, 4, 8 CTAs per tile), the persistent
+128 x 256-tile kernel (outputs with at least one such tile per SM), row
+counts that are not multiples of the 128-row tile, output counts that are
+not multiples of the tile or of 4 (the scalar store path), and the full
+vocabulary projection.
 """
 import numpy as np
 import pytest
@@ -56,7 +58,9 @@ def _dev(a, device):
     (1024, 1024, 4096, "bias_relu"),   # 2-way split
     (2048, 1024, 1024, "plain"),       # 4-way split
     (4100, 1024, 4096, "bias_relu"),   # no split, M tail
-    (40, 1024, 256206, "plain"),       # vocabulary projection shape
+    (40, 1024, 256206, "plain"),       # vocabulary projection shape (persistent kernel, N tail)
+    (2000, 1024, 3001, "residual"),    # persistent kernel, M and N tails, N % 4 != 0
+    (1100, 4096, 2048, "bias_relu"),   # persistent kernel, K = 4096
 ])
 def test_prepared_linear_matches_reference(cuda_device, M, K, N, epilogue):
     import torch
