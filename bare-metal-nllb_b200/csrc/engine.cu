@@ -459,7 +459,7 @@ int run_linear(nllb_model* m, const Lin& L, const float* x, int M, float* out, c
     if (M > 16 && L.wb && (size_t)M * L.in * 3 <= m->planes_elems) {
         // x -> three bf16 planes, then the TMA-fed tensor-core GEMM
         ENG_CK(launch_split3(x, L.in, M, L.in, m->planes, m->stream));
-        if (linear_tma_use_persistent(M, L.out, m->num_sms)) {
+        if (linear_tma_use_persistent(M, L.out, L.in, m->num_sms)) {
             auto ip = m->plane_maps_pers.find({M, L.in});
             if (ip == m->plane_maps_pers.end()) {
                 CUtensorMap tx;

@@ -53,10 +53,10 @@ cudaError_t launch_linear_tc(const LinearArgs& a, int splits, float* ws, int* ti
 cudaError_t configure_linear_tma();
 cudaError_t encode_bf16_map(CUtensorMap* map, const void* base, int cols, int rows, int planes);
 int linear_tma_splits(int M, int N, int K, int num_sms);
-// Persistent 128 x 256-tile form (K % 32 == 0), used when the output has at
-// least one such tile per SM; its tensor maps: planes box 32 x 128 x 3,
+// Persistent 128 x 256-tile form (K % 32 == 0), used when the output has
+// enough tiles for its K (linear_tma_use_persistent); its tensor maps: planes box 32 x 128 x 3,
 // weight box 32 x 256 (64-byte swizzle).  Either map pointer may be null.
-bool linear_tma_use_persistent(int M, int N, int num_sms);
+bool linear_tma_use_persistent(int M, int N, int K, int num_sms);
 cudaError_t encode_bf16_maps_persistent(CUtensorMap* x_map, const void* planes, int K, int M, CUtensorMap* w_map,
                                         const void* wb, int N);
 cudaError_t launch_linear_tma_persistent(const LinearArgs& a, const CUtensorMap* tx, const CUtensorMap* tw,

@@ -142,7 +142,7 @@ int nllb_linear_run(nllb_linear* L, const float* x, int M, float* out, const flo
         L->map_rows = M;
     }
     LP_CK(launch_split3(x, L->K, M, L->K, L->planes, st));
-    if (linear_tma_use_persistent(M, L->N, L->num_sms))
+    if (linear_tma_use_persistent(M, L->N, L->K, L->num_sms))
         LP_CK(launch_linear_tma_persistent(a, &L->tx_pers, &L->tm256, L->num_sms, L->err, st));
     else
         LP_CK(launch_linear_tma(a, &L->tx, &L->tm, linear_tma_splits(M, L->N, L->K, L->num_sms), L->err, st));

@@ -533,8 +533,13 @@ cudaError_t encode_bf16_maps_persistent(CUtensorMap* x_map, const void* planes, 
     return e;
 }
 
-bool linear_tma_use_persistent(int M, int N, int num_sms) {
-    return (long long)((M + pers::TM - 1) / pers::TM) * ((N + pers::TN - 1) / pers::TN) >= num_sms;
+// The persistent kernel runs each 128 x 256 tile's whole K loop in one CTA;
+// the split-K kernel spreads a tile's K over up to 8 CTAs.  Measured on
+// B200 over M 256..16384, N 1024..256206, K 1024..4096: the persistent
+// kernel wins once there are at least 20 tiles per 1024 of K (for 148 SMs).
+bool linear_tma_use_persistent(int M, int N, int K, int num_sms) {
+    const long long tiles = (long long)((M + pers::TM - 1) / pers::TM) * ((N + pers::TN - 1) / pers::TN);
+    return tiles * 1024 * 148 >= 20LL * K * num_sms;
 }
 
 cudaError_t launch_linear_tma_persistent(const LinearArgs& a, const CUtensorMap* tx, const CUtensorMap* tw,
@@ -546,11 +551,13 @@ cudaError_t launch_linear_tma_persistent(const LinearArgs& a, const CUtensorMap*
     return cudaGetLastError();
 }
 
+// Split-K depth: the largest of 1, 2, 4, 8 that keeps the grid to one wave
+// (one CTA per SM) and every CTA at least two K chunks.
 int linear_tma_splits(int M, int N, int K, int num_sms) {
     const int tiles = ((N + TN - 1) / TN) * ((M + TM - 1) / TM);
     const int nk = K / TK;
     int S = 1;
-    while (S < 8 && tiles * S < 2 * num_sms && nk / (2 * S) >= 2) S *= 2;  // 1, 2, 4, 8: divides 128 rows
+    while (S < 8 && tiles * 2 * S <= num_sms && nk / (2 * S) >= 2) S *= 2;
     return S;
 }
 

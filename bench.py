@@ -127,7 +127,7 @@ def parse_args():
     ap.add_argument("--cpu-sample-s", type=float, default=10.0)
     ap.add_argument("--translate-sentences", type=int, default=1024,
                     help="sentences of the sentence-batched translation (0: skip translation)")
-    ap.add_argument("--ncu-case", choices=("decode", "decode1", "cross", "prefill"),
+    ap.add_argument("--ncu-case", choices=("decode", "decode1", "cross", "prefill", "linear"),
                     help="run one small fixed case for an ncu capture and exit")
     return ap.parse_args()
 
@@ -557,6 +557,21 @@ def ncu_case(which: str) -> None:
         oc = torch.empty_like(qc)
         for _ in range(3):
             c.cross(0, 1, qc, oc)
+    elif which == "linear":
+        # INT8 linear on the engine's path (weights prepared once, TMA-fed tcgen05):
+        # 256 rows x 1024 -> 1024 (split-K cluster kernel), then the vocabulary
+        # projection 256 x 1024 -> 256206 (persistent kernel); 3 launches each
+        x = torch.randn((256, 1024), generator=g, device=dev)
+        for n_out in (1024, 256206):
+            w = torch.randint(-127, 128, (n_out, 1024), generator=g, device=dev, dtype=torch.int8)
+            sc = torch.full((n_out,), 3666.19, device=dev)
+            with na.PreparedLinear(w, sc) as lin:
+                for _ in range(3):
+                    lin(x)
+                torch.cuda.synchronize()
+                assert lin.status() == 0
+        print("ncu case linear: ok")
+        return
     elif which == "prefill":
         B, S = 8, 128
         c = na.Context(0, n_layers=0, max_sentences=0)

@@ -52,15 +52,18 @@ def _dev(a, device):
 
 
 @pytest.mark.parametrize("M,K,N,epilogue", [
-    (17, 1024, 300, "bias_relu"),      # 8-way split, 16-row slices, N tail
+    # split-K cluster kernel (128 x 128 tiles), depth chosen for one wave on 148 SMs
+    (17, 1024, 300, "bias_relu"),      # 8 CTAs per tile, 16-row slices, N tail
     (17, 1024, 301, "residual"),       # N % 4 != 0: scalar stores
-    (300, 4096, 1024, "residual"),     # 8-way split, M tail
-    (1024, 1024, 4096, "bias_relu"),   # 2-way split
-    (2048, 1024, 1024, "plain"),       # 4-way split
-    (4100, 1024, 4096, "bias_relu"),   # no split, M tail
-    (40, 1024, 256206, "plain"),       # vocabulary projection shape (persistent kernel, N tail)
-    (2000, 1024, 3001, "residual"),    # persistent kernel, M and N tails, N % 4 != 0
-    (1100, 4096, 2048, "bias_relu"),   # persistent kernel, K = 4096
+    (300, 4096, 1024, "residual"),     # 4 CTAs per tile, M tail
+    (1024, 4096, 1024, "bias_relu"),   # 2 CTAs per tile
+    (2048, 4096, 1024, "plain"),       # no split (plain launch, no cluster)
+    # persistent kernel (128 x 256 tiles)
+    (2048, 1024, 1024, "plain"),
+    (4100, 1024, 4096, "bias_relu"),   # M tail
+    (40, 1024, 256206, "plain"),       # vocabulary projection shape, N tail
+    (2000, 1024, 3001, "residual"),    # M and N tails, N % 4 != 0
+    (1100, 4096, 3072, "bias_relu"),   # K = 4096
 ])
 def test_prepared_linear_matches_reference(cuda_device, M, K, N, epilogue):
     import torch
