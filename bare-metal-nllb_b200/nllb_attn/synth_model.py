@@ -142,6 +142,17 @@ def ensure_model(path: str, seed: int = 0) -> str:
     return path
 
 
+def source_lengths(seed: int, n: int, lo: int, hi: int) -> List[int]:
+    """n source lengths uniform in [lo, hi) from a splitmix-style integer hash
+    of (seed, index): the same on every machine."""
+    with np.errstate(over="ignore"):
+        x = np.arange(n, dtype=np.uint64) + np.uint64((seed * 0xD1B54A32D192ED03) & (2**64 - 1))
+        z = x * np.uint64(0x9E3779B97F4A7C15)
+        z = (z ^ (z >> np.uint64(31))) * np.uint64(0xBF58476D1CE4E5B9)
+        z = z ^ (z >> np.uint64(29))
+    return [int(v) for v in (lo + (z % np.uint64(hi - lo)).astype(np.int64))]
+
+
 def source_ids(seed: int, n_tokens: int, src_lang: str = "eng_Latn") -> List[int]:
     """[src_lang] + n_tokens ids uniform in [4, 256000) + [2] (</s>), the way
     the reference builds its source (main.c:274-290)."""

@@ -434,11 +434,9 @@ SYNTH_MODEL = os.environ.get("NLLB_SYNTH_MODEL", "/tmp/nllb_synth/synth_nllb600m
 def config4_sources(n: int = 1024, seed: int = 4):
     """Sentence-batched translation workload: n sources of U[16,128] tokens
     (ids U[4,256000)), each [eng_Latn] ... [2]."""
-    sys.path.insert(0, os.path.join(REPO, "oracle"))
-    import pyoracle as po
     from nllb_attn import synth_model as sm
-    lengths = po.det_ints(seed, n, 16, 129)
-    return [sm.source_ids(seed * 1000003 + i, int(lengths[i])) for i in range(n)]
+    lengths = sm.source_lengths(seed, n, 16, 129)
+    return [sm.source_ids(seed * 1000003 + i, lengths[i]) for i in range(n)]
 
 
 def reference_translate_rate(model_path: str):
