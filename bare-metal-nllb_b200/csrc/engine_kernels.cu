@@ -250,23 +250,6 @@ __device__ __forceinline__ bool better(float va, int ia, float vb, int ib) {
     return va > vb || (va == vb && ia < ib);
 }
 
-template <int K>
-__device__ __forceinline__ void topk_insert(float (&tv)[K], int (&ti)[K], float v, int i) {
-    if (!better(v, i, tv[K - 1], ti[K - 1])) return;
-    // the candidate sinks to its place, each displaced entry moves one down
-#pragma unroll
-    for (int q = 0; q < K; ++q) {
-        if (better(v, i, tv[q], ti[q])) {
-            const float tvq = tv[q];
-            const int tiq = ti[q];
-            tv[q] = v;
-            ti[q] = i;
-            v = tvq;
-            i = tiq;
-        }
-    }
-}
-
 // (max, sum of exp relative to max) of two parts
 __device__ __forceinline__ void lse_combine(float& m, float& s, float mo, float so) {
     const float mn = fmaxf(m, mo);
@@ -299,19 +282,51 @@ __device__ __forceinline__ void warp_merge_topk(float (&tv)[K], int (&ti)[K], fl
     }
 }
 
+// A warp's running top-K, spread over lanes 0..K-1 (lane 0 best), with the
+// K-th entry (the admission threshold) in every lane.
 template <int K>
-__device__ __forceinline__ void visit(float v, int i, float& m, float& s, float (&tv)[K], int (&ti)[K]) {
-    if (v > m) {
-        s = s * expf(m - v) + 1.f;  // m = -FLT_MAX at the start: 0 * 0 + 1
-        m = v;
-    } else {
-        s += expf(v - m);
+struct WarpTopK {
+    float v = -FLT_MAX, tv = -FLT_MAX;  // own entry, threshold value
+    int i = 0x7fffffff, ti = 0x7fffffff;
+
+    // Insert a warp-uniform candidate that beats the threshold.
+    __device__ __forceinline__ void insert(float cv, int ci, int lane) {
+        const bool ahead = lane < K && better(v, i, cv, ci);
+        const int pos = __popc(__ballot_sync(0xffffffffu, ahead));  // entries ahead form a prefix
+        const float uv = __shfl_up_sync(0xffffffffu, v, 1);
+        const int ui = __shfl_up_sync(0xffffffffu, i, 1);
+        if (lane > pos && lane < K) v = uv, i = ui;
+        if (lane == pos) v = cv, i = ci;
+        tv = __shfl_sync(0xffffffffu, v, K - 1);
+        ti = __shfl_sync(0xffffffffu, i, K - 1);
     }
-    topk_insert<K>(tv, ti, v, i);
+    // Offer each lane's (x, ix) (valid lanes only); warp-uniform call.
+    __device__ __forceinline__ void offer(float x, int ix, bool valid, int lane) {
+        unsigned mask = __ballot_sync(0xffffffffu, valid && better(x, ix, tv, ti));
+        while (mask) {
+            const int src = __ffs(mask) - 1;
+            mask &= mask - 1;
+            const float cv = __shfl_sync(0xffffffffu, x, src);
+            const int ci = __shfl_sync(0xffffffffu, ix, src);
+            if (better(cv, ci, tv, ti)) insert(cv, ci, lane);
+        }
+    }
+};
+
+// Online (max, sum of exp relative to max) with e^d computed as 2^(d log2 e).
+__device__ __forceinline__ void lse_add4(float& m, float& s, float4 v, float m4) {
+    if (m4 > m) {  // rare after the first elements; m = -FLT_MAX at the start
+        s *= exp2f((m - m4) * kLog2e);
+        m = m4;
+    }
+    s += exp2f((v.x - m) * kLog2e) + exp2f((v.y - m) * kLog2e) + exp2f((v.z - m) * kLog2e) +
+         exp2f((v.w - m) * kLog2e);
 }
 
 // Partial over columns [c*chunk, (c+1)*chunk) of row r (grid: chunks x rows):
-// online max and sum of exp, K best; written to ws[r][c] = {m, s, v[K], i[K]}.
+// online max and sum of exp per thread, a top-K per warp (one ballot per
+// float4 against the warp's threshold; insertions are rare after the first
+// few elements), then a block merge.  Written to ws[r][c] = {m, s, v[K], i[K]}.
 template <int K>
 __global__ void __launch_bounds__(256) vocab_partial_kernel(const float* logits, size_t ld, int V, int chunk,
                                                             const unsigned char* active, float* ws) {
@@ -319,44 +334,56 @@ __global__ void __launch_bounds__(256) vocab_partial_kernel(const float* logits,
     __shared__ int sh_i[8 * K];
     const int r = blockIdx.y, c = blockIdx.x, C = gridDim.x;
     if (active && !active[r]) return;  // uniform per CTA
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const float* lg = logits + (size_t)r * ld;
     const int lo = c * chunk, hi = min(V, lo + chunk);
     float m = -FLT_MAX, s = 0.f;
-    float tv[K];
-    int ti[K];
-#pragma unroll
-    for (int q = 0; q < K; ++q) tv[q] = -FLT_MAX, ti[q] = 0x7fffffff;
-    // scalar head up to a 16-byte boundary, float4 body, scalar tail
+    WarpTopK<K> top;
+    // scalar head up to a 16-byte boundary and scalar tail: warp 0, one element per lane
     const int head = min(hi - lo, (int)(((16u - (uint32_t)(reinterpret_cast<uintptr_t>(lg + lo) & 15u)) & 15u) >> 2));
     const int b0 = lo + head, nb4 = (hi - b0) >> 2, t0 = b0 + 4 * nb4;
-    if ((int)threadIdx.x < head) visit<K>(lg[lo + threadIdx.x], lo + threadIdx.x, m, s, tv, ti);
-    const float4* body = reinterpret_cast<const float4*>(lg + b0);
-#pragma unroll 4
-    for (int j = threadIdx.x; j < nb4; j += 256) {
-        const float4 v = __ldcs(body + j);
-        const int i = b0 + 4 * j;
-        visit<K>(v.x, i, m, s, tv, ti);
-        visit<K>(v.y, i + 1, m, s, tv, ti);
-        visit<K>(v.z, i + 2, m, s, tv, ti);
-        visit<K>(v.w, i + 3, m, s, tv, ti);
+    if (warp == 0) {
+        for (int e = 0; e < 2; ++e) {
+            const int idx = e == 0 ? lo + lane : t0 + lane;
+            const bool valid = e == 0 ? lane < head : idx < hi;
+            const float x = valid ? lg[idx] : -INFINITY;
+            lse_add4(m, s, make_float4(x, -INFINITY, -INFINITY, -INFINITY), x);
+            top.offer(x, idx, valid, lane);
+        }
     }
-    if (t0 + (int)threadIdx.x < hi) visit<K>(lg[t0 + threadIdx.x], t0 + threadIdx.x, m, s, tv, ti);
+    // float4 body; the loop bound is uniform per warp (lane j0 + lane may be past the end)
+    const float4* body = reinterpret_cast<const float4*>(lg + b0);
+    const float4 none = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    int j = warp * 32 + lane;
+    float4 cur = j < nb4 ? __ldcs(body + j) : none;
+    for (int j0 = warp * 32; j0 < nb4; j0 += 256, j += 256) {
+        const float4 nxt = j + 256 < nb4 ? __ldcs(body + j + 256) : none;  // one float4 ahead
+        const bool valid = j < nb4;
+        const float m4 = fmaxf(fmaxf(cur.x, cur.y), fmaxf(cur.z, cur.w));
+        lse_add4(m, s, cur, m4);
+        const int i0 = b0 + 4 * j;
+        unsigned mask = __ballot_sync(0xffffffffu, valid && m4 >= top.tv);
+        while (mask) {
+            const int src = __ffs(mask) - 1;
+            mask &= mask - 1;
+            const float c0 = __shfl_sync(0xffffffffu, cur.x, src), c1 = __shfl_sync(0xffffffffu, cur.y, src);
+            const float c2 = __shfl_sync(0xffffffffu, cur.z, src), c3 = __shfl_sync(0xffffffffu, cur.w, src);
+            const int ci = __shfl_sync(0xffffffffu, i0, src);
+            if (better(c0, ci, top.tv, top.ti)) top.insert(c0, ci, lane);
+            if (better(c1, ci + 1, top.tv, top.ti)) top.insert(c1, ci + 1, lane);
+            if (better(c2, ci + 2, top.tv, top.ti)) top.insert(c2, ci + 2, lane);
+            if (better(c3, ci + 3, top.tv, top.ti)) top.insert(c3, ci + 3, lane);
+        }
+        cur = nxt;
+    }
     // warp, then block
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         const float mo = __shfl_xor_sync(0xffffffffu, m, o), so = __shfl_xor_sync(0xffffffffu, s, o);
         lse_combine(m, s, mo, so);
     }
-    float rv[K];
-    int ri[K];
-    warp_merge_topk<K>(tv, ti, rv, ri);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (lane == 0) {
-        sh_m[warp] = m;
-        sh_s[warp] = s;
-#pragma unroll
-        for (int q = 0; q < K; ++q) sh_v[warp * K + q] = rv[q], sh_i[warp * K + q] = ri[q];
-    }
+    if (lane == 0) sh_m[warp] = m, sh_s[warp] = s;
+    if (lane < K) sh_v[warp * K + lane] = top.v, sh_i[warp * K + lane] = top.i;
     __syncthreads();
     if (warp == 0) {
         m = lane < 8 ? sh_m[lane] : -FLT_MAX;
@@ -366,6 +393,8 @@ __global__ void __launch_bounds__(256) vocab_partial_kernel(const float* logits,
             const float mo = __shfl_xor_sync(0xffffffffu, m, o), so = __shfl_xor_sync(0xffffffffu, s, o);
             lse_combine(m, s, mo, so);
         }
+        float tv[K], rv[K];
+        int ti[K], ri[K];
 #pragma unroll
         for (int q = 0; q < K; ++q) {
             tv[q] = lane < 8 ? sh_v[lane * K + q] : -FLT_MAX;
