@@ -270,9 +270,8 @@ __global__ void __launch_bounds__(kThreads) decode_self_kernel(const SelfParams 
 // ---------------------------------------------------------------------------
 // Cross-attention: all beams of a sentence share each memory row.
 // ---------------------------------------------------------------------------
-template <int NB>
+template <int NB, int CP>
 __global__ void __launch_bounds__(kThreads) cross_kernel(const CrossParams p) {
-    constexpr int CP = kCrossChunkRows;
     constexpr int RPH = CP / 8;  // rows per half-warp per chunk
     constexpr int KV_FLOATS = CP * 64;
 
@@ -505,9 +504,9 @@ size_t self_smem_bytes() {
     return kBarBytes + (ring > merge ? ring : merge);
 }
 
-template <int NB>
+template <int NB, int CP>
 size_t cross_smem_bytes() {
-    const size_t ring = (size_t)kCrossStages * 2 * kCrossChunkRows * 64 * sizeof(float);
+    const size_t ring = (size_t)kCrossStages * 2 * CP * 64 * sizeof(float);
     const size_t merge = (size_t)(8 * NB + NB) * kPartFloats * sizeof(float);
     return kBarBytes + (ring > merge ? ring : merge);
 }
@@ -545,8 +544,11 @@ cudaError_t configure_nb() {
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)self_smem_bytes<NB>());
     if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(cross_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)cross_smem_bytes<NB>());
+    e = cudaFuncSetAttribute(cross_kernel<NB, kCrossShortRows>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)cross_smem_bytes<NB, kCrossShortRows>());
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(cross_kernel<NB, kCrossLongRows>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)cross_smem_bytes<NB, kCrossLongRows>());
 }
 
 template <int NB>
@@ -556,9 +558,12 @@ cudaError_t launch_self_nb(const SelfParams& p, int n_sent, cudaStream_t st) {
 }
 
 template <int NB>
-cudaError_t launch_cross_nb(const CrossParams& p, int n_sent, cudaStream_t st) {
-    return launch_ex(cross_kernel<NB>, dim3(p.n_split, p.H, n_sent), cross_smem_bytes<NB>(),
-                     p.n_split, st, p);
+cudaError_t launch_cross_nb(const CrossParams& p, int n_sent, int chunk_rows, cudaStream_t st) {
+    if (chunk_rows == kCrossLongRows)
+        return launch_ex(cross_kernel<NB, kCrossLongRows>, dim3(p.n_split, p.H, n_sent),
+                         cross_smem_bytes<NB, kCrossLongRows>(), p.n_split, st, p);
+    return launch_ex(cross_kernel<NB, kCrossShortRows>, dim3(p.n_split, p.H, n_sent),
+                     cross_smem_bytes<NB, kCrossShortRows>(), p.n_split, st, p);
 }
 
 }  // namespace
@@ -581,12 +586,12 @@ cudaError_t launch_decode_self(const SelfParams& p, int n_sent, int n_beams, cud
     }
 }
 
-cudaError_t launch_cross(const CrossParams& p, int n_sent, int n_beams, cudaStream_t st) {
+cudaError_t launch_cross(const CrossParams& p, int n_sent, int n_beams, int chunk_rows, cudaStream_t st) {
     switch (n_beams) {
-        case 1: return launch_cross_nb<1>(p, n_sent, st);
-        case 2: return launch_cross_nb<2>(p, n_sent, st);
-        case 4: return launch_cross_nb<4>(p, n_sent, st);
-        case 8: return launch_cross_nb<8>(p, n_sent, st);
+        case 1: return launch_cross_nb<1>(p, n_sent, chunk_rows, st);
+        case 2: return launch_cross_nb<2>(p, n_sent, chunk_rows, st);
+        case 4: return launch_cross_nb<4>(p, n_sent, chunk_rows, st);
+        case 8: return launch_cross_nb<8>(p, n_sent, chunk_rows, st);
         default: return cudaErrorInvalidValue;
     }
 }
