@@ -226,6 +226,8 @@ struct nllb_model {
     size_t planes_elems = 0;
     std::map<std::pair<int, int>, CUtensorMap> plane_maps;  // key (M, K): split-K kernel
     std::map<std::pair<int, int>, CUtensorMap> plane_maps_pers;  // key (M, K): persistent kernel
+    // buffers of translate calls, kept between calls (grow-only, taken in call order)
+    std::vector<std::pair<void*, size_t>> work_pool;
     int num_sms = 148;
     // decision margins of the last translate call, [sentence][step]
     std::vector<std::vector<float>> margins;
@@ -330,6 +332,8 @@ void nllb_model_free(nllb_model* m) {
     if (m->attn) nllb_attn_destroy(m->attn);
     for (void* p : m->allocs) cudaFree(p);
     if (m->planes) cudaFree(m->planes);
+    for (auto& b : m->work_pool)
+        if (b.first) cudaFree(b.first);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
 }
@@ -508,16 +512,23 @@ struct Work {
     float* top_lp = nullptr;
     float* topk_ws = nullptr;  // partials of the vocabulary log-softmax / top-k
     unsigned char* active = nullptr;
-    std::vector<void*> allocs;
-    ~Work() {
-        for (void* p : allocs) cudaFree(p);
-    }
+    // buffers come from the model's pool in call order: a call no larger than
+    // an earlier one allocates nothing (the previous call has finished: it
+    // returned its results to the host)
+    nllb_model* m = nullptr;
+    size_t next = 0;
     template <typename T>
     int alloc(T** p, size_t n) {
-        void* v = nullptr;
-        ENG_CK(cudaMalloc(&v, std::max<size_t>(n, 1) * sizeof(T)));
-        allocs.push_back(v);
-        *p = static_cast<T*>(v);
+        const size_t bytes = std::max<size_t>(n, 1) * sizeof(T);
+        if (next == m->work_pool.size()) m->work_pool.push_back({nullptr, 0});
+        auto& slot = m->work_pool[next++];
+        if (slot.second < bytes) {
+            if (slot.first) cudaFree(slot.first);
+            slot = {nullptr, 0};
+            ENG_CK(cudaMalloc(&slot.first, bytes));
+            slot.second = bytes;
+        }
+        *p = static_cast<T*>(slot.first);
         return NLLB_ATTN_OK;
     }
 };
@@ -623,6 +634,7 @@ extern "C" int nllb_translate(nllb_model* m, int n_sent, const int* src_tokens, 
     const auto t_start = std::chrono::steady_clock::now();
 
     Work w;
+    w.m = m;
     w.n_sent = n_sent;
     std::vector<int> n_src(n_sent), max_out(n_sent);
     int S = 0;

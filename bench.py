@@ -494,7 +494,7 @@ def measure_translation(args, rank, world, local_rank):
                 "tok_s_total": round(best.tokens_out / ((best.encode_ms + best.decode_ms) / 1e3), 1),
                 "ms_encode": round(best.encode_ms, 2), "ms_decode": round(best.decode_ms, 2)}
         if mine:
-            m.translate(mine[:min(4, len(mine))], tgt, max_gen=132)  # warm-up
+            m.translate(mine, tgt, max_gen=8)  # warm-up at the full batch: kernels, pooled buffers
         if world > 1:
             dist.barrier()
         t0 = time.perf_counter()
