@@ -1,9 +1,9 @@
 // device_common.cuh -- PTX helpers shared by the attention kernels (sm_100a).
 //
 // Bulk copies (cp.async.bulk, the 1-D form of TMA) move contiguous K/V
-// blocks from HBM into shared memory and complete on an mbarrier.  No copy
-// here uses .multicast::cluster: the kernels run unchanged on every GPU of a
-// multi-GPU job.  Every wait on an mbarrier is bounded by a clock64() budget;
+// blocks from HBM into shared memory and complete on an mbarrier.  Every copy
+// targets the issuing CTA's own shared memory only (no cluster-wide copies),
+// and no kernel reads another GPU's memory.  Every wait on an mbarrier is bounded by a clock64() budget;
 // on expiry the kernel records NLLB_DEV_ERR_TIMEOUT in the context's device
 // error word and leaves without writing outputs.
 #pragma once
