@@ -153,6 +153,59 @@ __global__ void __launch_bounds__(256) linear_skinny_kernel(const LinearArgs a) 
     }
 }
 
+// Weight-streaming shape (M <= MT rows, K % 16 == 0): a warp owns RPW
+// output columns over the whole K; lane l reads 16 consecutive int8 weights
+// of each of its rows at k = 512 j + 16 l (16-byte loads, so a warp has all
+// of its rows' bytes in flight after a few iterations) and the matching
+// activations through L1; the partial dots are summed over the warp.
+template <int MT, int RPW>
+__global__ void __launch_bounds__(256) linear_gemv_kernel(const LinearArgs a) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = (blockIdx.x * 8 + warp) * RPW;
+    if (n0 >= a.N) return;  // uniform per warp
+    float acc[RPW][MT];
+#pragma unroll
+    for (int r = 0; r < RPW; ++r)
+#pragma unroll
+        for (int m = 0; m < MT; ++m) acc[r][m] = 0.f;
+    const int8_t* wrow[RPW];
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) wrow[r] = a.w + (size_t)min(n0 + r, a.N - 1) * a.K;  // rows past N: repeat, not stored
+#pragma unroll 2
+    for (int k = lane * 16; k < a.K; k += 512) {
+        int4 w[RPW];
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) w[r] = __ldg(reinterpret_cast<const int4*>(wrow[r] + k));
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            if (m >= a.M) break;
+            const float4* xp = reinterpret_cast<const float4*>(a.x + (size_t)m * a.ldx + k);
+            const float4 x0 = __ldg(xp), x1 = __ldg(xp + 1), x2 = __ldg(xp + 2), x3 = __ldg(xp + 3);
+            const float xs[16] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w,
+                                  x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
+#pragma unroll
+            for (int r = 0; r < RPW; ++r) {
+                const int words[4] = {w[r].x, w[r].y, w[r].z, w[r].w};
+#pragma unroll
+                for (int q = 0; q < 16; ++q) {
+                    const float wv = (float)(int8_t)(words[q >> 2] >> (8 * (q & 3)));
+                    acc[r][m] = fmaf(wv, xs[q], acc[r][m]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            float v = acc[r][m];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == ((r * MT + m) & 31) && m < a.M && n0 + r < a.N) linear_store(a, m, n0 + r, v);
+        }
+    }
+}
+
 // General shape: 64 x 64 output tile per CTA, 256 threads with 4 x 4
 // outputs each, K in steps of 32 through shared memory (x transposed to
 // k-major, weights converted to fp32).
@@ -496,7 +549,13 @@ cudaError_t launch_layernorm(float* out, float* x, const float* res, const float
 cudaError_t launch_linear(const LinearArgs& a, const LinearWorkspace* wsp, int num_sms, int* err, cudaStream_t st) {
     if (a.M <= 0) return cudaSuccess;
     if ((a.K & 3) || (a.ldx & 3)) return cudaErrorInvalidValue;
-    if (a.M <= 4) {
+    const bool gemv = (a.K % 16 == 0) && (a.ldx % 4 == 0) && ((reinterpret_cast<uintptr_t>(a.w) & 15) == 0) &&
+                      ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0);
+    if (gemv && a.M <= 4) {
+        linear_gemv_kernel<4, 2><<<(a.N + 15) / 16, 256, 0, st>>>(a);
+    } else if (gemv && a.M <= 16) {
+        linear_gemv_kernel<16, 2><<<(a.N + 15) / 16, 256, 0, st>>>(a);
+    } else if (a.M <= 4) {
         linear_skinny_kernel<4, 2><<<(a.N + 15) / 16, 256, 0, st>>>(a);
     } else if (a.M <= 16) {
         linear_skinny_kernel<16, 2><<<(a.N + 15) / 16, 256, 0, st>>>(a);
