@@ -10,6 +10,8 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include <utility>
+
 namespace nllb {
 
 constexpr int kHeadDim = 64;
@@ -160,6 +162,28 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 // is visible; everything that reads a predecessor's output comes after this.
 __device__ __forceinline__ void pdl_wait_primary() {
     asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Launch with programmatic stream serialisation: the kernel may be scheduled
+// while its predecessor in the stream finishes (once every predecessor CTA has
+// started or triggered); it must execute pdl_wait_primary() before reading the
+// predecessor's outputs or writing global memory.  Waiting also covers every
+// earlier kernel of the stream, since each of them waited on its own
+// predecessor before finishing.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 }  // namespace nllb

@@ -460,6 +460,7 @@ int run_linear(nllb_model* m, const Lin& L, const float* x, int M, float* out, c
     a.cblock = cblock;
     a.relu = relu;
     a.mask_from = mask_from;
+    a.static_weights = 1;  // the model's own weights, written at load
     if (M > 16 && L.wb && (size_t)M * L.in * 3 <= m->planes_elems) {
         // x -> three bf16 planes, then the TMA-fed tensor-core GEMM
         ENG_CK(launch_split3(x, L.in, M, L.in, m->planes, m->stream));
@@ -894,6 +895,7 @@ extern "C" int nllb_linear_int8(const float* x, int M, int K, const int8_t* w, c
     a.cblock = N;
     a.relu = (flags & NLLB_LINEAR_RELU) ? 1 : 0;
     a.mask_from = -1;
+    a.static_weights = 0;
     // bounded-wait error word of the current device for callers without a context
     static int* err_words[64] = {nullptr};
     int dev = 0;

@@ -20,6 +20,8 @@ namespace {
 __global__ void embed_pos_kernel(float* x, const int* tokens, const int* positions, int pos_const,
                                  const int8_t* emb, const float* emb_inv_scale, const float* pos_table,
                                  float embed_scale, int rows, int vocab) {
+    pdl_launch_dependents();
+    pdl_wait_primary();  // inputs come from earlier kernels; outputs may still be read by them
     const int r = blockIdx.x;
     if (r >= rows) return;
     const int tok = min(max(tokens[r], 0), vocab - 1);
@@ -52,6 +54,8 @@ __device__ __forceinline__ float block_sum_256(float v, float* sh) {
 
 __global__ void __launch_bounds__(256) layernorm_kernel(float* out, float* x, const float* res,
                                                          const float* gamma, const float* beta, int rows) {
+    pdl_launch_dependents();
+    pdl_wait_primary();  // inputs come from earlier kernels; outputs may still be read by them
     __shared__ float sh[8];
     const int r = blockIdx.x;
     if (r >= rows) return;
@@ -97,6 +101,8 @@ __device__ __forceinline__ void linear_store(const LinearArgs& a, int m, int n, 
 // in shared memory and are read once per 4 weights for all RPW rows.
 template <int MT, int RPW>
 __global__ void __launch_bounds__(256) linear_skinny_kernel(const LinearArgs a) {
+    pdl_launch_dependents();
+    pdl_wait_primary();  // inputs come from earlier kernels; outputs may still be read by them
     constexpr int KC = 512;
     __shared__ __align__(16) float xs[MT][KC];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -153,55 +159,84 @@ __global__ void __launch_bounds__(256) linear_skinny_kernel(const LinearArgs a) 
     }
 }
 
-// Weight-streaming shape (M <= MT rows, K % 16 == 0): a warp owns RPW
-// output columns over the whole K; lane l reads 16 consecutive int8 weights
-// of each of its rows at k = 512 j + 16 l (16-byte loads, so a warp has all
-// of its rows' bytes in flight after a few iterations) and the matching
-// activations through L1; the partial dots are summed over the warp.
-template <int MT, int RPW>
+// Weight-streaming shape (M <= MT rows, K % 1024 == 0): lane l of every warp
+// owns output column n = 32 blockIdx.x + l.  The 8 warps of a CTA take K / 8
+// each, in blocks of 128 weights: a lane issues eight independent 16-byte
+// loads of its row (the block in flight at once), the next block's loads go
+// out before the current block is multiplied with x[m][k..k+127] (the same
+// address for every lane: broadcast loads).  The weights, scale and bias are
+// constants, so the first block and the column's factors are fetched before
+// waiting for the predecessor kernel.  Partial dots are summed through shared
+// memory.
+template <int MT>
 __global__ void __launch_bounds__(256) linear_gemv_kernel(const LinearArgs a) {
+    __shared__ float red[8][MT][32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = (blockIdx.x * 8 + warp) * RPW;
-    if (n0 >= a.N) return;  // uniform per warp
-    float acc[RPW][MT];
+    const int n = blockIdx.x * 32 + lane;
+    const int kw = a.K >> 3, k0 = warp * kw;
+    const int nc = min(n, a.N - 1);  // columns past N: repeat a row, not stored
+    const int8_t* wrow = a.w + (size_t)nc * a.K;
+    if (!a.static_weights) pdl_wait_primary();  // the caller may have written the weights just before
+    int4 w[8];
 #pragma unroll
-    for (int r = 0; r < RPW; ++r)
+    for (int i = 0; i < 8; ++i) w[i] = __ldg(reinterpret_cast<const int4*>(wrow + k0) + i);
+    float inv = 0.f, bias = 0.f;
+    if (warp == 0) {
+        inv = 1.0f / a.scale[nc];  // 1/scale as tensor.c:75
+        if (a.bias) bias = a.bias[nc];
+    }
+    pdl_launch_dependents();
+    pdl_wait_primary();  // x comes from the previous kernel
+    float acc[MT];
 #pragma unroll
-        for (int m = 0; m < MT; ++m) acc[r][m] = 0.f;
-    const int8_t* wrow[RPW];
+    for (int m = 0; m < MT; ++m) acc[m] = 0.f;
+    for (int kb = k0; kb < k0 + kw; kb += 128) {
+        const bool more = kb + 128 < k0 + kw;
+        int4 wn[8];
 #pragma unroll
-    for (int r = 0; r < RPW; ++r) wrow[r] = a.w + (size_t)min(n0 + r, a.N - 1) * a.K;  // rows past N: repeat, not stored
-#pragma unroll 2
-    for (int k = lane * 16; k < a.K; k += 512) {
-        int4 w[RPW];
+        for (int i = 0; i < 8; ++i)
+            wn[i] = more ? __ldg(reinterpret_cast<const int4*>(wrow + kb + 128) + i) : make_int4(0, 0, 0, 0);
 #pragma unroll
-        for (int r = 0; r < RPW; ++r) w[r] = __ldg(reinterpret_cast<const int4*>(wrow[r] + k));
+        for (int i = 0; i < 8; ++i) {
+            const int words[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
+            float wf[16];
 #pragma unroll
-        for (int m = 0; m < MT; ++m) {
-            if (m >= a.M) break;
-            const float4* xp = reinterpret_cast<const float4*>(a.x + (size_t)m * a.ldx + k);
-            const float4 x0 = __ldg(xp), x1 = __ldg(xp + 1), x2 = __ldg(xp + 2), x3 = __ldg(xp + 3);
-            const float xs[16] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w,
-                                  x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
+            for (int q = 0; q < 16; ++q) wf[q] = (float)(int8_t)(words[q >> 2] >> (8 * (q & 3)));
 #pragma unroll
-            for (int r = 0; r < RPW; ++r) {
-                const int words[4] = {w[r].x, w[r].y, w[r].z, w[r].w};
+            for (int m = 0; m < MT; ++m) {
+                if (m >= a.M) break;
+                const float4* xp = reinterpret_cast<const float4*>(a.x + (size_t)m * a.ldx + kb + 16 * i);
 #pragma unroll
-                for (int q = 0; q < 16; ++q) {
-                    const float wv = (float)(int8_t)(words[q >> 2] >> (8 * (q & 3)));
-                    acc[r][m] = fmaf(wv, xs[q], acc[r][m]);
+                for (int c = 0; c < 4; ++c) {
+                    const float4 xv = __ldg(xp + c);
+                    acc[m] = fmaf(wf[4 * c], xv.x, acc[m]);
+                    acc[m] = fmaf(wf[4 * c + 1], xv.y, acc[m]);
+                    acc[m] = fmaf(wf[4 * c + 2], xv.z, acc[m]);
+                    acc[m] = fmaf(wf[4 * c + 3], xv.w, acc[m]);
                 }
             }
         }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w[i] = wn[i];
     }
 #pragma unroll
-    for (int r = 0; r < RPW; ++r) {
+    for (int m = 0; m < MT; ++m) red[warp][m][lane] = acc[m];
+    __syncthreads();
+    if (warp == 0 && n < a.N) {
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
-            float v = acc[r][m];
+            if (m >= a.M) break;
+            float v = red[0][m][lane];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (lane == ((r * MT + m) & 31) && m < a.M && n0 + r < a.N) linear_store(a, m, n0 + r, v);
+            for (int w8 = 1; w8 < 8; ++w8) v += red[w8][m][lane];
+            float y = v * inv;
+            if (a.bias) y += bias;
+            if (a.relu) y = fmaxf(y, 0.f);
+            if (a.mask_from >= 0 && n >= a.mask_from) y = -1e30f;
+            const size_t o =
+                (size_t)(n / a.cblock) * ((size_t)a.M * a.cblock) + (size_t)m * a.cblock + (n % a.cblock);
+            if (a.residual) y += a.residual[o];
+            a.out[o] = y;
         }
     }
 }
@@ -210,6 +245,8 @@ __global__ void __launch_bounds__(256) linear_gemv_kernel(const LinearArgs a) {
 // outputs each, K in steps of 32 through shared memory (x transposed to
 // k-major, weights converted to fp32).
 __global__ void __launch_bounds__(256) linear_tiled_kernel(const LinearArgs a) {
+    pdl_launch_dependents();
+    pdl_wait_primary();  // inputs come from earlier kernels; outputs may still be read by them
     constexpr int BM = 64, BN = 64, BK = 32;
     __shared__ __align__(16) float xs[BK][BM + 4];
     __shared__ __align__(16) float ws[BK][BN + 4];
@@ -270,6 +307,8 @@ __global__ void __launch_bounds__(256) linear_tiled_kernel(const LinearArgs a) {
 // ---------------------------------------------------------------------------
 __global__ void penalties_kernel(float* logits, size_t ld, const int* hist, int hist_ld, const int* n_tokens,
                                  const unsigned char* active, int rows, float penalty, int ngram) {
+    pdl_launch_dependents();
+    pdl_wait_primary();  // inputs come from earlier kernels; outputs may still be read by them
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= rows || (active && !active[r])) return;
     float* lg = logits + (size_t)r * ld;
@@ -383,6 +422,8 @@ __device__ __forceinline__ void lse_add4(float& m, float& s, float4 v, float m4)
 template <int K>
 __global__ void __launch_bounds__(256) vocab_partial_kernel(const float* logits, size_t ld, int V, int chunk,
                                                             const unsigned char* active, float* ws) {
+    pdl_launch_dependents();
+    pdl_wait_primary();  // inputs come from earlier kernels; outputs may still be read by them
     __shared__ float sh_m[8], sh_s[8], sh_v[8 * K];
     __shared__ int sh_i[8 * K];
     const int r = blockIdx.y, c = blockIdx.x, C = gridDim.x;
@@ -468,6 +509,8 @@ template <int K>
 __global__ void __launch_bounds__(256) vocab_merge_kernel(const float* ws, int C, int rows,
                                                           const unsigned char* active, int* out_tok,
                                                           float* out_logp) {
+    pdl_launch_dependents();
+    pdl_wait_primary();  // inputs come from earlier kernels; outputs may still be read by them
     const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (r >= rows || (active && !active[r])) return;  // uniform per warp
     const float* p = ws + (size_t)r * C * (2 + 2 * K);
@@ -508,6 +551,8 @@ __global__ void __launch_bounds__(256) vocab_merge_kernel(const float* ws, int C
 __global__ void set_memory_batched_kernel(float* km, float* vm, int* n_src_slots, int max_src, int H,
                                           const float* k, const float* v, long long sent_stride,
                                           const int* n_src, int n_sent) {
+    pdl_launch_dependents();
+    pdl_wait_primary();  // inputs come from earlier kernels; outputs may still be read by them
     const int s = blockIdx.y;
     const int n = n_src[s];
     if (blockIdx.x == 0 && threadIdx.x == 0) n_src_slots[s] = n;
@@ -524,6 +569,8 @@ __global__ void set_memory_batched_kernel(float* km, float* vm, int* n_src_slots
 }
 
 __global__ void reciprocal_kernel(float* out, const float* in, size_t n) {
+    pdl_launch_dependents();
+    pdl_wait_primary();  // inputs come from earlier kernels; outputs may still be read by them
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
         out[i] = 1.0f / in[i];
 }
@@ -534,31 +581,29 @@ cudaError_t launch_embed_pos(float* x, const int* tokens, const int* positions, 
                              const float* emb_inv_scale, const float* pos_table, float embed_scale, int rows,
                              int vocab, cudaStream_t st) {
     if (rows <= 0) return cudaSuccess;
-    embed_pos_kernel<<<rows, 256, 0, st>>>(x, tokens, positions, pos_const, emb, emb_inv_scale, pos_table,
-                                           embed_scale, rows, vocab);
-    return cudaGetLastError();
+    return launch_pdl(embed_pos_kernel, dim3(rows), dim3(256), 0, st, x, tokens, positions, pos_const, emb,
+                      emb_inv_scale, pos_table, embed_scale, rows, vocab);
 }
 
 cudaError_t launch_layernorm(float* out, float* x, const float* res, const float* gamma, const float* beta,
                              int rows, cudaStream_t st) {
     if (rows <= 0) return cudaSuccess;
-    layernorm_kernel<<<rows, 256, 0, st>>>(out, x, res, gamma, beta, rows);
-    return cudaGetLastError();
+    return launch_pdl(layernorm_kernel, dim3(rows), dim3(256), 0, st, out, x, res, gamma, beta, rows);
 }
 
 cudaError_t launch_linear(const LinearArgs& a, const LinearWorkspace* wsp, int num_sms, int* err, cudaStream_t st) {
     if (a.M <= 0) return cudaSuccess;
     if ((a.K & 3) || (a.ldx & 3)) return cudaErrorInvalidValue;
-    const bool gemv = (a.K % 16 == 0) && (a.ldx % 4 == 0) && ((reinterpret_cast<uintptr_t>(a.w) & 15) == 0) &&
+    const bool gemv = (a.K % 1024 == 0) && (a.ldx % 4 == 0) && ((reinterpret_cast<uintptr_t>(a.w) & 15) == 0) &&
                       ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0);
     if (gemv && a.M <= 4) {
-        linear_gemv_kernel<4, 2><<<(a.N + 15) / 16, 256, 0, st>>>(a);
+        return launch_pdl(linear_gemv_kernel<4>, dim3((a.N + 31) / 32), dim3(256), 0, st, a);
     } else if (gemv && a.M <= 16) {
-        linear_gemv_kernel<16, 2><<<(a.N + 15) / 16, 256, 0, st>>>(a);
+        return launch_pdl(linear_gemv_kernel<16>, dim3((a.N + 31) / 32), dim3(256), 0, st, a);
     } else if (a.M <= 4) {
-        linear_skinny_kernel<4, 2><<<(a.N + 15) / 16, 256, 0, st>>>(a);
+        return launch_pdl(linear_skinny_kernel<4, 2>, dim3((a.N + 15) / 16), dim3(256), 0, st, a);
     } else if (a.M <= 16) {
-        linear_skinny_kernel<16, 2><<<(a.N + 15) / 16, 256, 0, st>>>(a);
+        return launch_pdl(linear_skinny_kernel<16, 2>, dim3((a.N + 15) / 16), dim3(256), 0, st, a);
     } else if (linear_tc_supports(a)) {
         int splits = linear_tc_splits(a, num_sms);
         if (!wsp || linear_tc_workspace_floats(a, splits) > wsp->ws_floats || linear_tc_tiles(a) > wsp->n_counters)
@@ -567,7 +612,7 @@ cudaError_t launch_linear(const LinearArgs& a, const LinearWorkspace* wsp, int n
     } else {
         if (a.K % 32) return cudaErrorInvalidValue;
         dim3 grid((a.N + 63) / 64, (a.M + 63) / 64);
-        linear_tiled_kernel<<<grid, 256, 0, st>>>(a);
+        return launch_pdl(linear_tiled_kernel, grid, dim3(256), 0, st, a);
     }
     return cudaGetLastError();
 }
@@ -575,9 +620,8 @@ cudaError_t launch_linear(const LinearArgs& a, const LinearWorkspace* wsp, int n
 cudaError_t launch_penalties(float* logits, size_t ld, const int* hist, int hist_ld, const int* n_tokens,
                              const unsigned char* active, int rows, float penalty, int ngram, cudaStream_t st) {
     if (rows <= 0) return cudaSuccess;
-    penalties_kernel<<<(rows + 127) / 128, 128, 0, st>>>(logits, ld, hist, hist_ld, n_tokens, active, rows,
-                                                          penalty, ngram);
-    return cudaGetLastError();
+    return launch_pdl(penalties_kernel, dim3((rows + 127) / 128), dim3(128), 0, st, logits, ld, hist, hist_ld,
+                      n_tokens, active, rows, penalty, ngram);
 }
 
 int vocab_topk_chunks(int V, int rows) {
@@ -598,11 +642,13 @@ cudaError_t launch_logsoftmax_topk(const float* logits, size_t ld, int V, int ro
     const int chunk = (((V + C - 1) / C) + 3) & ~3;
     const dim3 g1(C, rows), g2((rows + 7) / 8);
     if (k == 8) {
-        vocab_partial_kernel<8><<<g1, 256, 0, st>>>(logits, ld, V, chunk, active, ws);
-        vocab_merge_kernel<8><<<g2, 256, 0, st>>>(ws, C, rows, active, out_tok, out_logp);
+        cudaError_t e = launch_pdl(vocab_partial_kernel<8>, g1, dim3(256), 0, st, logits, ld, V, chunk, active, ws);
+        if (e != cudaSuccess) return e;
+        return launch_pdl(vocab_merge_kernel<8>, g2, dim3(256), 0, st, ws, C, rows, active, out_tok, out_logp);
     } else if (k == 4) {
-        vocab_partial_kernel<4><<<g1, 256, 0, st>>>(logits, ld, V, chunk, active, ws);
-        vocab_merge_kernel<4><<<g2, 256, 0, st>>>(ws, C, rows, active, out_tok, out_logp);
+        cudaError_t e = launch_pdl(vocab_partial_kernel<4>, g1, dim3(256), 0, st, logits, ld, V, chunk, active, ws);
+        if (e != cudaSuccess) return e;
+        return launch_pdl(vocab_merge_kernel<4>, g2, dim3(256), 0, st, ws, C, rows, active, out_tok, out_logp);
     } else {
         return cudaErrorInvalidValue;
     }
@@ -614,9 +660,8 @@ cudaError_t launch_set_memory_batched(float* km, float* vm, int* n_src_slots, in
                                       int max_n, cudaStream_t st) {
     if (n_sent <= 0) return cudaSuccess;
     const int bx = (int)(((size_t)H * max_n * 16 + 255) / 256);
-    set_memory_batched_kernel<<<dim3(bx < 64 ? bx : 64, n_sent), 256, 0, st>>>(km, vm, n_src_slots, max_src, H, k,
-                                                                                v, sent_stride, n_src, n_sent);
-    return cudaGetLastError();
+    return launch_pdl(set_memory_batched_kernel, dim3(bx < 64 ? bx : 64, n_sent), dim3(256), 0, st, km, vm,
+                      n_src_slots, max_src, H, k, v, sent_stride, n_src, n_sent);
 }
 
 cudaError_t launch_reciprocal(float* out, const float* in, size_t n, cudaStream_t st) {

@@ -20,6 +20,8 @@ struct LinearArgs {
     int cblock;              // output column block (N for row-major)
     int relu;
     int mask_from;           // columns >= mask_from are set to -1e30 (-1: none)
+    int static_weights;      // 1: w, scale, bias are not written by earlier kernels of the stream
+                             // (a kernel may fetch them before waiting for its predecessor)
 };
 
 cudaError_t launch_embed_pos(float* x, const int* tokens, const int* positions, int pos_const, const int8_t* emb,

@@ -108,6 +108,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         fence_barrier_init();
         *s_abort = 0;
     }
+    pdl_launch_dependents();
+    pdl_wait_primary();  // the planes come from the previous kernel; the output may still be read by earlier ones
     if (tid < TN) s_inv[tid] = (n0 + tid < a.N) ? 1.0f / a.scale[n0 + tid] : 0.f;  // 1/scale as tensor.c:75
     tc_fence_before();
     __syncthreads();
@@ -337,6 +339,8 @@ __global__ void __launch_bounds__(pers::THREADS, 1)
         *s_abort = 0;
         fence_barrier_init();
     }
+    pdl_launch_dependents();
+    pdl_wait_primary();  // the planes come from the previous kernel; the output may still be read by earlier ones
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -456,6 +460,8 @@ __global__ void __launch_bounds__(pers::THREADS, 1)
 
 // x [M][ldx] fp32 -> planes [3][M][K] bf16 with x = p0 + p1 + p2 (to 24 bits)
 __global__ void split3_kernel(const float* x, int ldx, int M, int K, __nv_bfloat16* planes) {
+    pdl_launch_dependents();
+    pdl_wait_primary();  // x comes from the previous kernel; the planes may still be read by the previous GEMM
     const size_t n4 = (size_t)M * (K / 4);
     const size_t plane = (size_t)M * K;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
@@ -547,8 +553,8 @@ cudaError_t launch_linear_tma_persistent(const LinearArgs& a, const CUtensorMap*
     const int tiles = ((a.M + pers::TM - 1) / pers::TM) * ((a.N + pers::TN - 1) / pers::TN);
     const int grid = tiles < num_sms ? tiles : num_sms;
     if (grid < 1) return cudaSuccess;
-    linear_tma_persistent_kernel<<<grid, pers::THREADS, pers::SMEM_TOTAL, st>>>(*tx, *tw, a, err);
-    return cudaGetLastError();
+    return launch_pdl(linear_tma_persistent_kernel, dim3(grid), dim3(pers::THREADS), pers::SMEM_TOTAL, st, *tx, *tw, a,
+                      err);
 }
 
 // Split-K depth: the largest of 1, 2, 4, 8 that keeps the grid to one wave
@@ -566,8 +572,8 @@ cudaError_t launch_split3(const float* x, int ldx, int M, int K, void* planes, c
     int blocks = (int)((n4 + 255) / 256);
     blocks = blocks < 4096 ? blocks : 4096;
     if (blocks < 1) return cudaSuccess;
-    split3_kernel<<<blocks, 256, 0, st>>>(x, ldx, M, K, static_cast<__nv_bfloat16*>(planes));
-    return cudaGetLastError();
+    return launch_pdl(split3_kernel, dim3(blocks), dim3(256), 0, st, x, ldx, M, K,
+                      static_cast<__nv_bfloat16*>(planes));
 }
 
 cudaError_t launch_int8_to_bf16(const int8_t* w, void* out, size_t n, cudaStream_t st) {
@@ -585,13 +591,15 @@ cudaError_t launch_linear_tma(const LinearArgs& a, const CUtensorMap* tx, const 
     cfg.blockDim = dim3(THREADS, 1, 1);
     cfg.dynamicSmemBytes = SMEM_TOTAL;
     cfg.stream = st;
-    cudaLaunchAttribute attr;
-    attr.id = cudaLaunchAttributeClusterDimension;
-    attr.val.clusterDim.x = (unsigned)splits;
-    attr.val.clusterDim.y = 1;
-    attr.val.clusterDim.z = 1;
-    cfg.attrs = &attr;
-    cfg.numAttrs = 1;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // the kernel waits after its prologue
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, linear_tma_kernel, *tx, *tw, a, splits, err);
 }
 
