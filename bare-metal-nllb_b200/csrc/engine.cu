@@ -226,6 +226,8 @@ struct nllb_model {
     size_t planes_elems = 0;
     std::map<std::pair<int, int>, CUtensorMap> plane_maps;  // key (M, K): split-K kernel
     std::map<std::pair<int, int>, CUtensorMap> plane_maps_pers;  // key (M, K): persistent kernel
+    int* live_h = nullptr;          // pinned [max_gen]: running sentences after each step
+    cudaEvent_t step_ev[4] = {};    // recorded after each step's count copy
     // buffers of translate calls, kept between calls (grow-only, taken in call order)
     std::vector<std::pair<void*, size_t>> work_pool;
     int num_sms = 148;
@@ -334,6 +336,9 @@ void nllb_model_free(nllb_model* m) {
     if (m->planes) cudaFree(m->planes);
     for (auto& b : m->work_pool)
         if (b.first) cudaFree(b.first);
+    for (auto& e : m->step_ev)
+        if (e) cudaEventDestroy(e);
+    if (m->live_h) cudaFreeHost(m->live_h);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
 }
@@ -369,6 +374,12 @@ int nllb_model_load(const char* path, int device, int max_sentences, int max_src
         cudaMemset(m->lws.tile_count, 0, m->lws.n_counters * sizeof(int)) != cudaSuccess)
         return fail(nllb::set_error(NLLB_ATTN_ECUDA, "cannot allocate the linear-layer workspace"));
     nllb_attn_set_stream(attn, m->stream);
+    if (cudaHostAlloc(reinterpret_cast<void**>(&m->live_h), (size_t)max_gen * sizeof(int), cudaHostAllocDefault) !=
+        cudaSuccess)
+        return fail(nllb::set_error(NLLB_ATTN_ECUDA, "cannot allocate pinned host memory"));
+    for (auto& e : m->step_ev)
+        if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess)
+            return fail(nllb::set_error(NLLB_ATTN_ECUDA, "cannot create events"));
 
     const int fd = open(path, O_RDONLY);
     if (fd < 0) return fail(nllb::set_error(NLLB_ATTN_EINVAL, std::string("cannot open ") + path));
@@ -602,10 +613,11 @@ int decode_step(nllb_model* m, Work& w, int step) {
 
 // Tied vocabulary projection with language rows masked (decoder.c:319-354),
 // penalties (main.c:186-213) and log-softmax + top-k (main.c:154-182).
-int vocab_topk(nllb_model* m, Work& w, int k, bool penalties, const nllb_translate_opts& o) {
+int vocab_topk(nllb_model* m, Work& w, int k, bool penalties, const nllb_translate_opts& o,
+               const int* hist = nullptr) {
     ENG_RC(run_linear(m, m->vocab, w.h, w.rows, w.logits, nullptr, 0, VOCAB_LD, LANG_START));
     if (penalties)
-        ENG_CK(launch_penalties(w.logits, VOCAB_LD, w.hist, m->max_gen, w.ntok, w.active, w.rows,
+        ENG_CK(launch_penalties(w.logits, VOCAB_LD, hist ? hist : w.hist, m->max_gen, w.ntok, w.active, w.rows,
                                 o.repetition_penalty, o.no_repeat_ngram, m->stream));
     ENG_CK(launch_logsoftmax_topk(w.logits, VOCAB_LD, VOCAB, w.rows, w.active, k, w.top_tok, w.top_lp, w.topk_ws,
                                   m->stream));
@@ -746,84 +758,135 @@ extern "C" int nllb_translate(nllb_model* m, int n_sent, const int* src_tokens, 
         }
     int steps_run = 2;
 
-    // ---- steps 2 .. max_out+1 (main.c:411-511)
-    for (int step = 2;; ++step) {
-        bool any = false;
+    // ---- steps 2 .. max_out+1 (main.c:411-511): selection on the device (beam.cu),
+    // the host only reads a running-sentence count, at most two steps behind
+    const int GD = m->max_gen;  // row length of the device histories
+    BeamState B{};
+    B.G = GD;
+    B.n_sent = n_sent;
+    B.bt0 = w.hist;
+    B.bn = w.ntok;
+    B.tok = w.tok;
+    B.active = w.active;
+    B.parent = w.parent;
+    int* maxo_d = nullptr;
+    ENG_RC(w.alloc(&B.bt1, R * (size_t)GD));
+    ENG_RC(w.alloc(&B.bsc, R));
+    ENG_RC(w.alloc(&B.beos, R));
+    ENG_RC(w.alloc(&B.bfin, R));
+    ENG_RC(w.alloc(&B.done, (size_t)n_sent));
+    ENG_RC(w.alloc(&maxo_d, (size_t)n_sent));
+    B.maxo = maxo_d;
+    ENG_RC(w.alloc(&B.ctok, (size_t)n_sent * 8 * GD));
+    ENG_RC(w.alloc(&B.cn, (size_t)n_sent * 8));
+    ENG_RC(w.alloc(&B.csc, (size_t)n_sent * 8));
+    ENG_RC(w.alloc(&B.ceos, (size_t)n_sent * 8));
+    ENG_RC(w.alloc(&B.ccnt, (size_t)n_sent));
+    ENG_RC(w.alloc(&B.margins, (size_t)n_sent * GD));
+    ENG_RC(w.alloc(&B.mcnt, (size_t)n_sent));
+    ENG_RC(w.alloc(&B.live, (size_t)GD));
+    {
+        std::vector<float> bsc(R), beos(R, 0.f);
+        std::vector<unsigned char> bfin(R), done_h(n_sent);
+        int live0 = 0;
         for (int s = 0; s < n_sent; ++s) {
-            if (done[s]) continue;
             int n_active = 0;
-            for (int b = 0; b < NB; ++b) n_active += !beams[(size_t)s * NB + b].finished;
-            if (step >= max_out[s] + 2 || n_active == 0) {
-                done[s] = 1;
-                continue;
-            }
-            any = true;
-        }
-        if (!any) break;
-        if (step >= m->max_gen) return nllb::set_error(NLLB_ATTN_ECAPACITY, "decode ran past max_gen");
-        for (int s = 0; s < n_sent; ++s)
             for (int b = 0; b < NB; ++b) {
                 const size_t r = (size_t)s * NB + b;
                 const Beam& bm = beams[r];
-                tok_h[r] = bm.tokens[bm.n - 1];
+                std::copy(bm.tokens.begin(), bm.tokens.begin() + bm.n, hist_h.begin() + r * GD);
                 ntok_h[r] = bm.n;
-                active_h[r] = (!done[s] && !bm.finished) ? 1 : 0;
-                std::copy(bm.tokens.begin(), bm.tokens.begin() + bm.n, hist_h.begin() + r * m->max_gen);
+                tok_h[r] = bm.tokens[bm.n - 1];
+                bsc[r] = bm.score;
+                bfin[r] = bm.finished ? 1 : 0;
+                n_active += !bm.finished;
             }
-        ENG_RC(upload_tokens());
-        ENG_CK(cudaMemcpyAsync(w.ntok, ntok_h.data(), R * sizeof(int), cudaMemcpyHostToDevice, m->stream));
-        ENG_CK(cudaMemcpyAsync(w.active, active_h.data(), R, cudaMemcpyHostToDevice, m->stream));
-        ENG_CK(cudaMemcpyAsync(w.hist, hist_h.data(), hist_h.size() * sizeof(int), cudaMemcpyHostToDevice,
-                               m->stream));
-        ENG_RC(decode_step(m, w, step));
-        ENG_RC(vocab_topk(m, w, 8, true, o));
-        ENG_CK(cudaMemcpyAsync(top_tok_h.data(), w.top_tok, R * 8 * sizeof(int), cudaMemcpyDeviceToHost, m->stream));
-        ENG_CK(cudaMemcpyAsync(top_lp_h.data(), w.top_lp, R * 8 * sizeof(float), cudaMemcpyDeviceToHost, m->stream));
-        ENG_CK(cudaStreamSynchronize(m->stream));
-        ++steps_run;
-
-        // candidate selection per sentence (main.c:413-488)
-        for (int s = 0; s < n_sent; ++s) {
-            Beam* bs = &beams[(size_t)s * NB];
-            if (done[s]) {
-                for (int b = 0; b < NB; ++b) parent_h[(size_t)s * NB + b] = b;
-                continue;
-            }
-            std::vector<Cand> cands;
-            cands.reserve(NB * 8 + NB);
-            for (int b = 0; b < NB; ++b)
-                if (bs[b].finished) cands.push_back({b, 2, bs[b].score});
+            done_h[s] = (2 >= max_out[s] + 2 || n_active == 0) ? 1 : 0;  // main.c:411-412 at step 2
+            live0 += !done_h[s];
             for (int b = 0; b < NB; ++b) {
-                if (bs[b].finished) continue;
                 const size_t r = (size_t)s * NB + b;
-                for (int k = 0; k < 8; ++k) cands.push_back({b, top_tok_h[r * 8 + k], bs[b].score + top_lp_h[r * 8 + k]});
+                active_h[r] = (!done_h[s] && !beams[r].finished) ? 1 : 0;
             }
-            // the reference's exchange sort, descending (main.c:456-460)
-            const int nc = (int)cands.size();
-            for (int i = 0; i < nc - 1; ++i)
-                for (int j = i + 1; j < nc; ++j)
-                    if (cands[j].score > cands[i].score) std::swap(cands[i], cands[j]);
-            float gap = INFINITY;
-            for (int i = 0; i + 1 < std::min(nc, NB + 1); ++i) gap = std::min(gap, cands[i].score - cands[i + 1].score);
-            m->margins[s].push_back(gap);
-            Beam nb[NB];
-            for (int i = 0; i < NB; ++i) {
-                const int par = cands[i].beam;
-                nb[i].tokens = bs[par].tokens;
-                nb[i].n = bs[par].n;
-                nb[i].tokens[nb[i].n++] = cands[i].token;
-                nb[i].score = cands[i].score;
-                nb[i].finished = cands[i].token == 2;
-                nb[i].eos_score = nb[i].finished ? cands[i].score - bs[par].score : bs[par].eos_score;
-                parent_h[(size_t)s * NB + i] = par;
-                if (nb[i].finished && completed[s].size() < (size_t)(2 * NB)) completed[s].push_back(nb[i]);
-            }
-            for (int i = 0; i < NB; ++i) bs[i] = nb[i];
         }
-        ENG_CK(cudaMemcpyAsync(w.parent, parent_h.data(), R * sizeof(int), cudaMemcpyHostToDevice, m->stream));
+        ENG_CK(cudaMemcpyAsync(B.bt0, hist_h.data(), R * (size_t)GD * sizeof(int), cudaMemcpyHostToDevice, m->stream));
+        ENG_CK(cudaMemcpyAsync(B.bn, ntok_h.data(), R * sizeof(int), cudaMemcpyHostToDevice, m->stream));
+        ENG_CK(cudaMemcpyAsync(B.tok, tok_h.data(), R * sizeof(int), cudaMemcpyHostToDevice, m->stream));
+        ENG_CK(cudaMemcpyAsync(B.bsc, bsc.data(), R * sizeof(float), cudaMemcpyHostToDevice, m->stream));
+        ENG_CK(cudaMemcpyAsync(B.beos, beos.data(), R * sizeof(float), cudaMemcpyHostToDevice, m->stream));
+        ENG_CK(cudaMemcpyAsync(B.bfin, bfin.data(), R, cudaMemcpyHostToDevice, m->stream));
+        ENG_CK(cudaMemcpyAsync(B.active, active_h.data(), R, cudaMemcpyHostToDevice, m->stream));
+        ENG_CK(cudaMemcpyAsync(B.done, done_h.data(), n_sent, cudaMemcpyHostToDevice, m->stream));
+        ENG_CK(cudaMemcpyAsync(maxo_d, max_out.data(), n_sent * sizeof(int), cudaMemcpyHostToDevice, m->stream));
+        ENG_CK(cudaMemsetAsync(B.ccnt, 0, n_sent * sizeof(int), m->stream));
+        ENG_CK(cudaMemsetAsync(B.mcnt, 0, n_sent * sizeof(int), m->stream));
+        ENG_CK(cudaMemsetAsync(B.live, 0, GD * sizeof(int), m->stream));
+        ENG_CK(cudaStreamSynchronize(m->stream));  // host vectors above go out of scope
+        steps_run += live0 > 0;
+        if (live0 == 0) max_out.assign(n_sent, 0);  // nothing to run
+    }
+    int last_step = 1;
+    for (int s = 0; s < n_sent; ++s) last_step = std::max(last_step, max_out[s] + 1);
+    if (last_step >= m->max_gen) return nllb::set_error(NLLB_ATTN_ECAPACITY, "decode would run past max_gen");
+    int cur = 0, launched_to = 1;
+    for (int step = 2; step <= last_step; ++step) {
+        if (step >= 4) {  // two steps of lookahead: the count of step - 2 decides whether to go on
+            ENG_CK(cudaEventSynchronize(m->step_ev[(step - 2) & 3]));
+            if (m->live_h[step - 2] == 0) break;
+        }
+        ENG_RC(decode_step(m, w, step));
+        ENG_RC(vocab_topk(m, w, 8, true, o, cur ? B.bt1 : B.bt0));
+        ENG_CK(launch_beam_select(B, cur, w.top_tok, w.top_lp, step, m->stream));
+        ENG_CK(cudaMemcpyAsync(m->live_h + step, B.live + step, sizeof(int), cudaMemcpyDeviceToHost, m->stream));
+        ENG_CK(cudaEventRecord(m->step_ev[step & 3], m->stream));
         ENG_RC(nllb_attn_reorder(m->attn, n_sent, w.parent));
+        cur ^= 1;
+        launched_to = step;
     }
     ENG_RC(nllb_attn_sync(m->attn));
+    for (int t = 3; t <= launched_to; ++t) steps_run += m->live_h[t - 1] > 0;
+
+    // ---- device beam state back to the host structures of the final choice
+    {
+        std::vector<int> bt(R * (size_t)GD), bn(R), cn((size_t)n_sent * 8), ccnt(n_sent), mcnt(n_sent);
+        std::vector<int> ct((size_t)n_sent * 8 * GD);
+        std::vector<float> bsc(R), beos(R), csc((size_t)n_sent * 8), ceos((size_t)n_sent * 8);
+        std::vector<float> marg((size_t)n_sent * GD);
+        std::vector<unsigned char> bfin(R);
+        ENG_CK(cudaMemcpy(bt.data(), cur ? B.bt1 : B.bt0, bt.size() * sizeof(int), cudaMemcpyDeviceToHost));
+        ENG_CK(cudaMemcpy(bn.data(), B.bn, R * sizeof(int), cudaMemcpyDeviceToHost));
+        ENG_CK(cudaMemcpy(bsc.data(), B.bsc, R * sizeof(float), cudaMemcpyDeviceToHost));
+        ENG_CK(cudaMemcpy(beos.data(), B.beos, R * sizeof(float), cudaMemcpyDeviceToHost));
+        ENG_CK(cudaMemcpy(bfin.data(), B.bfin, R, cudaMemcpyDeviceToHost));
+        ENG_CK(cudaMemcpy(ct.data(), B.ctok, ct.size() * sizeof(int), cudaMemcpyDeviceToHost));
+        ENG_CK(cudaMemcpy(cn.data(), B.cn, cn.size() * sizeof(int), cudaMemcpyDeviceToHost));
+        ENG_CK(cudaMemcpy(csc.data(), B.csc, csc.size() * sizeof(float), cudaMemcpyDeviceToHost));
+        ENG_CK(cudaMemcpy(ceos.data(), B.ceos, ceos.size() * sizeof(float), cudaMemcpyDeviceToHost));
+        ENG_CK(cudaMemcpy(ccnt.data(), B.ccnt, n_sent * sizeof(int), cudaMemcpyDeviceToHost));
+        ENG_CK(cudaMemcpy(marg.data(), B.margins, marg.size() * sizeof(float), cudaMemcpyDeviceToHost));
+        ENG_CK(cudaMemcpy(mcnt.data(), B.mcnt, n_sent * sizeof(int), cudaMemcpyDeviceToHost));
+        for (int s = 0; s < n_sent; ++s) {
+            for (int b = 0; b < NB; ++b) {
+                const size_t r = (size_t)s * NB + b;
+                Beam& bm = beams[r];
+                bm.n = bn[r];
+                std::copy(bt.begin() + r * GD, bt.begin() + r * GD + bm.n, bm.tokens.begin());
+                bm.score = bsc[r];
+                bm.eos_score = beos[r];
+                bm.finished = bfin[r] != 0;
+            }
+            for (int c = 0; c < ccnt[s]; ++c) {
+                const size_t k = (size_t)s * 8 + c;
+                Beam hb;
+                hb.n = cn[k];
+                hb.tokens.assign(ct.begin() + k * GD, ct.begin() + k * GD + GD);
+                hb.score = csc[k];
+                hb.eos_score = ceos[k];
+                hb.finished = true;
+                completed[s].push_back(hb);
+            }
+            m->margins[s].assign(marg.begin() + (size_t)s * GD, marg.begin() + (size_t)s * GD + mcnt[s]);
+        }
+    }
     const double t_dec = ms_since(t_dec0);
 
     // ---- final choice (main.c:511-546)

@@ -78,4 +78,31 @@ cudaError_t launch_set_memory_batched(float* km, float* vm, int* n_src_slots, in
                                       int max_n, cudaStream_t st);
 cudaError_t launch_reciprocal(float* out, const float* in, size_t n, cudaStream_t st);
 
+// Beam-search state of a translate call on the device (4 beams per sentence,
+// G = positions per beam), updated by launch_beam_select after every step.
+struct BeamState {
+    int* bt0;                // [rows][G] token histories, two buffers: step parity `cur` reads
+    int* bt1;                //   bt0 (cur 0) or bt1 (cur 1) and writes the other
+    int* bn;                 // [rows] tokens per beam
+    float* bsc;              // [rows] beam score
+    float* beos;             // [rows] score at the step that emitted token 2
+    unsigned char* bfin;     // [rows] finished
+    unsigned char* done;     // [sentences] no further step
+    const int* maxo;         // [sentences] max_out (main.c:315-316)
+    int* ctok;               // [sentences][8][G] completed hypotheses
+    int* cn;                 // [sentences][8]
+    float* csc;              // [sentences][8]
+    float* ceos;             // [sentences][8]
+    int* ccnt;               // [sentences]
+    float* margins;          // [sentences][G] smallest gap among the best 5 candidates, per step
+    int* mcnt;               // [sentences]
+    int* tok;                // [rows] last token (next step's input)
+    unsigned char* active;   // [rows] unfinished beam of a running sentence
+    int* parent;             // [rows] parent beam of each new beam
+    int* live;               // [G] running sentences after each step (zeroed before the loop)
+    int G, n_sent;
+};
+cudaError_t launch_beam_select(const BeamState& b, int cur, const int* top_tok, const float* top_lp, int step,
+                               cudaStream_t st);
+
 }  // namespace nllb
