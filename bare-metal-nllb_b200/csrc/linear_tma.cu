@@ -557,13 +557,47 @@ cudaError_t launch_linear_tma_persistent(const LinearArgs& a, const CUtensorMap*
                       err);
 }
 
-// Split-K depth: the largest of 1, 2, 4, 8 that keeps the grid to one wave
-// (one CTA per SM) and every CTA at least two K chunks.
+// Clusters of S CTAs of the split-K kernel that can be resident at once on the
+// current device (thread-block clusters must fit inside one GPC, so this is
+// below num_sms / S for large S).  Queried once per device and S.
+int cluster_capacity(int S) {
+    static std::mutex mu;
+    static int cap[64][4] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    const int idx = S == 2 ? 1 : S == 4 ? 2 : S == 8 ? 3 : 0;
+    std::lock_guard<std::mutex> lock(mu);
+    if (cap[dev][idx] == 0) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(S, 1, 1);
+        cfg.blockDim = dim3(THREADS, 1, 1);
+        cfg.dynamicSmemBytes = SMEM_TOTAL;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = (unsigned)S;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, linear_tma_kernel, &cfg) != cudaSuccess || n < 1) {
+            cudaGetLastError();  // clear
+            n = -1;
+        }
+        cap[dev][idx] = n;
+    }
+    return cap[dev][idx];
+}
+
+// Split-K depth: the largest of 1, 2, 4, 8 whose clusters all fit on the GPU
+// at once (one wave) with every CTA keeping at least two K chunks.  Measured
+// on B200: 16 tiles run 17 us as 16 clusters of 8 (more than one wave) and
+// 11 us as 16 clusters of 4; 8 tiles run fastest as 8 clusters of 8.
 int linear_tma_splits(int M, int N, int K, int num_sms) {
     const int tiles = ((N + TN - 1) / TN) * ((M + TM - 1) / TM);
     const int nk = K / TK;
     int S = 1;
-    while (S < 8 && tiles * 2 * S <= num_sms && nk / (2 * S) >= 2) S *= 2;
+    while (S < 8 && tiles * 2 * S <= num_sms && nk / (2 * S) >= 2 && tiles <= cluster_capacity(2 * S)) S *= 2;
     return S;
 }
 
