@@ -15,6 +15,7 @@
 #include <cstdio>
 #include <cstring>
 #include <map>
+#include <tuple>
 #include <string>
 #include <vector>
 
@@ -222,10 +223,12 @@ struct nllb_model {
     Lin vocab;            // tied output projection: the shared embedding (decoder.c:319-354)
     // activations split into bf16 planes for the TMA-fed linear kernel ([3][M][K]),
     // grow-only, with its tensor maps per (M, K)
+    // (two buffers: a GEMM that writes planes for the next one reads the other)
     void* planes = nullptr;
+    void* planes2 = nullptr;
     size_t planes_elems = 0;
-    std::map<std::pair<int, int>, CUtensorMap> plane_maps;  // key (M, K): split-K kernel
-    std::map<std::pair<int, int>, CUtensorMap> plane_maps_pers;  // key (M, K): persistent kernel
+    // tensor maps of the plane buffers, key (buffer, M, K, persistent kernel)
+    std::map<std::tuple<const void*, int, int, bool>, CUtensorMap> plane_maps;
     int* live_h = nullptr;          // pinned [max_gen]: running sentences after each step
     cudaEvent_t step_ev[4] = {};    // recorded after each step's count copy
     // buffers of translate calls, kept between calls (grow-only, taken in call order)
@@ -334,6 +337,7 @@ void nllb_model_free(nllb_model* m) {
     if (m->attn) nllb_attn_destroy(m->attn);
     for (void* p : m->allocs) cudaFree(p);
     if (m->planes) cudaFree(m->planes);
+    if (m->planes2) cudaFree(m->planes2);
     for (auto& b : m->work_pool)
         if (b.first) cudaFree(b.first);
     for (auto& e : m->step_ev)
@@ -455,8 +459,19 @@ int nllb_model_load(const char* path, int device, int max_sentences, int max_src
 
 namespace {
 
+// The TMA-fed tensor-core kernels take more than 16 rows (fewer go to the
+// weight-streaming kernel over the int8 matrix).
+bool tma_path(const nllb_model* m, const Lin& L, int M) {
+    return M > 16 && L.wb && (size_t)M * L.in * 3 <= m->planes_elems;
+}
+
+// out = x W^T / scale + bias (+ relu, + residual).  On the tensor-core path
+// the activations are read as bf16 planes: in_planes when the producer wrote
+// them already (LayerNorm, the previous GEMM), else x is split into
+// m->planes first; with out_planes the result is written as planes for the
+// next GEMM instead of to out.
 int run_linear(nllb_model* m, const Lin& L, const float* x, int M, float* out, const float* residual, int relu,
-               int cblock, int mask_from = -1) {
+               int cblock, int mask_from = -1, const void* in_planes = nullptr, void* out_planes = nullptr) {
     LinearArgs a;
     a.x = x;
     a.ldx = L.in;
@@ -472,29 +487,33 @@ int run_linear(nllb_model* m, const Lin& L, const float* x, int M, float* out, c
     a.relu = relu;
     a.mask_from = mask_from;
     a.static_weights = 1;  // the model's own weights, written at load
-    if (M > 16 && L.wb && (size_t)M * L.in * 3 <= m->planes_elems) {
-        // x -> three bf16 planes, then the TMA-fed tensor-core GEMM
-        ENG_CK(launch_split3(x, L.in, M, L.in, m->planes, m->stream));
-        if (linear_tma_use_persistent(M, L.out, L.in, m->num_sms)) {
-            auto ip = m->plane_maps_pers.find({M, L.in});
-            if (ip == m->plane_maps_pers.end()) {
-                CUtensorMap tx;
-                ENG_CK(encode_bf16_maps_persistent(&tx, m->planes, L.in, M, nullptr, nullptr, 0));
-                ip = m->plane_maps_pers.emplace(std::make_pair(M, L.in), tx).first;
-            }
-            ENG_CK(launch_linear_tma_persistent(a, &ip->second, &L.tm256, m->num_sms, m->attn->err, m->stream));
-            return NLLB_ATTN_OK;
+    a.out_planes = out_planes;
+    if (tma_path(m, L, M)) {
+        if (out_planes && (cblock != L.out || residual))
+            return nllb::set_error(NLLB_ATTN_EINVAL, "plane output needs a plain row-major result");
+        if (!in_planes) {
+            ENG_CK(launch_split3(x, L.in, M, L.in, m->planes, m->stream));
+            in_planes = m->planes;
         }
-        auto it = m->plane_maps.find({M, L.in});
+        const bool pers = linear_tma_use_persistent(M, L.out, L.in, m->num_sms);
+        const auto key = std::make_tuple(in_planes, M, L.in, pers);
+        auto it = m->plane_maps.find(key);
         if (it == m->plane_maps.end()) {
             CUtensorMap tx;
-            ENG_CK(encode_bf16_map(&tx, m->planes, L.in, M, 3));
-            it = m->plane_maps.emplace(std::make_pair(M, L.in), tx).first;
+            if (pers)
+                ENG_CK(encode_bf16_maps_persistent(&tx, in_planes, L.in, M, nullptr, nullptr, 0));
+            else
+                ENG_CK(encode_bf16_map(&tx, in_planes, L.in, M, 3));
+            it = m->plane_maps.emplace(key, tx).first;
         }
-        const int splits = linear_tma_splits(M, L.out, L.in, m->num_sms);
-        ENG_CK(launch_linear_tma(a, &it->second, &L.tm, splits, m->attn->err, m->stream));
+        if (pers)
+            ENG_CK(launch_linear_tma_persistent(a, &it->second, &L.tm256, m->num_sms, m->attn->err, m->stream));
+        else
+            ENG_CK(launch_linear_tma(a, &it->second, &L.tm, linear_tma_splits(M, L.out, L.in, m->num_sms),
+                                     m->attn->err, m->stream));
         return NLLB_ATTN_OK;
     }
+    if (in_planes || out_planes) return nllb::set_error(NLLB_ATTN_EINVAL, "planes need the tensor-core path");
     ENG_CK(launch_linear(a, &m->lws, m->num_sms, m->attn->err, m->stream));
     return NLLB_ATTN_OK;
 }
@@ -504,11 +523,12 @@ int ensure_planes(nllb_model* m, size_t elems) {
     if (elems <= m->planes_elems) return NLLB_ATTN_OK;
     ENG_CK(cudaStreamSynchronize(m->stream));
     if (m->planes) cudaFree(m->planes);
-    m->planes = nullptr;
+    if (m->planes2) cudaFree(m->planes2);
+    m->planes = m->planes2 = nullptr;
     m->planes_elems = 0;
     m->plane_maps.clear();
-    m->plane_maps_pers.clear();
     ENG_CK(cudaMalloc(&m->planes, elems * sizeof(__nv_bfloat16)));
+    ENG_CK(cudaMalloc(&m->planes2, elems * sizeof(__nv_bfloat16)));
     m->planes_elems = elems;
     return NLLB_ATTN_OK;
 }
@@ -548,10 +568,16 @@ struct Work {
 int encode(nllb_model* m, Work& w, const std::vector<int>& n_src) {
     const int R = w.rows_enc;
     ENG_CK(launch_embed_pos(w.ex, w.etok, w.epos, 0, m->emb, m->emb_inv, m->pos_table, 32.0f, R, VOCAB, m->stream));
+    // LayerNorm writes the bf16 planes of the next GEMM's input directly when
+    // that GEMM runs on the tensor cores, fc1 writes fc2's input planes
+    const bool tp = tma_path(m, m->enc[0].qkv, R);
+    void* P1 = tp ? m->planes : nullptr;
+    void* P2 = tp ? m->planes2 : nullptr;
+    float* lnout = tp ? nullptr : w.eh;
     for (int l = 0; l < LAYERS; ++l) {
         auto& E = m->enc[l];
-        ENG_CK(launch_layernorm(w.eh, w.ex, nullptr, E.ln1g, E.ln1b, R, m->stream));
-        ENG_RC(run_linear(m, E.qkv, w.eh, R, w.eqkv, nullptr, 0, D));
+        ENG_CK(launch_layernorm(lnout, w.ex, nullptr, E.ln1g, E.ln1b, R, P1, m->stream));
+        ENG_RC(run_linear(m, E.qkv, w.eh, R, w.eqkv, nullptr, 0, D, -1, P1));
         nllb_attn_prefill_args a{};
         a.q = w.eqkv;
         a.k = w.eqkv + (size_t)R * D;
@@ -568,16 +594,16 @@ int encode(nllb_model* m, Work& w, const std::vector<int>& n_src) {
         a.scale = 1.0f / sqrtf(64.0f);
         ENG_RC(nllb_attn_prefill(m->attn, &a));
         ENG_RC(run_linear(m, E.out, w.eattn, R, w.ex, w.ex, 0, D));
-        ENG_CK(launch_layernorm(w.eh, w.ex, nullptr, E.ln2g, E.ln2b, R, m->stream));
-        ENG_RC(run_linear(m, E.fc1, w.eh, R, w.effn, nullptr, 1, FFN));
-        ENG_RC(run_linear(m, E.fc2, w.effn, R, w.ex, w.ex, 0, D));
+        ENG_CK(launch_layernorm(lnout, w.ex, nullptr, E.ln2g, E.ln2b, R, P1, m->stream));
+        ENG_RC(run_linear(m, E.fc1, w.eh, R, w.effn, nullptr, 1, FFN, -1, P1, P2));
+        ENG_RC(run_linear(m, E.fc2, w.effn, R, w.ex, w.ex, 0, D, -1, P2));
     }
-    ENG_CK(launch_layernorm(w.eh, w.ex, nullptr, m->enc_lng, m->enc_lnb, R, m->stream));  // encoder_out
+    ENG_CK(launch_layernorm(lnout, w.ex, nullptr, m->enc_lng, m->enc_lnb, R, P1, m->stream));  // encoder_out
     // cross-attention memory of every layer (decoder.c:118-125, projected once)
     nllb_attn_ctx* c = m->attn;
     const size_t layer_floats = (size_t)c->d.max_sentences * H * (size_t)c->d.max_src * 64;
     for (int l = 0; l < LAYERS; ++l) {
-        ENG_RC(run_linear(m, m->dec[l].xkv, w.eh, R, w.ekv, nullptr, 0, D));
+        ENG_RC(run_linear(m, m->dec[l].xkv, w.eh, R, w.ekv, nullptr, 0, D, -1, P1));
         ENG_CK(launch_set_memory_batched(c->km + l * layer_floats, c->vm + l * layer_floats,
                                          c->n_src_dev + (size_t)l * c->d.max_sentences, c->d.max_src, H, w.ekv,
                                          w.ekv + (size_t)R * D, (long long)w.S * D, w.evalid, w.n_sent, w.S,
@@ -592,22 +618,26 @@ int encode(nllb_model* m, Work& w, const std::vector<int>& n_src) {
 int decode_step(nllb_model* m, Work& w, int step) {
     const int R = w.rows;
     ENG_CK(launch_embed_pos(w.x, w.tok, nullptr, step + 2, m->emb, m->emb_inv, m->pos_table, 32.0f, R, VOCAB, m->stream));
+    const bool tp = tma_path(m, m->dec[0].qkv, R);
+    void* P1 = tp ? m->planes : nullptr;
+    void* P2 = tp ? m->planes2 : nullptr;
+    float* lnout = tp ? nullptr : w.h;
     for (int l = 0; l < LAYERS; ++l) {
         auto& Dl = m->dec[l];
-        ENG_CK(launch_layernorm(w.h, w.x, nullptr, Dl.ln1g, Dl.ln1b, R, m->stream));
-        ENG_RC(run_linear(m, Dl.qkv, w.h, R, w.qkv, nullptr, 0, D));
+        ENG_CK(launch_layernorm(lnout, w.x, nullptr, Dl.ln1g, Dl.ln1b, R, P1, m->stream));
+        ENG_RC(run_linear(m, Dl.qkv, w.h, R, w.qkv, nullptr, 0, D, -1, P1));
         ENG_RC(nllb_attn_decode_self(m->attn, l, step, w.n_sent, w.qkv, w.qkv + (size_t)R * D,
                                      w.qkv + (size_t)2 * R * D, w.attn));
         ENG_RC(run_linear(m, Dl.out, w.attn, R, w.x, w.x, 0, D));
-        ENG_CK(launch_layernorm(w.h, w.x, nullptr, Dl.ln2g, Dl.ln2b, R, m->stream));
-        ENG_RC(run_linear(m, Dl.xq, w.h, R, w.qx, nullptr, 0, D));
+        ENG_CK(launch_layernorm(lnout, w.x, nullptr, Dl.ln2g, Dl.ln2b, R, P1, m->stream));
+        ENG_RC(run_linear(m, Dl.xq, w.h, R, w.qx, nullptr, 0, D, -1, P1));
         ENG_RC(nllb_attn_cross(m->attn, l, w.n_sent, w.qx, w.attn));
         ENG_RC(run_linear(m, Dl.xout, w.attn, R, w.x, w.x, 0, D));
-        ENG_CK(launch_layernorm(w.h, w.x, nullptr, Dl.ln3g, Dl.ln3b, R, m->stream));
-        ENG_RC(run_linear(m, Dl.fc1, w.h, R, w.ffn, nullptr, 1, FFN));
-        ENG_RC(run_linear(m, Dl.fc2, w.ffn, R, w.x, w.x, 0, D));
+        ENG_CK(launch_layernorm(lnout, w.x, nullptr, Dl.ln3g, Dl.ln3b, R, P1, m->stream));
+        ENG_RC(run_linear(m, Dl.fc1, w.h, R, w.ffn, nullptr, 1, FFN, -1, P1, P2));
+        ENG_RC(run_linear(m, Dl.fc2, w.ffn, R, w.x, w.x, 0, D, -1, P2));
     }
-    ENG_CK(launch_layernorm(w.h, w.x, nullptr, m->dec_lng, m->dec_lnb, R, m->stream));
+    ENG_CK(launch_layernorm(lnout, w.x, nullptr, m->dec_lng, m->dec_lnb, R, P1, m->stream));
     return NLLB_ATTN_OK;
 }
 
@@ -615,7 +645,8 @@ int decode_step(nllb_model* m, Work& w, int step) {
 // penalties (main.c:186-213) and log-softmax + top-k (main.c:154-182).
 int vocab_topk(nllb_model* m, Work& w, int k, bool penalties, const nllb_translate_opts& o,
                const int* hist = nullptr) {
-    ENG_RC(run_linear(m, m->vocab, w.h, w.rows, w.logits, nullptr, 0, VOCAB_LD, LANG_START));
+    const bool tp = tma_path(m, m->vocab, w.rows);  // the final LayerNorm left the planes of h
+    ENG_RC(run_linear(m, m->vocab, w.h, w.rows, w.logits, nullptr, 0, VOCAB_LD, LANG_START, tp ? m->planes : nullptr));
     if (penalties)
         ENG_CK(launch_penalties(w.logits, VOCAB_LD, hist ? hist : w.hist, m->max_gen, w.ntok, w.active, w.rows,
                                 o.repetition_penalty, o.no_repeat_ngram, m->stream));
@@ -959,6 +990,7 @@ extern "C" int nllb_linear_int8(const float* x, int M, int K, const int8_t* w, c
     a.relu = (flags & NLLB_LINEAR_RELU) ? 1 : 0;
     a.mask_from = -1;
     a.static_weights = 0;
+    a.out_planes = nullptr;
     // bounded-wait error word of the current device for callers without a context
     static int* err_words[64] = {nullptr};
     int dev = 0;

@@ -22,13 +22,16 @@ struct LinearArgs {
     int mask_from;           // columns >= mask_from are set to -1e30 (-1: none)
     int static_weights;      // 1: w, scale, bias are not written by earlier kernels of the stream
                              // (a kernel may fetch them before waiting for its predecessor)
+    void* out_planes;        // TMA kernels only: write bf16 planes [3][M][N] (split3 of the result)
+                             // instead of out; requires cblock == N and no residual
 };
 
 cudaError_t launch_embed_pos(float* x, const int* tokens, const int* positions, int pos_const, const int8_t* emb,
                              const float* emb_inv_scale, const float* pos_table, float embed_scale, int rows,
                              int vocab, cudaStream_t st);
+// out (fp32, may be null) and/or planes (bf16 [3][rows][1024], may be null)
 cudaError_t launch_layernorm(float* out, float* x, const float* res, const float* gamma, const float* beta,
-                             int rows, cudaStream_t st);
+                             int rows, void* planes, cudaStream_t st);
 // Split-K workspace of the tensor-core linear kernel: partial tiles and one
 // arrival counter per output tile (zero between calls).
 struct LinearWorkspace {

@@ -102,6 +102,7 @@ extern "C" int nllb_linear_int8_noalloc(const float* x, int M, int K, const int8
     a.relu = (flags & NLLB_LINEAR_RELU) ? 1 : 0;
     a.mask_from = -1;
     a.static_weights = 0;
+    a.out_planes = nullptr;
 
     cudaError_t e = cudaMemsetAsync(counters, 0, (kCounters + 1) * sizeof(int), st);
     if (e != cudaSuccess) return nllb::set_error(NLLB_ATTN_ECUDA, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));

@@ -123,6 +123,7 @@ int nllb_linear_run(nllb_linear* L, const float* x, int M, float* out, const flo
     a.relu = (flags & NLLB_LINEAR_RELU) ? 1 : 0;
     a.mask_from = -1;
     a.static_weights = 0;
+    a.out_planes = nullptr;
     if (M <= 16) {
         LP_CK(launch_linear(a, nullptr, L->num_sms, L->err, st));
         return NLLB_ATTN_OK;

@@ -25,6 +25,7 @@
 
 #include "device_common.cuh"
 #include "engine_kernels.h"
+#include "planes.cuh"
 
 namespace nllb {
 
@@ -74,7 +75,10 @@ __device__ __forceinline__ void epilogue_store(const LinearArgs& a, int m, int n
     if (a.mask_from >= 0 && n >= a.mask_from) y = -1e30f;
     const size_t o = (size_t)(n / a.cblock) * ((size_t)a.M * a.cblock) + (size_t)m * a.cblock + (n % a.cblock);
     if (a.residual) y += a.residual[o];
-    a.out[o] = y;
+    if (a.out_planes)
+        store_split3_x1(static_cast<__nv_bfloat16*>(a.out_planes), (size_t)a.M * a.N, o, y);
+    else
+        a.out[o] = y;
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -226,7 +230,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                         const float4 r = *reinterpret_cast<const float4*>(a.residual + o);
                         y[0] += r.x, y[1] += r.y, y[2] += r.z, y[3] += r.w;
                     }
-                    *reinterpret_cast<float4*>(a.out + o) = make_float4(y[0], y[1], y[2], y[3]);
+                    if (a.out_planes)
+                        store_split3_x4(static_cast<__nv_bfloat16*>(a.out_planes), (size_t)a.M * a.N, o,
+                                        make_float4(y[0], y[1], y[2], y[3]));
+                    else
+                        *reinterpret_cast<float4*>(a.out + o) = make_float4(y[0], y[1], y[2], y[3]);
                 } else {
 #pragma unroll
                     for (int j = 0; j < 4; ++j)
@@ -439,7 +447,10 @@ __global__ void __launch_bounds__(pers::THREADS, 1)
                         if (masked) y = -1e30f;
                         const size_t o = colbase + (size_t)(mrow + r) * a.cblock;
                         if (a.residual) y += a.residual[o];
-                        a.out[o] = y;
+                        if (a.out_planes)
+                            store_split3_x1(static_cast<__nv_bfloat16*>(a.out_planes), (size_t)a.M * a.N, o, y);
+                        else
+                            a.out[o] = y;
                     }
                 }
                 __syncwarp();
@@ -467,18 +478,7 @@ __global__ void split3_kernel(const float* x, int ldx, int M, int K, __nv_bfloat
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
         const int m = (int)(i / (K / 4)), k = (int)(i % (K / 4)) * 4;
         const float4 v = *reinterpret_cast<const float4*>(x + (size_t)m * ldx + k);
-        const float f[4] = {v.x, v.y, v.z, v.w};
-        __nv_bfloat16 p[3][4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            p[0][e] = __float2bfloat16_rn(f[e]);
-            const float r1 = f[e] - __bfloat162float(p[0][e]);
-            p[1][e] = __float2bfloat16_rn(r1);
-            p[2][e] = __float2bfloat16_rn(r1 - __bfloat162float(p[1][e]));
-        }
-        const size_t o = (size_t)m * K + k;
-#pragma unroll
-        for (int q = 0; q < 3; ++q) *reinterpret_cast<uint2*>(planes + q * plane + o) = *reinterpret_cast<const uint2*>(p[q]);
+        store_split3_x4(planes, plane, (size_t)m * K + k, v);
     }
 }
 
