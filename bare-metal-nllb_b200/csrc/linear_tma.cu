@@ -540,12 +540,15 @@ cudaError_t encode_bf16_maps_persistent(CUtensorMap* x_map, const void* planes, 
 }
 
 // The persistent kernel runs each 128 x 256 tile's whole K loop in one CTA;
-// the split-K kernel spreads a tile's K over up to 8 CTAs.  Measured on
-// B200 over M 256..16384, N 1024..256206, K 1024..4096: the persistent
-// kernel wins once there are at least 20 tiles per 1024 of K (for 148 SMs).
+// the split-K kernel spreads a 128 x 128 tile's K over a cluster of up to 8
+// CTAs.  Measured on B200 over M 256..4096, N 1024..4096, K 1024 / 4096
+// (split depth as linear_tma_splits picks it): the persistent kernel wins from
+// about 96 tiles of 128 x 256 up (1024 x 1024 -> 3072: 28 us against 36) and
+// loses below 64 (512 x 1024 -> 3072: 27 us against 20), whatever K.
 bool linear_tma_use_persistent(int M, int N, int K, int num_sms) {
+    (void)K;
     const long long tiles = (long long)((M + pers::TM - 1) / pers::TM) * ((N + pers::TN - 1) / pers::TN);
-    return tiles * 1024 * 148 >= 20LL * K * num_sms;
+    return tiles * 148 >= 80LL * num_sms;
 }
 
 cudaError_t launch_linear_tma_persistent(const LinearArgs& a, const CUtensorMap* tx, const CUtensorMap* tw,

@@ -58,8 +58,8 @@ def _dev(a, device):
     (300, 4096, 1024, "residual"),     # 4 CTAs per tile, M tail
     (1024, 4096, 1024, "bias_relu"),   # 2 CTAs per tile
     (2048, 4096, 1024, "plain"),       # no split (plain launch, no cluster)
-    # persistent kernel (128 x 256 tiles)
-    (2048, 1024, 1024, "plain"),
+    (2048, 1024, 1024, "residual"),    # no split, K = 1024
+    # persistent kernel (at least 80 tiles of 128 x 256)
     (4100, 1024, 4096, "bias_relu"),   # M tail
     (40, 1024, 256206, "plain"),       # vocabulary projection shape, N tail
     (2000, 1024, 3001, "residual"),    # M and N tails, N % 4 != 0
