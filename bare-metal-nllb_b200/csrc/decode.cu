@@ -524,7 +524,7 @@ cudaError_t launch_ex(void (*kernel)(Params), dim3 grid, size_t smem, int cluste
     cudaLaunchAttribute attrs[2];
     int n = 0;
     attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attrs[n].val.programmaticStreamSerializationAllowed = 1;
+    attrs[n].val.programmaticStreamSerializationAllowed = kPdlLaunch;
     ++n;
     if (cluster_x > 1) {
         attrs[n].id = cudaLaunchAttributeClusterDimension;
@@ -604,7 +604,7 @@ cudaError_t launch_reorder(uint8_t* hist, int Tp, const int* parent, int n_sent,
     cfg.stream = st;
     cudaLaunchAttribute attr;
     attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr.val.programmaticStreamSerializationAllowed = 1;
+    attr.val.programmaticStreamSerializationAllowed = kPdlLaunch;
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, reorder_kernel, hist, Tp, parent, n_beams, err);

@@ -164,6 +164,15 @@ __device__ __forceinline__ void pdl_wait_primary() {
     asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
+// Programmatic dependent launch for every kernel of the library (builds for
+// per-kernel timing set NLLB_NO_PDL: each kernel then waits for the full
+// completion of its predecessor, so profiler durations do not overlap).
+#ifdef NLLB_NO_PDL
+constexpr int kPdlLaunch = 0;
+#else
+constexpr int kPdlLaunch = 1;
+#endif
+
 // Launch with programmatic stream serialisation: the kernel may be scheduled
 // while its predecessor in the stream finishes (once every predecessor CTA has
 // started or triggered); it must execute pdl_wait_primary() before reading the
@@ -180,7 +189,7 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
     cfg.stream = st;
     cudaLaunchAttribute attr;
     attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr.val.programmaticStreamSerializationAllowed = 1;
+    attr.val.programmaticStreamSerializationAllowed = kPdlLaunch;
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);

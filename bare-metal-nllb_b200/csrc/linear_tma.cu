@@ -634,7 +634,7 @@ cudaError_t launch_linear_tma(const LinearArgs& a, const CUtensorMap* tx, const 
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // the kernel waits after its prologue
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].val.programmaticStreamSerializationAllowed = kPdlLaunch;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, linear_tma_kernel, *tx, *tw, a, splits, err);

@@ -480,7 +480,7 @@ cudaError_t launch_prefill(const PrefillParams& p, cudaStream_t st) {
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr;
     attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr.val.programmaticStreamSerializationAllowed = 1;
+    attr.val.programmaticStreamSerializationAllowed = kPdlLaunch;
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
     cfg.stream = st;
