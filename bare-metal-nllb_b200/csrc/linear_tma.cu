@@ -60,6 +60,10 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         : "memory");
 }
 
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
@@ -113,16 +117,38 @@ __global__ void __launch_bounds__(THREADS, 1)
         *s_abort = 0;
     }
     pdl_launch_dependents();
-    pdl_wait_primary();  // the planes come from the previous kernel; the output may still be read by earlier ones
-    if (tid < TN) s_inv[tid] = (n0 + tid < a.N) ? 1.0f / a.scale[n0 + tid] : 0.f;  // 1/scale as tensor.c:75
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    const bool producer = warp == EPI_WARPS && lane == 0;
+    if (!producer) {
+        pdl_wait_primary();  // the output may still be read by earlier kernels
+        if (tid < TN) s_inv[tid] = (n0 + tid < a.N) ? 1.0f / a.scale[n0 + tid] : 0.f;  // 1/scale as tensor.c:75
+    }
 
-    if (warp == EPI_WARPS && lane == 0) {
-        // ---- TMA producer
-        for (int c = 0; c < nk; ++c) {
+    if (producer) {
+        // ---- TMA producer.  The model's weights do not depend on earlier
+        // kernels: the first stages' weight tiles go out before waiting for
+        // the previous kernel, whose output (the planes) is loaded after.
+        prefetch_tensormap(&tx);
+        prefetch_tensormap(&tw);
+        const int pre = nk < STAGES ? nk : STAGES;
+        if (a.static_weights)
+            for (int c = 0; c < pre; ++c) {
+                mbar_arrive_expect_tx(&full[c], STAGE_BYTES);
+                tma_load_2d(base + c * STAGE_BYTES + 3 * PLANE, &tw, (kc0 + c) * TK, n0, &full[c]);
+            }
+        pdl_wait_primary();
+        for (int c = 0; c < pre; ++c) {
+            unsigned char* st = base + c * STAGE_BYTES;
+            if (!a.static_weights) {
+                mbar_arrive_expect_tx(&full[c], STAGE_BYTES);
+                tma_load_2d(st + 3 * PLANE, &tw, (kc0 + c) * TK, n0, &full[c]);
+            }
+            tma_load_3d(st, &tx, (kc0 + c) * TK, m0, 0, &full[c]);  // box 64 x 128 x 3: the three planes
+        }
+        for (int c = pre; c < nk; ++c) {
             const int s = c % STAGES;
             if (c >= STAGES && !mbar_wait_bounded(&empty[s], (uint32_t)((c / STAGES - 1) & 1))) {
                 atomicExch(s_abort, 1);
@@ -348,19 +374,40 @@ __global__ void __launch_bounds__(pers::THREADS, 1)
         fence_barrier_init();
     }
     pdl_launch_dependents();
-    pdl_wait_primary();  // the planes come from the previous kernel; the output may still be read by earlier ones
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    if (!(warp == 0 && lane == 0)) pdl_wait_primary();  // the output may still be read by earlier kernels
 
     if (warp == 0) {
         if (lane == 0) {  // ---- TMA producer
+            // the model's weights do not depend on earlier kernels: the first
+            // tile's first weight tiles go out before waiting for the planes
+            prefetch_tensormap(&tx);
+            prefetch_tensormap(&tw);
+            const int pre = (int)blockIdx.x < tiles ? (nk < STAGES ? nk : STAGES) : 0;
+            if (a.static_weights)
+                for (int c = 0; c < pre; ++c) {
+                    mbar_arrive_expect_tx(&full[c], STAGE_BYTES);
+                    tma_load_2d(base + c * STAGE_BYTES + 3 * A_PLANE, &tw, c * TK, ((int)blockIdx.x / MT) * TN,
+                                &full[c]);
+                }
+            pdl_wait_primary();
             uint32_t g = 0;
             for (int t = blockIdx.x; t < tiles && !*s_abort; t += gridDim.x) {
                 const int m0 = (t % MT) * TM, n0 = (t / MT) * TN;
                 for (int c = 0; c < nk; ++c, ++g) {
                     const uint32_t s = g % STAGES, use = g / STAGES;
+                    if ((int)g < pre) {  // fresh stage of the first tile
+                        unsigned char* st = base + s * STAGE_BYTES;
+                        if (!a.static_weights) {
+                            mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+                            tma_load_2d(st + 3 * A_PLANE, &tw, c * TK, n0, &full[s]);
+                        }
+                        tma_load_3d(st, &tx, c * TK, m0, 0, &full[s]);  // box 32 x 128 x 3: the three planes
+                        continue;
+                    }
                     if (!mbar_wait_bounded(&empty[s], (use & 1u) ^ 1u)) {
                         *s_abort = 1;
                         break;
