@@ -270,7 +270,7 @@ __global__ void __launch_bounds__(kThreads) decode_self_kernel(const SelfParams 
 // ---------------------------------------------------------------------------
 // Cross-attention: all beams of a sentence share each memory row.
 // ---------------------------------------------------------------------------
-template <int NB, int CP>
+template <int NB, int CP, int kCrossStages>
 __global__ void __launch_bounds__(kThreads) cross_kernel(const CrossParams p) {
     constexpr int RPH = CP / 8;  // rows per half-warp per chunk
     constexpr int KV_FLOATS = CP * 64;
@@ -504,7 +504,7 @@ size_t self_smem_bytes() {
     return kBarBytes + (ring > merge ? ring : merge);
 }
 
-template <int NB, int CP>
+template <int NB, int CP, int kCrossStages>
 size_t cross_smem_bytes() {
     const size_t ring = (size_t)kCrossStages * 2 * CP * 64 * sizeof(float);
     const size_t merge = (size_t)(8 * NB + NB) * kPartFloats * sizeof(float);
@@ -544,11 +544,14 @@ cudaError_t configure_nb() {
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)self_smem_bytes<NB>());
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(cross_kernel<NB, kCrossShortRows>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)cross_smem_bytes<NB, kCrossShortRows>());
+    e = cudaFuncSetAttribute(cross_kernel<NB, kCrossShortRows, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)cross_smem_bytes<NB, kCrossShortRows, 3>());
     if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(cross_kernel<NB, kCrossLongRows>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)cross_smem_bytes<NB, kCrossLongRows>());
+    e = cudaFuncSetAttribute(cross_kernel<NB, kCrossLongRows, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)cross_smem_bytes<NB, kCrossLongRows, 3>());
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(cross_kernel<NB, kCrossSplitRows, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)cross_smem_bytes<NB, kCrossSplitRows, 2>());
 }
 
 template <int NB>
@@ -559,11 +562,14 @@ cudaError_t launch_self_nb(const SelfParams& p, int n_sent, cudaStream_t st) {
 
 template <int NB>
 cudaError_t launch_cross_nb(const CrossParams& p, int n_sent, int chunk_rows, cudaStream_t st) {
+    if (chunk_rows == kCrossSplitRows)
+        return launch_ex(cross_kernel<NB, kCrossSplitRows, 2>, dim3(p.n_split, p.H, n_sent),
+                         cross_smem_bytes<NB, kCrossSplitRows, 2>(), p.n_split, st, p);
     if (chunk_rows == kCrossLongRows)
-        return launch_ex(cross_kernel<NB, kCrossLongRows>, dim3(p.n_split, p.H, n_sent),
-                         cross_smem_bytes<NB, kCrossLongRows>(), p.n_split, st, p);
-    return launch_ex(cross_kernel<NB, kCrossShortRows>, dim3(p.n_split, p.H, n_sent),
-                     cross_smem_bytes<NB, kCrossShortRows>(), p.n_split, st, p);
+        return launch_ex(cross_kernel<NB, kCrossLongRows, 3>, dim3(p.n_split, p.H, n_sent),
+                         cross_smem_bytes<NB, kCrossLongRows, 3>(), p.n_split, st, p);
+    return launch_ex(cross_kernel<NB, kCrossShortRows, 3>, dim3(p.n_split, p.H, n_sent),
+                     cross_smem_bytes<NB, kCrossShortRows, 3>(), p.n_split, st, p);
 }
 
 }  // namespace

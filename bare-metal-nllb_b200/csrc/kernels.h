@@ -15,23 +15,23 @@ namespace nllb {
 // (cross_chunk_rows).  Measured on B200: 32 x 3 (4 CTAs per SM) for the
 // self-attention stream; for cross-attention 16 x 3 when every memory of the
 // call has at most 160 rows (1024 sentences of 18..130 rows: 127 us against
-// 189 us for 64 x 2) and 32 x 3 for longer memories (16 x 512 rows: 16.6 us).
+// 189 us for 64 x 2), 32 x 3 for longer memories (16 x 512 rows: 16.6 us
+// against 24 us), and 64 x 2 when split-KV leaves each CTA at most 64 rows
+// (one sentence of 512 rows: one chunk per split CTA, 6.2 us against 7.4).
 #ifndef NLLB_SELF_CHUNK_ROWS
 #define NLLB_SELF_CHUNK_ROWS 32
 #endif
 #ifndef NLLB_SELF_STAGES
 #define NLLB_SELF_STAGES 3
 #endif
-#ifndef NLLB_CROSS_STAGES
-#define NLLB_CROSS_STAGES 3
-#endif
 constexpr int kSelfChunkRows = NLLB_SELF_CHUNK_ROWS;
 constexpr int kSelfStages = NLLB_SELF_STAGES;
-constexpr int kCrossShortRows = 16, kCrossLongRows = 32, kCrossLongFrom = 160;
-constexpr int kCrossStages = NLLB_CROSS_STAGES;
-inline int cross_chunk_rows(int max_len) { return max_len > kCrossLongFrom ? kCrossLongRows : kCrossShortRows; }
+constexpr int kCrossShortRows = 16, kCrossLongRows = 32, kCrossSplitRows = 64, kCrossLongFrom = 160;
+// Chunk rows for the longest memory of a call (the split plan may then move
+// to kCrossSplitRows, see the cross-attention entry point).
+inline int cross_chunk_rows(int max_len) { return max_len <= kCrossLongFrom ? kCrossShortRows : kCrossLongRows; }
 static_assert(kSelfChunkRows % 16 == 0 && kSelfChunkRows >= 16, "chunk rows: multiple of 16");
-static_assert(kSelfStages >= 1 && kSelfStages <= 16 && kCrossStages >= 1 && kCrossStages <= 16,
+static_assert(kSelfStages >= 1 && kSelfStages <= 16,
               "ring depth: 1..16 (the barrier block holds 16)");
 inline int self_chunk_positions(int n_beams) { return kSelfChunkRows / n_beams; }
 constexpr int kPartFloats = 68;  // split record per beam: m, l, pad, pad, acc[64]

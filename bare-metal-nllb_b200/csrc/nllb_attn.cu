@@ -538,8 +538,12 @@ static int cross_dev(nllb_attn_ctx* c, int layer, int n_sent, const float* q, fl
     p.out = out;
     p.H = d.n_heads;
     p.max_src = d.max_src;
-    const int chunk_rows = cross_chunk_rows(max_len);
+    int chunk_rows = cross_chunk_rows(max_len);
     choose_split(c, n_sent * d.n_heads, max_len, chunk_rows, &p.n_split, &p.pos_per_split);
+    if (chunk_rows == kCrossLongRows && p.n_split > 1 && p.pos_per_split <= kCrossSplitRows) {
+        chunk_rows = kCrossSplitRows;  // one chunk per split CTA
+        choose_split(c, n_sent * d.n_heads, max_len, chunk_rows, &p.n_split, &p.pos_per_split);
+    }
     p.scale_log2 = (1.0f / std::sqrt(64.0f)) * kLog2e;
     p.err = c->err;
     NLLB_CK(launch_cross(p, n_sent, d.n_beams, chunk_rows, c->stream));
