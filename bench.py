@@ -127,7 +127,7 @@ def parse_args():
     ap.add_argument("--cpu-sample-s", type=float, default=10.0)
     ap.add_argument("--translate-sentences", type=int, default=1024,
                     help="sentences of the sentence-batched translation (0: skip translation)")
-    ap.add_argument("--ncu-case", choices=("decode", "decode1", "cross", "prefill", "linear"),
+    ap.add_argument("--ncu-case", choices=("decode", "decode1", "cross", "prefill", "linear", "translate"),
                     help="run one small fixed case for an ncu capture and exit")
     return ap.parse_args()
 
@@ -575,7 +575,18 @@ def ncu_case(which: str) -> None:
                 assert lin.status() == 0
         print("ncu case linear: ok")
         return
-    elif which == "prefill":
+    elif which == "translate":
+        # the translation engine on 64 sentences of config 4's workload, 40 target tokens at most
+        # (after a 4-sentence warm-up): the launch list of a decode-dominated run
+        from nllb_attn import synth_model as sm
+        sm.ensure_model(SYNTH_MODEL, seed=0)
+        srcs = config4_sources(1024)[:64]
+        with na.Model(SYNTH_MODEL, device=0, max_sentences=64, max_src=132, max_gen=132) as m:
+            m.translate(srcs[:4], sm.LANG["fra_Latn"], max_gen=8)
+            _, _, st = m.translate(srcs, sm.LANG["fra_Latn"], max_gen=40)
+        print(f"ncu case translate: ok, {st.tokens_out} tokens in {st.steps} steps")
+        return
+
         B, S = 8, 128
         c = na.Context(0, n_layers=0, max_sentences=0)
         qp, kp, vp = (torch.randn((B, HEADS, S, HEAD_DIM), generator=g, device=dev) for _ in range(3))
