@@ -459,10 +459,14 @@ int nllb_model_load(const char* path, int device, int max_sentences, int max_src
 
 namespace {
 
-// The TMA-fed tensor-core kernels take more than 16 rows (fewer go to the
-// weight-streaming kernel over the int8 matrix).
+// The TMA-fed tensor-core kernels take more than 4 rows, and the vocabulary
+// projection at any row count; up to 4 rows of the other layers go to the
+// weight-streaming kernel over the int8 matrix.  Measured on B200: 16 rows x
+// 1024 -> 1024 in 26 us on the weight-streaming kernel against about 9 us on
+// the split-K tensor-core kernel; 4 rows x 1024 -> 256206 in 220 us against
+// a persistent kernel over one row tile.
 bool tma_path(const nllb_model* m, const Lin& L, int M) {
-    return M > 16 && L.wb && (size_t)M * L.in * 3 <= m->planes_elems;
+    return M >= 1 && (M > 4 || L.out >= 65536) && L.wb && (size_t)M * L.in * 3 <= m->planes_elems;
 }
 
 // out = x W^T / scale + bias (+ relu, + residual).  On the tensor-core path
@@ -544,6 +548,7 @@ struct Work {
     float* top_lp = nullptr;
     float* topk_ws = nullptr;  // partials of the vocabulary log-softmax / top-k
     unsigned char* active = nullptr;
+    bool h_planes = false;  // the last decoder step left h as bf16 planes in m->planes (else fp32 in h)
     // buffers come from the model's pool in call order: a call no larger than
     // an earlier one allocates nothing (the previous call has finished: it
     // returned its results to the host)
@@ -622,6 +627,7 @@ int decode_step(nllb_model* m, Work& w, int step) {
     void* P1 = tp ? m->planes : nullptr;
     void* P2 = tp ? m->planes2 : nullptr;
     float* lnout = tp ? nullptr : w.h;
+    w.h_planes = tp;  // the final LayerNorm below leaves h as planes (tp) or as fp32
     for (int l = 0; l < LAYERS; ++l) {
         auto& Dl = m->dec[l];
         ENG_CK(launch_layernorm(lnout, w.x, nullptr, Dl.ln1g, Dl.ln1b, R, P1, m->stream));
@@ -645,8 +651,8 @@ int decode_step(nllb_model* m, Work& w, int step) {
 // penalties (main.c:186-213) and log-softmax + top-k (main.c:154-182).
 int vocab_topk(nllb_model* m, Work& w, int k, bool penalties, const nllb_translate_opts& o,
                const int* hist = nullptr) {
-    const bool tp = tma_path(m, m->vocab, w.rows);  // the final LayerNorm left the planes of h
-    ENG_RC(run_linear(m, m->vocab, w.h, w.rows, w.logits, nullptr, 0, VOCAB_LD, LANG_START, tp ? m->planes : nullptr));
+    ENG_RC(run_linear(m, m->vocab, w.h, w.rows, w.logits, nullptr, 0, VOCAB_LD, LANG_START,
+                      w.h_planes ? m->planes : nullptr));
     if (penalties)
         ENG_CK(launch_penalties(w.logits, VOCAB_LD, hist ? hist : w.hist, m->max_gen, w.ntok, w.active, w.rows,
                                 o.repetition_penalty, o.no_repeat_ngram, m->stream));
