@@ -27,5 +27,14 @@ struct nllb_attn_ctx {
     // staging for *_host calls, grown on demand
     void* stg[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
     size_t stg_bytes[6] = {0, 0, 0, 0, 0, 0};
+    // pipelined host-buffer decode: input copies on copy_in, kernels on stream,
+    // output copies on copy_out, chunk by chunk of sentences (created on first use)
+    static constexpr int kHostChunks = 4;
+    cudaStream_t copy_in = nullptr, copy_out = nullptr;
+    cudaEvent_t ev_in[kHostChunks] = {}, ev_k[kHostChunks] = {};
+    cudaEvent_t ev_parent = nullptr;  // the last host parent copy has left par_h
+    int* err_h = nullptr;             // pinned: device error word read with the outputs
+    int* par_h = nullptr;             // pinned staging of reorder_host's parents
+    size_t par_h_ints = 0;
 };
 

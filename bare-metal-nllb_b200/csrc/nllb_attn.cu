@@ -107,6 +107,21 @@ int check_device_error(nllb_attn_ctx* c) {
     return fail(NLLB_ATTN_EINVAL, "reorder: parent index outside [0, n_beams)");
 }
 
+// Copy streams, events and pinned words of the pipelined host-buffer calls.
+int ensure_host_pipeline(nllb_attn_ctx* c) {
+    if (c->copy_in) return NLLB_ATTN_OK;
+    NLLB_CK(cudaStreamCreateWithFlags(&c->copy_in, cudaStreamNonBlocking));
+    NLLB_CK(cudaStreamCreateWithFlags(&c->copy_out, cudaStreamNonBlocking));
+    for (int i = 0; i < nllb_attn_ctx::kHostChunks; ++i) {
+        NLLB_CK(cudaEventCreateWithFlags(&c->ev_in[i], cudaEventDisableTiming));
+        NLLB_CK(cudaEventCreateWithFlags(&c->ev_k[i], cudaEventDisableTiming));
+    }
+    NLLB_CK(cudaEventCreateWithFlags(&c->ev_parent, cudaEventDisableTiming));
+    NLLB_CK(cudaHostAlloc(reinterpret_cast<void**>(&c->err_h), sizeof(int), cudaHostAllocDefault));
+    *c->err_h = 0;
+    return NLLB_ATTN_OK;
+}
+
 int finish_host_call(nllb_attn_ctx* c) {
     NLLB_CK(cudaStreamSynchronize(c->stream));
     return check_device_error(c);
@@ -163,6 +178,20 @@ void nllb_attn_destroy(nllb_attn_ctx* c) {
         if (p) cudaFree(p);
     for (void* p : c->stg)
         if (p) cudaFree(p);
+    if (c->copy_in) cudaStreamSynchronize(c->copy_in);
+    if (c->copy_out) cudaStreamSynchronize(c->copy_out);
+    for (int i = 0; i < nllb_attn_ctx::kHostChunks; ++i) {
+        if (c->ev_in[i]) cudaEventDestroy(c->ev_in[i]);
+        if (c->ev_k[i]) cudaEventDestroy(c->ev_k[i]);
+    }
+    if (c->ev_parent) {
+        cudaEventSynchronize(c->ev_parent);
+        cudaEventDestroy(c->ev_parent);
+    }
+    if (c->copy_in) cudaStreamDestroy(c->copy_in);
+    if (c->copy_out) cudaStreamDestroy(c->copy_out);
+    if (c->err_h) cudaFreeHost(c->err_h);
+    if (c->par_h) cudaFreeHost(c->par_h);
     if (c->own_stream) cudaStreamDestroy(c->own_stream);
     delete c;
 }
@@ -373,17 +402,19 @@ static int check_beam_call(nllb_attn_ctx* c, int layer, int n_sent) {
     return NLLB_ATTN_OK;
 }
 
-static int decode_self_dev(nllb_attn_ctx* c, int layer, int step, int n_sent, const float* q,
+// Sentences s0 .. s0 + n_sent - 1; q, k_new, v_new, out point at sentence s0.
+static int decode_self_dev(nllb_attn_ctx* c, int layer, int step, int s0, int n_sent, const float* q,
                            const float* k_new, const float* v_new, float* out) {
     const nllb_attn_dims& d = c->d;
     const size_t layer_floats = (size_t)d.max_sentences * d.n_heads * (size_t)d.max_tgt * d.n_beams * 64;
+    const size_t sent_floats = (size_t)d.n_heads * d.max_tgt * d.n_beams * 64;
     SelfParams p;
-    p.kc = c->kc + (size_t)layer * layer_floats;
-    p.vc = c->vc + (size_t)layer * layer_floats;
-    p.kc_w = c->kc + (size_t)layer * layer_floats;
-    p.vc_w = c->vc + (size_t)layer * layer_floats;
-    p.hist = c->hist;
-    p.hist_w = c->hist;
+    p.kc = c->kc + (size_t)layer * layer_floats + (size_t)s0 * sent_floats;
+    p.vc = c->vc + (size_t)layer * layer_floats + (size_t)s0 * sent_floats;
+    p.kc_w = c->kc + (size_t)layer * layer_floats + (size_t)s0 * sent_floats;
+    p.vc_w = c->vc + (size_t)layer * layer_floats + (size_t)s0 * sent_floats;
+    p.hist = c->hist + (size_t)s0 * c->Tp * 8;
+    p.hist_w = c->hist + (size_t)s0 * c->Tp * 8;
     p.q = q;
     p.k_new = k_new;
     p.v_new = v_new;
@@ -410,7 +441,7 @@ int nllb_attn_decode_self(nllb_attn_ctx* c, int layer, int step, int n_sent, con
     if (!aligned16(q) || !aligned16(k_new) || !aligned16(v_new) || !aligned16(out))
         return fail(NLLB_ATTN_EINVAL, "q, k_new, v_new, out must be 16-byte aligned");
     if ((rc = set_device(c))) return rc;
-    return decode_self_dev(c, layer, step, n_sent, q, k_new, v_new, out);
+    return decode_self_dev(c, layer, step, 0, n_sent, q, k_new, v_new, out);
 }
 
 int nllb_attn_decode_self_host(nllb_attn_ctx* c, int layer, int step, int n_sent, const float* q,
@@ -421,19 +452,37 @@ int nllb_attn_decode_self_host(nllb_attn_ctx* c, int layer, int step, int n_sent
     if (step >= c->d.max_tgt) return fail(NLLB_ATTN_ECAPACITY, "step >= max_tgt");
     if (!q || !k_new || !v_new || !out) return fail(NLLB_ATTN_EINVAL, "q, k_new, v_new, out are required");
     if ((rc = set_device(c))) return rc;
-    const size_t bytes = (size_t)n_sent * c->d.n_beams * c->d.n_heads * 64 * sizeof(float);
+    const size_t sent_floats = (size_t)c->d.n_beams * c->d.n_heads * 64;
+    const size_t bytes = (size_t)n_sent * sent_floats * sizeof(float);
     for (int i = 0; i < 4; ++i)
         if ((rc = ensure_stage(c, i, bytes))) return rc;
+    if ((rc = ensure_host_pipeline(c))) return rc;
     float* dq = static_cast<float*>(c->stg[0]);
     float* dk = static_cast<float*>(c->stg[1]);
     float* dv = static_cast<float*>(c->stg[2]);
     float* dout = static_cast<float*>(c->stg[3]);
-    NLLB_CK(cudaMemcpyAsync(dq, q, bytes, cudaMemcpyHostToDevice, c->stream));
-    NLLB_CK(cudaMemcpyAsync(dk, k_new, bytes, cudaMemcpyHostToDevice, c->stream));
-    NLLB_CK(cudaMemcpyAsync(dv, v_new, bytes, cudaMemcpyHostToDevice, c->stream));
-    if ((rc = decode_self_dev(c, layer, step, n_sent, dq, dk, dv, dout))) return rc;
-    NLLB_CK(cudaMemcpyAsync(out, dout, bytes, cudaMemcpyDeviceToHost, c->stream));
-    return finish_host_call(c);
+    // chunks of sentences: the input copy of chunk j + 1 and the output copy of
+    // chunk j - 1 run while chunk j's kernel runs (separate copy streams)
+    const int C = std::min(nllb_attn_ctx::kHostChunks, n_sent);
+    for (int j = 0; j < C; ++j) {
+        const int s0 = (int)((long long)j * n_sent / C), s1 = (int)((long long)(j + 1) * n_sent / C);
+        const size_t off = (size_t)s0 * sent_floats, cb = (size_t)(s1 - s0) * sent_floats * sizeof(float);
+        NLLB_CK(cudaMemcpyAsync(dq + off, q + off, cb, cudaMemcpyHostToDevice, c->copy_in));
+        NLLB_CK(cudaMemcpyAsync(dk + off, k_new + off, cb, cudaMemcpyHostToDevice, c->copy_in));
+        NLLB_CK(cudaMemcpyAsync(dv + off, v_new + off, cb, cudaMemcpyHostToDevice, c->copy_in));
+        NLLB_CK(cudaEventRecord(c->ev_in[j], c->copy_in));
+        NLLB_CK(cudaStreamWaitEvent(c->stream, c->ev_in[j], 0));
+        if ((rc = decode_self_dev(c, layer, step, s0, s1 - s0, dq + off, dk + off, dv + off, dout + off)))
+            return rc;
+        NLLB_CK(cudaEventRecord(c->ev_k[j], c->stream));
+        NLLB_CK(cudaStreamWaitEvent(c->copy_out, c->ev_k[j], 0));
+        NLLB_CK(cudaMemcpyAsync(out + off, dout + off, cb, cudaMemcpyDeviceToHost, c->copy_out));
+    }
+    // the error word after the last kernel, with the outputs
+    NLLB_CK(cudaMemcpyAsync(c->err_h, c->err, sizeof(int), cudaMemcpyDeviceToHost, c->copy_out));
+    NLLB_CK(cudaStreamSynchronize(c->copy_out));
+    if (*c->err_h == 0) return NLLB_ATTN_OK;
+    return check_device_error(c);  // reads, reports and clears the word
 }
 
 int nllb_attn_reorder(nllb_attn_ctx* c, int n_sent, const int* parent) {
@@ -459,12 +508,26 @@ int nllb_attn_reorder_host(nllb_attn_ctx* c, int n_sent, const int* parent) {
             return fail(NLLB_ATTN_EINVAL, "parent index outside [0, n_beams)");
     int rc = set_device(c);
     if (rc) return rc;
-    const size_t bytes = (size_t)n_sent * c->d.n_beams * sizeof(int);
-    if ((rc = ensure_stage(c, 4, bytes))) return rc;
-    NLLB_CK(cudaMemcpyAsync(c->stg[4], parent, bytes, cudaMemcpyHostToDevice, c->stream));
+    const size_t n = (size_t)n_sent * c->d.n_beams;
+    if ((rc = ensure_stage(c, 4, n * sizeof(int)))) return rc;
+    if ((rc = ensure_host_pipeline(c))) return rc;
+    // The parents (checked above) go through a pinned copy, so the call returns
+    // once the reorder is enqueued and the caller's buffer is free at once;
+    // later calls on the context are ordered after it.
+    NLLB_CK(cudaEventSynchronize(c->ev_parent));  // the previous copy has left par_h
+    if (c->par_h_ints < n) {
+        if (c->par_h) cudaFreeHost(c->par_h);
+        c->par_h = nullptr;
+        c->par_h_ints = 0;
+        NLLB_CK(cudaHostAlloc(reinterpret_cast<void**>(&c->par_h), n * sizeof(int), cudaHostAllocDefault));
+        c->par_h_ints = n;
+    }
+    std::memcpy(c->par_h, parent, n * sizeof(int));
+    NLLB_CK(cudaMemcpyAsync(c->stg[4], c->par_h, n * sizeof(int), cudaMemcpyHostToDevice, c->stream));
+    NLLB_CK(cudaEventRecord(c->ev_parent, c->stream));
     NLLB_CK(launch_reorder(c->hist, c->Tp, static_cast<int*>(c->stg[4]), n_sent, c->d.n_beams, c->err,
                            c->stream));
-    return finish_host_call(c);
+    return NLLB_ATTN_OK;
 }
 
 // ---------------------------------------------------------------------------

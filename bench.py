@@ -253,12 +253,12 @@ def run_ours(args, rank, world, local_rank):
     # e2e through the host-buffer C ABI: H2D of q/k/v/parents, D2H of out, every launch
     e2e = None
     n_pool = 8
-    qh = torch.empty((n_pool, S, BEAMS, DMODEL), pin_memory=True)
-    qh.normal_()
-    kh = torch.empty_like(qh).normal_()
-    vh = torch.empty_like(qh).normal_()
-    oh = torch.empty_like(qh)
-    ph = torch.argsort(torch.rand((T, S, BEAMS)), dim=-1).to(torch.int32).contiguous()
+    # every host buffer pinned (torch.empty_like would not keep the pinning)
+    qh, kh, vh, oh = (torch.empty((n_pool, S, BEAMS, DMODEL), pin_memory=True) for _ in range(4))
+    for t_ in (qh, kh, vh):
+        t_.normal_()
+    ph = torch.empty((T, S, BEAMS), dtype=torch.int32, pin_memory=True)
+    ph.copy_(torch.argsort(torch.rand((T, S, BEAMS)), dim=-1).to(torch.int32))
     qn, kn, vn, on, pn = qh.numpy(), kh.numpy(), vh.numpy(), oh.numpy(), ph.numpy()
     e2e_steps = max(1, min(args.steps, 2))
     ctx.set_stream(None)

@@ -148,7 +148,10 @@ NLLB_ATTN_API int nllb_attn_decode_self_host(nllb_attn_ctx* ctx, int layer, int 
  * bootstrap copies main.c:335-340, 384-392): new beam b of sentence s
  * continues the history of old beam parent[s*n_beams + b], for every layer.
  * Applies to positions already written; costs O(n_sentences*max_tgt) bytes,
- * independent of the cache size.  parent: [n_sentences][n_beams] int32. */
+ * independent of the cache size.  parent: [n_sentences][n_beams] int32.
+ * nllb_attn_reorder_host checks the parents on the host and returns once the
+ * reorder is enqueued (the caller may reuse its buffer at once); later calls
+ * on the context run after it. */
 NLLB_ATTN_API int nllb_attn_reorder(nllb_attn_ctx* ctx, int n_sentences, const int* parent);
 NLLB_ATTN_API int nllb_attn_reorder_host(nllb_attn_ctx* ctx, int n_sentences, const int* parent);
 
