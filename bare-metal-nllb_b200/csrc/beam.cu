@@ -6,7 +6,9 @@
 //   * candidates: every finished beam carries itself with token 2 and its
 //     score, then every unfinished beam offers its 8 best tokens with
 //     score + log-probability, in beam order (main.c:413-450);
-//   * the reference's exchange sort, descending (main.c:456-460);
+//   * the reference's exchange sort, descending (main.c:456-460), run for its
+//     first NBEAM + 1 outer iterations only: iteration i writes positions >= i,
+//     so positions 0..NBEAM (all that is read afterwards) are final by then;
 //   * the best 4 candidates become the new beams: tokens of the parent plus
 //     the new token, finished when the token is 2, the score of the step that
 //     emitted token 2 kept as eos_score (main.c:462-488);
@@ -15,7 +17,8 @@
 //   * the sentence stops when the next step would reach max_out + 2 or no
 //     beam is unfinished (main.c:411-412, 503-509).
 // Lane 0 does the scalar work in the reference's order (its float compares
-// and adds are the reference's); the lanes copy token histories.
+// and adds are the reference's); the lanes load the beams' top-k lists and
+// copy token histories.
 #include "device_common.cuh"
 #include "engine_kernels.h"
 
@@ -33,6 +36,9 @@ __global__ void __launch_bounds__(32 * SENT_PER_CTA) beam_select_kernel(const Be
     __shared__ int n_par[SENT_PER_CTA][NBEAM], n_tok[SENT_PER_CTA][NBEAM], n_len[SENT_PER_CTA][NBEAM];
     __shared__ int n_slot[SENT_PER_CTA][NBEAM];
     __shared__ int s_done[SENT_PER_CTA];
+    __shared__ int s_tok[SENT_PER_CTA][NBEAM * TOPK];
+    __shared__ float s_lp[SENT_PER_CTA][NBEAM * TOPK];
+    static_assert(NBEAM * TOPK == 32, "one top-k entry per lane");
     pdl_launch_dependents();
     pdl_wait_primary();  // the top-k lists come from the previous kernel
     const int wi = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -44,6 +50,8 @@ __global__ void __launch_bounds__(32 * SENT_PER_CTA) beam_select_kernel(const Be
     const int r0 = s * NBEAM;
 
     if (lane == 0) s_done[wi] = B.done[s];
+    s_tok[wi][lane] = top_tok[(size_t)r0 * TOPK + lane];  // the 4 beams' lists are contiguous
+    s_lp[wi][lane] = top_lp[(size_t)r0 * TOPK + lane];
     __syncwarp();
     if (s_done[wi]) {
         // finished sentence: beams unchanged (carried into the other buffer), parents identity
@@ -67,12 +75,13 @@ __global__ void __launch_bounds__(32 * SENT_PER_CTA) beam_select_kernel(const Be
             const float base = B.bsc[r0 + b];
             for (int k = 0; k < TOPK; ++k) {
                 cb[nc] = b;
-                ct[nc] = top_tok[(size_t)(r0 + b) * TOPK + k];
-                cs[nc] = base + top_lp[(size_t)(r0 + b) * TOPK + k];
+                ct[nc] = s_tok[wi][b * TOPK + k];
+                cs[nc] = base + s_lp[wi][b * TOPK + k];
                 ++nc;
             }
         }
-        for (int i = 0; i < nc - 1; ++i)
+        const int n_outer = nc - 1 < NBEAM + 1 ? nc - 1 : NBEAM + 1;
+        for (int i = 0; i < n_outer; ++i)
             for (int j = i + 1; j < nc; ++j)
                 if (cs[j] > cs[i]) {
                     const int tb = cb[i], tt = ct[i];

@@ -313,6 +313,10 @@ __global__ void __launch_bounds__(256) linear_tiled_kernel(const LinearArgs a) {
 // sequence; the lane holding the first occurrence of a token applies all of
 // its occurrences, so the float operations are the reference's.  Then the
 // no-repeat-bigram ban (main.c:196-213) sets the banned logits to -1e30.
+// A lane owns positions g0 + lane + 32q (q < 4) of a 128-position group; one
+// branch-free pass over the history (the same address for all lanes) finds for
+// each whether an earlier position holds its token and how many later ones
+// do, then the logits of first occurrences are loaded together and written.
 __global__ void penalties_kernel(float* logits, size_t ld, const int* hist, int hist_ld, const int* n_tokens,
                                  const unsigned char* active, int rows, float penalty, int ngram) {
     pdl_launch_dependents();
@@ -322,17 +326,38 @@ __global__ void penalties_kernel(float* logits, size_t ld, const int* hist, int 
     float* lg = logits + (size_t)r * ld;
     const int* tk = hist + (size_t)r * hist_ld;
     const int n = n_tokens[r];
-    for (int g = 2 + lane; g < n; g += 32) {
-        const int t = tk[g];
-        if (t == 2) continue;
-        bool first = true;
-        for (int j = 2; j < g && first; ++j) first = tk[j] != t;
-        if (!first) continue;
-        int count = 1;
-        for (int j = g + 1; j < n; ++j) count += tk[j] == t;
-        float v = lg[t];
-        for (int c = 0; c < count; ++c) v = (v > 0.f) ? v / penalty : v * penalty;
-        lg[t] = v;
+    for (int g0 = 2; g0 < n; g0 += 128) {
+        int t[4], cnt[4];    // t = -1: no position, or token 2 (never penalised, never matches)
+        unsigned seen = 0;   // bit q: an earlier position holds t[q]
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int g = g0 + 32 * q + lane;
+            t[q] = g < n ? __ldg(tk + g) : -1;
+            if (t[q] == 2) t[q] = -1;
+            cnt[q] = t[q] >= 0 ? 1 : 0;
+        }
+#pragma unroll 4
+        for (int j = 2; j < n; ++j) {
+            const int u = __ldg(tk + j);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int g = g0 + 32 * q + lane;
+                const bool eq = u == t[q];
+                seen |= (eq && j < g) ? (1u << q) : 0u;
+                cnt[q] += (eq && j > g) ? 1 : 0;
+            }
+        }
+        float v[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            if (cnt[q] > 0 && !((seen >> q) & 1u)) v[q] = lg[t[q]];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            if (cnt[q] > 0 && !((seen >> q) & 1u)) {
+                float x = v[q];
+                for (int c = 0; c < cnt[q]; ++c) x = (x > 0.f) ? x / penalty : x * penalty;
+                lg[t[q]] = x;
+            }
     }
     __syncwarp();
     if (ngram == 2 && n >= 2) {
