@@ -311,8 +311,12 @@ __global__ void __launch_bounds__(256) linear_tiled_kernel(const LinearArgs a) {
 // One warp per row.  Repetition penalty (main.c:186-194): every occurrence of
 // a token at positions 2..n-1 (token 2 skipped) scales its logit once, in
 // sequence; the lane holding the first occurrence of a token applies all of
-// its occurrences, so the float operations are the reference's.  Then the
-// no-repeat-bigram ban (main.c:196-213) sets the banned logits to -1e30.
+// its occurrences, so the float operations are the reference's.  A positive
+// logit is multiplied by the fp32 reciprocal of the penalty: every release
+// build of the reference (Makefile:15,19,33) compiles `logits[t] /= penalty`
+// under -ffast-math, which turns the division by the constant into that
+// multiplication.  Then the no-repeat-bigram ban (main.c:196-213) sets the
+// banned logits to -1e30.
 // A lane owns positions g0 + lane + 32q (q < 4) of a 128-position group; one
 // branch-free pass over the history (the same address for all lanes) finds for
 // each whether an earlier position holds its token and how many later ones
@@ -326,6 +330,7 @@ __global__ void penalties_kernel(float* logits, size_t ld, const int* hist, int 
     float* lg = logits + (size_t)r * ld;
     const int* tk = hist + (size_t)r * hist_ld;
     const int n = n_tokens[r];
+    const float inv_penalty = 1.0f / penalty;
     for (int g0 = 2; g0 < n; g0 += 128) {
         int t[4], cnt[4];    // t = -1: no position, or token 2 (never penalised, never matches)
         unsigned seen = 0;   // bit q: an earlier position holds t[q]
@@ -355,7 +360,7 @@ __global__ void penalties_kernel(float* logits, size_t ld, const int* hist, int 
         for (int q = 0; q < 4; ++q)
             if (cnt[q] > 0 && !((seen >> q) & 1u)) {
                 float x = v[q];
-                for (int c = 0; c < cnt[q]; ++c) x = (x > 0.f) ? x / penalty : x * penalty;
+                for (int c = 0; c < cnt[q]; ++c) x = (x > 0.f) ? x * inv_penalty : x * penalty;
                 lg[t[q]] = x;
             }
     }
@@ -369,7 +374,7 @@ __global__ void penalties_kernel(float* logits, size_t ld, const int* hist, int 
 
 // ---------------------------------------------------------------------------
 // log-softmax over the vocabulary and the K best entries (main.c:154-182):
-// each row split into C column chunks (about 8 CTAs per SM in all); one
+// each row split into C column chunks (vocab_topk_chunks); one
 // streaming pass per chunk keeps an online max and sum of exp and a per-thread
 // top-K (greater value first, lower index first among equals, as find_topk's
 // strict comparison does); a warp per row then merges the C partials.
@@ -485,30 +490,46 @@ __global__ void __launch_bounds__(256) vocab_partial_kernel(const float* logits,
             top.offer(x, idx, valid, lane);
         }
     }
-    // float4 body; the loop bound is uniform per warp (lane j0 + lane may be past the end)
+    // float4 body in batches of kBatch float4 per thread (element j0 + 256 u +
+    // thread, u < kBatch), the next batch in flight while this one is used:
+    // 2 kBatch loads of 16 B outstanding per thread keep enough bytes in
+    // flight to stream at HBM speed.  The loop bound is uniform per CTA.
+    constexpr int kBatch = 4;
     const float4* body = reinterpret_cast<const float4*>(lg + b0);
     const float4 none = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-    int j = warp * 32 + lane;
-    float4 cur = j < nb4 ? __ldcs(body + j) : none;
-    for (int j0 = warp * 32; j0 < nb4; j0 += 256, j += 256) {
-        const float4 nxt = j + 256 < nb4 ? __ldcs(body + j + 256) : none;  // one float4 ahead
-        const bool valid = j < nb4;
-        const float m4 = fmaxf(fmaxf(cur.x, cur.y), fmaxf(cur.z, cur.w));
-        lse_add4(m, s, cur, m4);
-        const int i0 = b0 + 4 * j;
-        unsigned mask = __ballot_sync(0xffffffffu, valid && m4 >= top.tv);
-        while (mask) {
-            const int src = __ffs(mask) - 1;
-            mask &= mask - 1;
-            const float c0 = __shfl_sync(0xffffffffu, cur.x, src), c1 = __shfl_sync(0xffffffffu, cur.y, src);
-            const float c2 = __shfl_sync(0xffffffffu, cur.z, src), c3 = __shfl_sync(0xffffffffu, cur.w, src);
-            const int ci = __shfl_sync(0xffffffffu, i0, src);
-            if (better(c0, ci, top.tv, top.ti)) top.insert(c0, ci, lane);
-            if (better(c1, ci + 1, top.tv, top.ti)) top.insert(c1, ci + 1, lane);
-            if (better(c2, ci + 2, top.tv, top.ti)) top.insert(c2, ci + 2, lane);
-            if (better(c3, ci + 3, top.tv, top.ti)) top.insert(c3, ci + 3, lane);
+    const int jt = warp * 32 + lane;
+    float4 cur[kBatch], nxt[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) cur[u] = jt + 256 * u < nb4 ? __ldcs(body + jt + 256 * u) : none;
+    for (int j0 = 0; j0 < nb4; j0 += 256 * kBatch) {
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const int jn = j0 + 256 * (kBatch + u) + jt;
+            nxt[u] = jn < nb4 ? __ldcs(body + jn) : none;
         }
-        cur = nxt;
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const int j = j0 + 256 * u + jt;
+            const bool valid = j < nb4;
+            const float4 v = cur[u];
+            const float m4 = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
+            lse_add4(m, s, v, m4);
+            const int i0 = b0 + 4 * j;
+            unsigned mask = __ballot_sync(0xffffffffu, valid && m4 >= top.tv);
+            while (mask) {
+                const int src = __ffs(mask) - 1;
+                mask &= mask - 1;
+                const float c0 = __shfl_sync(0xffffffffu, v.x, src), c1 = __shfl_sync(0xffffffffu, v.y, src);
+                const float c2 = __shfl_sync(0xffffffffu, v.z, src), c3 = __shfl_sync(0xffffffffu, v.w, src);
+                const int ci = __shfl_sync(0xffffffffu, i0, src);
+                if (better(c0, ci, top.tv, top.ti)) top.insert(c0, ci, lane);
+                if (better(c1, ci + 1, top.tv, top.ti)) top.insert(c1, ci + 1, lane);
+                if (better(c2, ci + 2, top.tv, top.ti)) top.insert(c2, ci + 2, lane);
+                if (better(c3, ci + 3, top.tv, top.ti)) top.insert(c3, ci + 3, lane);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) cur[u] = nxt[u];
     }
     // warp, then block
 #pragma unroll
@@ -665,10 +686,12 @@ cudaError_t launch_penalties(float* logits, size_t ld, const int* hist, int hist
                       n_tokens, active, rows, penalty, ngram);
 }
 
-// About 8 CTAs per SM in all (measured at 512 rows: 167 us per launch, against
-// 187 us with 16 and 246 us with 32).
+// Chunks for about 2 CTAs per SM in all, i.e. one CTA per row from 296 rows
+// up.  Measured on B200 (256206 logits per row, vocab_partial + merge): 512
+// rows 121 us with 2, 133 with 4, 154 with 8, 196 with 16; 4096 rows 740 us
+// for all of them (one chunk per row).
 #ifndef NLLB_TOPK_CTAS_PER_SM
-#define NLLB_TOPK_CTAS_PER_SM 8
+#define NLLB_TOPK_CTAS_PER_SM 2
 #endif
 int vocab_topk_chunks(int V, int rows) {
     int C = (148 * NLLB_TOPK_CTAS_PER_SM + rows - 1) / rows;

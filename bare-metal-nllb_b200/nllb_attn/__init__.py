@@ -89,6 +89,10 @@ SIGNATURES = {
     "nllb_linear_run": (_c_int, [_c_void_p, _fp, _c_int, _fp, _fp, _c_int, _c_void_p]),
     "nllb_linear_status": (_c_int, [_c_void_p]),
     "nllb_linear_free": (None, [_c_void_p]),
+    "nllb_apply_penalties": (_c_int, [_fp, ctypes.c_longlong, _c_int, _fp, _c_int, _fp, ctypes.c_float, _c_int,
+                                      _c_void_p]),
+    "nllb_logsoftmax_topk_ws_bytes": (_c_size_t, [_c_int, _c_int, _c_int]),
+    "nllb_logsoftmax_topk": (_c_int, [_fp, ctypes.c_longlong, _c_int, _c_int, _c_int, _fp, _fp, _fp, _c_void_p]),
 }
 
 _LIB: Optional[ctypes.CDLL] = None
@@ -325,6 +329,32 @@ def linear_int8_noalloc(x, w, weight_scale, out, bias=None, residual=None, relu=
                                              ptr(residual), LINEAR_RELU if relu else 0, stream),
            "nllb_linear_int8_noalloc")
     return out
+
+
+def apply_penalties(logits, tokens, n_tokens, penalty=1.2, no_repeat_ngram=2, stream=None):
+    """nllb_apply_penalties on torch CUDA tensors, in place: logits [rows][ld]
+    fp32, tokens [rows][tokens_ld] int32, n_tokens [rows] int32."""
+    lib = load()
+    rows = logits.shape[0]
+    _check(lib, lib.nllb_apply_penalties(ptr(logits), logits.stride(0), rows, ptr(tokens), tokens.stride(0),
+                                         ptr(n_tokens), penalty, no_repeat_ngram, stream), "nllb_apply_penalties")
+    return logits
+
+
+def logsoftmax_topk(logits, k=8, vocab=None, stream=None):
+    """nllb_logsoftmax_topk on a torch CUDA tensor logits [rows][ld] fp32:
+    returns (tokens [rows][k] int32, log-probabilities [rows][k] fp32)."""
+    import torch
+    lib = load()
+    rows = logits.shape[0]
+    V = logits.shape[1] if vocab is None else vocab
+    tok = torch.empty((rows, k), dtype=torch.int32, device=logits.device)
+    lp = torch.empty((rows, k), dtype=torch.float32, device=logits.device)
+    ws = torch.empty(max(1, lib.nllb_logsoftmax_topk_ws_bytes(V, max(rows, 1), k)), dtype=torch.uint8,
+                     device=logits.device)
+    _check(lib, lib.nllb_logsoftmax_topk(ptr(logits), logits.stride(0), V, rows, k, ptr(tok), ptr(lp), ptr(ws),
+                                         stream), "nllb_logsoftmax_topk")
+    return tok, lp
 
 
 class PreparedLinear:

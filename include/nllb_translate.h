@@ -13,9 +13,10 @@
  *                 length-normalised score; max_out = min(3*n_src+10, max_gen-4)
  *
  *  The attention runs through libnllb_attn's kernels; the rest (INT8 linear
- *  layers, LayerNorm, embeddings, vocabulary projection, penalties, top-k) are
- *  this library's kernels too.  The candidate selection of each step runs on
- *  the host from the per-beam top-8 (a few KB per step).
+ *  layers, LayerNorm, embeddings, vocabulary projection, penalties, top-k and
+ *  the candidate selection of each step) are this library's kernels too: the
+ *  decode loop runs on the device and the host only polls how many sentences
+ *  are still running.
  *
  *  Returns NLLB_ATTN_* status codes (nllb_attn.h).
  */
@@ -123,6 +124,30 @@ NLLB_ATTN_API int nllb_linear_run(nllb_linear* layer, const float* x, int M, flo
                                   int flags, void* stream);
 NLLB_ATTN_API int nllb_linear_status(nllb_linear* layer);
 NLLB_ATTN_API void nllb_linear_free(nllb_linear* layer);
+
+/* ---- per-step vocabulary operations of the beam search --------------------
+ * nllb_apply_penalties: for each of `rows` rows of logits (row r at
+ * logits + r*ld) and its token history (tokens + r*tokens_ld, n_tokens[r]
+ * entries): apply_repetition_penalty (main.c:186-194) -- every occurrence of
+ * a token at positions 2..n-1 other than 2 divides a positive logit by
+ * `penalty` or multiplies a non-positive one, once per occurrence -- then,
+ * with no_repeat_ngram 2, apply_no_repeat_ngram (main.c:196-213): every token
+ * that followed an earlier occurrence of the last token gets -1e30 (token 2
+ * excepted).  no_repeat_ngram: 0 (off) or 2.
+ * nllb_logsoftmax_topk: for each row, the k best entries of the row's
+ * log-softmax -- log_softmax_inplace + find_topk (main.c:154-182) -- as
+ * out_tok[r*k + j] / out_logp[r*k + j], best first, the lower index first
+ * among equal logits; the logits are not modified.  Logits a few ulps apart
+ * whose log-probabilities round to the same fp32 value keep their logit order
+ * here, where find_topk puts the lower index first.  k: 4 or 8; at most 65535
+ * rows.  ws: device scratch of nllb_logsoftmax_topk_ws_bytes(vocab, rows, k)
+ * bytes, 16-byte aligned.
+ * Device pointers; asynchronous on `stream` (a cudaStream_t, NULL = default). */
+NLLB_ATTN_API int nllb_apply_penalties(float* logits, long long ld, int rows, const int* tokens, int tokens_ld,
+                                       const int* n_tokens, float penalty, int no_repeat_ngram, void* stream);
+NLLB_ATTN_API size_t nllb_logsoftmax_topk_ws_bytes(int vocab, int rows, int k);
+NLLB_ATTN_API int nllb_logsoftmax_topk(const float* logits, long long ld, int vocab, int rows, int k,
+                                       int* out_tok, float* out_logp, void* ws, void* stream);
 
 #ifdef __cplusplus
 }

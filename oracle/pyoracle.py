@@ -266,3 +266,104 @@ def ref_cross(K, V, q) -> np.ndarray:
         lib.ref_cross_beam(_p(cache), 0, n_src, flat[i].ctypes.data, _p(ob), 1)
         out[i] = ob
     return out.reshape(np.shape(q))
+
+
+# ---------------------------------------------------------------------------
+# per-step vocabulary operations of the beam search (main.c:154-213)
+# ---------------------------------------------------------------------------
+REF_SEARCH_SO = os.path.join(ORACLE_DIR, "_ref", "libnllb_ref_search.so")
+_ref_search: Optional[ctypes.CDLL] = None
+
+
+def ref_search_available() -> bool:
+    return os.path.exists(REF_SEARCH_SO)
+
+
+def ref_search_lib() -> ctypes.CDLL:
+    """main.c's own penalty / log-softmax / top-k functions (ref_search_harness.c)."""
+    global _ref_search
+    if _ref_search is None:
+        if not os.path.exists(REF_SEARCH_SO):
+            raise FileNotFoundError(f"{REF_SEARCH_SO} missing: run make -C {ORACLE_DIR} ref-main where the "
+                                    "reference sources are present")
+        lib = ctypes.CDLL(REF_SEARCH_SO)
+        lib.ref_apply_penalties.argtypes = [_fp, ctypes.c_long, ctypes.c_int, _fp, ctypes.c_int, _fp,
+                                            ctypes.c_float, ctypes.c_int]
+        lib.ref_log_softmax_topk.argtypes = [_fp, ctypes.c_long, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                             _fp, _fp]
+        _ref_search = lib
+    return _ref_search
+
+
+def penalties(logits: np.ndarray, tokens: np.ndarray, n_tokens, penalty: float = 1.2,
+              ngram: int = 2) -> np.ndarray:
+    """apply_repetition_penalty (main.c:186-194) then apply_no_repeat_ngram
+    (main.c:196-213, bigrams) on each row; returns a new fp32 array.  Every
+    occurrence at positions 2..n-1 (token 2 excepted) divides a positive logit
+    by the penalty or multiplies a non-positive one, in sequence.  The division
+    is the multiplication by the fp32 reciprocal that every release build of
+    the reference (-ffast-math, Makefile:15,19,33) compiles it to."""
+    out = np.array(logits, dtype=np.float32, copy=True)
+    pen = np.float32(penalty)
+    inv = np.float32(1.0) / pen
+    for r in range(out.shape[0]):
+        lg, tk, n = out[r], tokens[r], int(n_tokens[r])
+        for g in range(2, n):
+            t = int(tk[g])
+            if t == 2:
+                continue
+            lg[t] = lg[t] * inv if lg[t] > 0 else lg[t] * pen
+        if ngram == 2 and n >= 2:
+            cur = int(tk[n - 1])
+            for i in range(0, n - 1):
+                if int(tk[i]) == cur and int(tk[i + 1]) != 2:
+                    lg[int(tk[i + 1])] = np.float32(-1e30)
+    return out
+
+
+def ref_penalties(logits: np.ndarray, tokens: np.ndarray, n_tokens, penalty: float = 1.2,
+                  ngram: int = 2) -> np.ndarray:
+    """The same through the reference's own functions (compiled main.c)."""
+    lib = ref_search_lib()
+    out = np.array(logits, dtype=np.float32, copy=True, order="C")
+    tk = np.ascontiguousarray(tokens, dtype=np.int32)
+    nt = np.ascontiguousarray(n_tokens, dtype=np.int32)
+    lib.ref_apply_penalties(_p(out), out.shape[1], out.shape[0], _p(tk), tk.shape[1], _p(nt), penalty, ngram)
+    return out
+
+
+def logsoftmax_topk(logits: np.ndarray, k: int):
+    """log_softmax_inplace (main.c:154-161) and find_topk (main.c:165-182) per
+    row: the k largest log-probabilities, best first, the lower index first
+    among equal values (find_topk's strict comparison), entries at or below
+    -1e30 never taken.  Max and log in fp32 as the reference; the sum of
+    exponentials in float64 (its order is not part of the result's contract)."""
+    lg = np.asarray(logits, dtype=np.float32)
+    rows = lg.shape[0]
+    tok = np.zeros((rows, k), np.int32)
+    lp = np.zeros((rows, k), np.float32)
+    for r in range(rows):
+        x = lg[r]
+        mx = np.float32(x.max())
+        se = np.exp((x - mx).astype(np.float64)).sum()
+        ln = np.float32(mx + np.float32(np.log(se)))
+        y = (x - ln).astype(np.float32)
+        cand = np.nonzero(y > np.float32(-1e30))[0]
+        part = cand[np.argpartition(-y[cand], min(k, len(cand)) - 1)[:k]] if len(cand) > k else cand
+        kth = y[part].min()
+        pool = cand[y[cand] >= kth]
+        order = pool[np.lexsort((pool, -y[pool]))][:k]
+        tok[r, :len(order)] = order
+        lp[r, :len(order)] = y[order]
+    return tok, lp
+
+
+def ref_logsoftmax_topk(logits: np.ndarray, k: int):
+    """The same through the reference's own functions (compiled main.c)."""
+    lib = ref_search_lib()
+    lg = np.array(logits, dtype=np.float32, copy=True, order="C")
+    rows, n = lg.shape
+    tok = np.zeros((rows, k), np.int32)
+    sc = np.zeros((rows, k), np.float32)
+    lib.ref_log_softmax_topk(_p(lg), n, n, rows, k, _p(tok), _p(sc))
+    return tok, sc

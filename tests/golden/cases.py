@@ -11,6 +11,9 @@ Routines pinned (reference file:line):
   head_mask        attention_head         tensor.c:255-282
   decode_*         decoder_self_attn_cached decoder.c:48-99, reorder by copy main.c:481-482
   cross_*          decoder_cross_attn_cached decoder.c:103-152
+  pen_*            apply_repetition_penalty + apply_no_repeat_ngram main.c:186-213
+                   (stored as the flat indices and values of the changed logits)
+  topk_*           log_softmax_inplace + find_topk main.c:154-182
 """
 from __future__ import annotations
 
@@ -96,6 +99,44 @@ def cross_case(name):
 
 
 CROSS_CASES = ("cross_512", "cross_77", "cross_1")
+
+
+def penalties_case(name):
+    """Logits, token histories and lengths for the penalty functions: tokens
+    from a small range so that most repeat, token 2 mixed in, lengths from 0
+    (nothing to do) to the full history."""
+    rows, V, T, seed, ngram = {"pen_small": (9, 4099, 140, 501, 2), "pen_vocab": (4, 256206, 132, 511, 2),
+                               "pen_nongram": (5, 1031, 64, 521, 0)}[name]
+    logits = po.det_uniform(seed, (rows, V), 3.0)
+    tokens = po.det_ints(seed + 1, rows * T, 0, 48).reshape(rows, T)
+    tokens[:, 0] = 2
+    tokens[:, 1] = V - 1
+    tokens[po.det_ints(seed + 2, rows * T, 0, 9).reshape(rows, T) == 0] = 2
+    lens = po.det_ints(seed + 3, rows, 0, T + 1)
+    lens[0], lens[-1] = 0, T
+    if rows > 2:
+        lens[1] = 1
+    return logits, tokens, lens, 1.2, ngram
+
+
+PENALTY_CASES = ("pen_small", "pen_vocab", "pen_nongram")
+
+
+def topk_case(name):
+    """Logits for log-softmax + top-k: the full vocabulary; values on a coarse
+    grid (many equal logits, so the lower-index-first rule decides); a small
+    vocabulary; rows with banned (-1e30) entries."""
+    rows, V, k, seed, grid = {"topk_vocab8": (3, 256206, 8, 601, 0.0), "topk_vocab4": (2, 256206, 4, 611, 0.0),
+                              "topk_ties": (6, 5003, 8, 621, 0.25), "topk_small": (7, 37, 4, 631, 0.0)}[name]
+    logits = po.det_uniform(seed, (rows, V), 4.0)
+    if grid:
+        logits = (np.round(logits / grid) * grid).astype(np.float32)
+    banned = po.det_ints(seed + 1, rows * V, 0, 5).reshape(rows, V) == 0
+    logits[banned] = np.float32(-1e30)
+    return logits, k
+
+
+TOPK_CASES = ("topk_vocab8", "topk_vocab4", "topk_ties", "topk_small")
 
 
 def load_golden():

@@ -1,8 +1,9 @@
 """Regenerate tests/golden/golden_outputs.npz from the reference itself.
 
 Runs the reference's own attention code (tensor.c / decoder.c compiled from
-the reference sources into oracle/_ref/ by oracle/Makefile) on the seeded
-inputs defined in cases.py and stores its outputs.  Needs the reference
+the reference sources into oracle/_ref/ by oracle/Makefile) and main.c's
+penalty / log-softmax / top-k functions (oracle/ref_search_harness.c) on the
+seeded inputs defined in cases.py and stores their outputs.  Needs the reference
 sources at build time (REF_DIR, default /root/reference); the fixtures are
 committed so that nothing else ever needs them.
 
@@ -36,6 +37,17 @@ def main() -> None:
     for name in cases.CROSS_CASES:
         K, V, q = cases.cross_case(name)
         out[name] = po.ref_cross(K, V, q)
+    for name in cases.PENALTY_CASES:
+        logits, tokens, lens, pen, ngram = cases.penalties_case(name)
+        res = po.ref_penalties(logits, tokens, lens, pen, ngram)
+        idx = np.nonzero((res != logits).reshape(-1))[0].astype(np.int64)
+        out[name + "_idx"] = idx
+        out[name + "_val"] = res.reshape(-1)[idx]
+    for name in cases.TOPK_CASES:
+        logits, k = cases.topk_case(name)
+        tok, sc = po.ref_logsoftmax_topk(logits, k)
+        out[name + "_tok"] = tok
+        out[name + "_logp"] = sc
     np.savez_compressed(cases.GOLDEN_NPZ, **out)
     for k_, v_ in out.items():
         print(f"{k_:22s} {str(v_.shape):22s} sum={float(np.sum(v_, dtype=np.float64)):+.6f}")

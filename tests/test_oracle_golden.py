@@ -78,3 +78,24 @@ def test_reference_harness_reproduces_golden(golden):
     np.testing.assert_array_equal(po.ref_prefill_flash(q, k, v, vl), golden["prefill_small"])
     K, V, qc = cases.cross_case("cross_77")
     np.testing.assert_array_equal(po.ref_cross(K, V, qc), golden["cross_77"])
+
+
+@pytest.mark.parametrize("name", cases.PENALTY_CASES)
+def test_penalties_oracle_matches_reference(golden, name):
+    """Bit for bit: the same fp32 operations in the same order."""
+    logits, tokens, lens, pen, ngram = cases.penalties_case(name)
+    out = po.penalties(logits, tokens, lens, pen, ngram).reshape(-1)
+    idx = np.nonzero(out != logits.reshape(-1))[0]
+    np.testing.assert_array_equal(idx, golden[name + "_idx"])
+    np.testing.assert_array_equal(out[idx], golden[name + "_val"])
+
+
+@pytest.mark.parametrize("name", cases.TOPK_CASES)
+def test_logsoftmax_topk_oracle_matches_reference(golden, name):
+    """Token ids exactly; log-probabilities to 1e-4: the reference sums the
+    256206 exponentials in one fp32 running sum, which drifts by ~5e-5 from
+    the float64 sum of the restatement."""
+    logits, k = cases.topk_case(name)
+    tok, lp = po.logsoftmax_topk(logits, k)
+    np.testing.assert_array_equal(tok, golden[name + "_tok"])
+    np.testing.assert_allclose(lp, golden[name + "_logp"], atol=1e-4, rtol=1e-5)
