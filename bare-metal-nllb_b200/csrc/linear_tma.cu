@@ -97,7 +97,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint64_t* done = empty + STAGES;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
     int* s_abort = reinterpret_cast<int*>(tmem_slot + 1);
-    __shared__ float s_inv[TN];
+    __shared__ __align__(16) float s_inv[TN];
+    __shared__ __align__(16) float s_bias[TN];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int S = splits, z = blockIdx.x % S, mt = blockIdx.x / S;
@@ -125,6 +126,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (!producer) {
         pdl_wait_primary();  // the output may still be read by earlier kernels
         if (tid < TN) s_inv[tid] = (n0 + tid < a.N) ? 1.0f / a.scale[n0 + tid] : 0.f;  // 1/scale as tensor.c:75
+        else if (tid < 2 * TN)
+            s_bias[tid - TN] = (a.bias && n0 + tid - TN < a.N) ? a.bias[n0 + tid - TN] : 0.f;
     }
 
     if (producer) {
@@ -217,54 +220,70 @@ __global__ void __launch_bounds__(THREADS, 1)
         const bool vec = (a.cblock % 4 == 0) && ((reinterpret_cast<uintptr_t>(a.out) & 15) == 0) &&
                          ((reinterpret_cast<uintptr_t>(a.residual) & 15) == 0) &&
                          ((reinterpret_cast<uintptr_t>(a.bias) & 15) == 0);
-        if (vec) {
-            // a warp stores one 128-column row as float4s
-            for (int item = tid; item < R * (TN / 4); item += THREADS) {
-                const int rr = z * R + item / (TN / 4), c4 = item % (TN / 4);
-                const int m = m0 + rr;
-                if (m >= a.M) break;  // rows grow with item
-                const float* src = part + rr * PART_STRIDE + c4 * 4;
-                float4 acc;
-                if (S == 1) {
-                    acc = *reinterpret_cast<const float4*>(src);
-                } else {
-                    float4 p[8];  // all remote loads in flight before the first add
+        if (vec && a.cblock % TN == 0) {
+            // A warp stores one 128-column row as float4s.  THREADS is a
+            // multiple of the 32 float4 of a row, so a thread keeps one column
+            // quad (its factors, bias and mask loaded once) and walks rows
+            // THREADS / 32 apart, kU rows per pass with every load of the pass
+            // issued before its first store.  The tile lies in one column
+            // block, whose offset is found once.
+            static_assert(THREADS % (TN / 4) == 0, "a thread keeps one column quad");
+            constexpr int kU = 4, kRowStep = THREADS / (TN / 4);
+            const int c4 = tid % (TN / 4), nl = c4 * 4, n = n0 + nl;
+            const size_t tile_off = (size_t)(n0 / a.cblock) * ((size_t)a.M * a.cblock) + (n0 % a.cblock) + nl;
+            const float4 inv = *reinterpret_cast<const float4*>(s_inv + nl);
+            const float4 bias = a.bias ? *reinterpret_cast<const float4*>(s_bias + nl) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const bool full4 = n + 3 < a.N;
+            bool masked[4];
 #pragma unroll
-                    for (int r = 0; r < 8; ++r)
-                        if (r < S) p[r] = ld_cluster_f4(map_rank(src, r));
-                    acc = p[0];
+            for (int j = 0; j < 4; ++j) masked[j] = a.mask_from >= 0 && n + j >= a.mask_from;
+            for (int r0 = tid / (TN / 4); r0 < R; r0 += kRowStep * kU) {
+                float4 acc[kU], res[kU];
 #pragma unroll
-                    for (int r = 1; r < 8; ++r)
-                        if (r < S) acc.x += p[r].x, acc.y += p[r].y, acc.z += p[r].z, acc.w += p[r].w;
+                for (int u = 0; u < kU; ++u) {
+                    const int rr = r0 + u * kRowStep;  // row within this rank's share
+                    const int m = m0 + z * R + rr;
+                    const bool live = rr < R && m < a.M;
+                    const float* src = part + (z * R + (live ? rr : 0)) * PART_STRIDE + nl;
+                    if (S == 1) {
+                        acc[u] = *reinterpret_cast<const float4*>(src);
+                    } else {
+                        acc[u] = ld_cluster_f4(map_rank(src, 0));
+                        for (int r = 1; r < S; ++r) {  // rank order: the sum is the same on every run
+                            const float4 q = ld_cluster_f4(map_rank(src, r));
+                            acc[u].x += q.x, acc[u].y += q.y, acc[u].z += q.z, acc[u].w += q.w;
+                        }
+                    }
+                    res[u] = (a.residual && live && full4)
+                                 ? *reinterpret_cast<const float4*>(a.residual + tile_off + (size_t)m * a.cblock)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
-                const int nl = c4 * 4, n = n0 + nl;
-                float y[4] = {acc.x * s_inv[nl], acc.y * s_inv[nl + 1], acc.z * s_inv[nl + 2],
-                              acc.w * s_inv[nl + 3]};
-                if (n + 3 < a.N) {
-                    if (a.bias) {
-                        const float4 b = *reinterpret_cast<const float4*>(a.bias + n);
-                        y[0] += b.x, y[1] += b.y, y[2] += b.z, y[3] += b.w;
-                    }
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        if (a.relu) y[j] = fmaxf(y[j], 0.f);
-                        if (a.mask_from >= 0 && n + j >= a.mask_from) y[j] = -1e30f;
-                    }
-                    const size_t o =
-                        (size_t)(n / a.cblock) * ((size_t)a.M * a.cblock) + (size_t)m * a.cblock + (n % a.cblock);
-                    if (a.residual) {
-                        const float4 r = *reinterpret_cast<const float4*>(a.residual + o);
-                        y[0] += r.x, y[1] += r.y, y[2] += r.z, y[3] += r.w;
-                    }
-                    if (a.out_planes)
-                        store_split3_x4(static_cast<__nv_bfloat16*>(a.out_planes), (size_t)a.M * a.N, o,
-                                        make_float4(y[0], y[1], y[2], y[3]));
-                    else
-                        *reinterpret_cast<float4*>(a.out + o) = make_float4(y[0], y[1], y[2], y[3]);
-                } else {
+                for (int u = 0; u < kU; ++u) {
+                    const int rr = r0 + u * kRowStep;
+                    const int m = m0 + z * R + rr;
+                    if (rr >= R || m >= a.M) continue;
+                    float y[4] = {acc[u].x * inv.x, acc[u].y * inv.y, acc[u].z * inv.z, acc[u].w * inv.w};
+                    if (full4) {
+                        if (a.bias) y[0] += bias.x, y[1] += bias.y, y[2] += bias.z, y[3] += bias.w;
 #pragma unroll
-                    for (int j = 0; j < 4; ++j)
-                        if (n + j < a.N) epilogue_store(a, m, n + j, y[j]);
+                        for (int j = 0; j < 4; ++j) {
+                            if (a.relu) y[j] = fmaxf(y[j], 0.f);
+                            if (masked[j]) y[j] = -1e30f;
+                        }
+                        if (a.residual) y[0] += res[u].x, y[1] += res[u].y, y[2] += res[u].z, y[3] += res[u].w;
+                        const size_t o = tile_off + (size_t)m * a.cblock;
+                        const float4 yv = make_float4(y[0], y[1], y[2], y[3]);
+                        if (a.out_planes) {
+                            store_split3_x4(static_cast<__nv_bfloat16*>(a.out_planes), (size_t)a.M * a.N, o, yv);
+                        } else {
+                            *reinterpret_cast<float4*>(a.out + o) = yv;
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            if (n + j < a.N) epilogue_store(a, m, n + j, y[j]);
+                    }
                 }
             }
         } else {
