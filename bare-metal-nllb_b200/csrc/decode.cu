@@ -26,6 +26,7 @@
 // caches (the reference copies each parent cache, main.c:481-482).
 #include "device_common.cuh"
 #include "kernels.h"
+#include "planes.cuh"
 
 namespace nllb {
 
@@ -42,9 +43,23 @@ constexpr int kBarBytes = 128;  // mbarriers at the start of dynamic shared memo
 // records of each beam and writes out[bb*row_stride + 0..63].  Every thread of
 // every CTA of the cluster calls this (the barriers are cluster-wide), so
 // no CTA leaves while its records may still be read.
+// Where a CTA's output rows go: fp32 rows, or the same element offsets in
+// three bf16 planes.
+struct OutRows {
+    float* out;               // row 0, column 0 of this (sentence, head)
+    __nv_bfloat16* planes;    // same offset in plane 0, or null
+    size_t row_stride, plane_stride;
+    __device__ __forceinline__ void put(int bb, int q4, float4 v) const {
+        if (planes)
+            store_split3_x4(planes, plane_stride, (size_t)bb * row_stride + 4 * q4, v);
+        else
+            reinterpret_cast<float4*>(out + bb * row_stride)[q4] = v;
+    }
+};
+
 template <int NB>
 __device__ __forceinline__ void cluster_merge(const float* rec, const int* abort_flag, int n_split,
-                                              float* out, size_t row_stride) {
+                                              const OutRows& dst) {
     cluster_sync_all();
     if (cluster_ctarank() == 0) {
         bool any_abort = false;
@@ -63,7 +78,7 @@ __device__ __forceinline__ void cluster_merge(const float* rec, const int* abort
                     L = fmaf(w, ld_cluster_f32(base + 4), L);
                     A = f4_fma(w, ld_cluster_f4(base + 16 + 16 * q4), A);
                 }
-                reinterpret_cast<float4*>(out + bb * row_stride)[q4] = f4_scale(A, 1.0f / L);
+                dst.put(bb, q4, f4_scale(A, 1.0f / L));
             }
         }
     }
@@ -207,8 +222,10 @@ __global__ void __launch_bounds__(kThreads) decode_self_kernel(const SelfParams 
 
     float* red = sK;                    // [8 half-warps][68], overlays the ring (free after the loop)
     float* rec = sK + 8 * kPartFloats;  // [NB][68] this CTA's merged records
-    float* out_base = p.out + (size_t)s * NB * p.H * 64 + (size_t)h * 64;
-    const size_t out_stride = (size_t)p.H * 64;
+    const size_t out_off = (size_t)s * NB * p.H * 64 + (size_t)h * 64;
+    const OutRows dst{p.out ? p.out + out_off : nullptr,
+                      p.out_planes ? static_cast<__nv_bfloat16*>(p.out_planes) + out_off : nullptr,
+                      (size_t)p.H * 64, p.plane_stride};
 
     if (s_abort) {
         // let copies still in flight into this CTA's shared memory land, then stop
@@ -253,7 +270,7 @@ __global__ void __launch_bounds__(kThreads) decode_self_kernel(const SelfParams 
             float4 A;
             merge_local(red + bb * kPartFloats, NSUB, NB * kPartFloats, q4, M, L, A);
             if (p.n_split == 1) {
-                reinterpret_cast<float4*>(out_base + bb * out_stride)[q4] = f4_scale(A, 1.0f / L);
+                dst.put(bb, q4, f4_scale(A, 1.0f / L));
             } else {
                 float* r = rec + bb * kPartFloats;
                 if (q4 == 0) {
@@ -264,7 +281,7 @@ __global__ void __launch_bounds__(kThreads) decode_self_kernel(const SelfParams 
             }
         }
     }
-    if (p.n_split > 1) cluster_merge<NB>(rec, &s_abort, p.n_split, out_base, out_stride);
+    if (p.n_split > 1) cluster_merge<NB>(rec, &s_abort, p.n_split, dst);
 }
 
 // ---------------------------------------------------------------------------
@@ -387,8 +404,10 @@ __global__ void __launch_bounds__(kThreads) cross_kernel(const CrossParams p) {
 
     float* red = sK;                         // [8 half-warps][NB][68], overlays the ring
     float* rec = sK + 8 * NB * kPartFloats;  // [NB][68]
-    float* out_base = p.out + (size_t)s * NB * p.H * 64 + (size_t)h * 64;
-    const size_t out_stride = (size_t)p.H * 64;
+    const size_t out_off = (size_t)s * NB * p.H * 64 + (size_t)h * 64;
+    const OutRows dst{p.out ? p.out + out_off : nullptr,
+                      p.out_planes ? static_cast<__nv_bfloat16*>(p.out_planes) + out_off : nullptr,
+                      (size_t)p.H * 64, p.plane_stride};
 
     if (s_abort) {
         if (tid == 0) {
@@ -415,7 +434,7 @@ __global__ void __launch_bounds__(kThreads) cross_kernel(const CrossParams p) {
             float4 A;
             merge_local(red + bb * kPartFloats, 8, NB * kPartFloats, q4, M, L, A);
             if (p.n_split == 1) {
-                reinterpret_cast<float4*>(out_base + bb * out_stride)[q4] = f4_scale(A, 1.0f / L);
+                dst.put(bb, q4, f4_scale(A, 1.0f / L));
             } else {
                 float* r = rec + bb * kPartFloats;
                 if (q4 == 0) {
@@ -426,7 +445,7 @@ __global__ void __launch_bounds__(kThreads) cross_kernel(const CrossParams p) {
             }
         }
     }
-    if (p.n_split > 1) cluster_merge<NB>(rec, &s_abort, p.n_split, out_base, out_stride);
+    if (p.n_split > 1) cluster_merge<NB>(rec, &s_abort, p.n_split, dst);
 }
 
 // ---------------------------------------------------------------------------

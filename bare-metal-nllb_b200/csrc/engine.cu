@@ -632,13 +632,26 @@ int decode_step(nllb_model* m, Work& w, int step) {
         auto& Dl = m->dec[l];
         ENG_CK(launch_layernorm(lnout, w.x, nullptr, Dl.ln1g, Dl.ln1b, R, P1, m->stream));
         ENG_RC(run_linear(m, Dl.qkv, w.h, R, w.qkv, nullptr, 0, D, -1, P1));
-        ENG_RC(nllb_attn_decode_self(m->attn, l, step, w.n_sent, w.qkv, w.qkv + (size_t)R * D,
-                                     w.qkv + (size_t)2 * R * D, w.attn));
-        ENG_RC(run_linear(m, Dl.out, w.attn, R, w.x, w.x, 0, D));
+        // on the tensor-core path the attention kernels write the output
+        // projection's bf16 planes themselves (no fp32 output, no split pass)
+        if (tp && tma_path(m, Dl.out, R)) {
+            ENG_RC(nllb::attn_decode_self_planes(m->attn, l, step, w.n_sent, w.qkv, w.qkv + (size_t)R * D,
+                                                 w.qkv + (size_t)2 * R * D, m->planes, (size_t)R * D));
+            ENG_RC(run_linear(m, Dl.out, w.attn, R, w.x, w.x, 0, D, -1, m->planes));
+        } else {
+            ENG_RC(nllb_attn_decode_self(m->attn, l, step, w.n_sent, w.qkv, w.qkv + (size_t)R * D,
+                                         w.qkv + (size_t)2 * R * D, w.attn));
+            ENG_RC(run_linear(m, Dl.out, w.attn, R, w.x, w.x, 0, D));
+        }
         ENG_CK(launch_layernorm(lnout, w.x, nullptr, Dl.ln2g, Dl.ln2b, R, P1, m->stream));
         ENG_RC(run_linear(m, Dl.xq, w.h, R, w.qx, nullptr, 0, D, -1, P1));
-        ENG_RC(nllb_attn_cross(m->attn, l, w.n_sent, w.qx, w.attn));
-        ENG_RC(run_linear(m, Dl.xout, w.attn, R, w.x, w.x, 0, D));
+        if (tp && tma_path(m, Dl.xout, R)) {
+            ENG_RC(nllb::attn_cross_planes(m->attn, l, w.n_sent, w.qx, m->planes, (size_t)R * D));
+            ENG_RC(run_linear(m, Dl.xout, w.attn, R, w.x, w.x, 0, D, -1, m->planes));
+        } else {
+            ENG_RC(nllb_attn_cross(m->attn, l, w.n_sent, w.qx, w.attn));
+            ENG_RC(run_linear(m, Dl.xout, w.attn, R, w.x, w.x, 0, D));
+        }
         ENG_CK(launch_layernorm(lnout, w.x, nullptr, Dl.ln3g, Dl.ln3b, R, P1, m->stream));
         ENG_RC(run_linear(m, Dl.fc1, w.h, R, w.ffn, nullptr, 1, FFN, -1, P1, P2));
         ENG_RC(run_linear(m, Dl.fc2, w.ffn, R, w.x, w.x, 0, D, -1, P2));

@@ -53,6 +53,11 @@ struct SelfParams {
     const float* k_new;
     const float* v_new;
     float* out;
+    // optional: instead of out, the three bf16 planes of the output (x = p0 +
+    // p1 + p2, planes.cuh) at the same element offsets, plane_stride elements
+    // apart -- the A operand of the output projection
+    void* out_planes = nullptr;
+    size_t plane_stride = 0;
     int H, T, Tp;
     int step;             // position of the new token; cache holds 0..step-1
     int n_split, pos_per_split;
@@ -68,6 +73,8 @@ struct CrossParams {
     const int* n_src;     // [S] rows per sentence for this layer
     const float* q;       // [n_sent][n_beams][H*64]
     float* out;
+    void* out_planes = nullptr;  // as in SelfParams
+    size_t plane_stride = 0;
     int H, max_src;
     int n_split, pos_per_split;
     float scale_log2;
