@@ -223,3 +223,30 @@ def test_cross_many_sentences_no_split(cuda_device):
         out = dout.cpu().numpy()
     for s in (0, 17, 63):
         assert_attn_close(out[s], po.cross(K[s], V[s], q[s]), f"s{s}")
+
+
+@pytest.mark.parametrize("max_len", [130, 200])
+def test_cross_many_ragged_sentences(cuda_device, max_len):
+    """72 sentences (no split-KV) with memories of every length from 1 up
+    (16-row chunks up to 160 rows, 32-row chunks beyond): every sentence
+    against the oracle."""
+    import torch
+    rng = np.random.default_rng(7 + max_len)
+    NB = 4
+    lens = [1, 2, 15, 16, 17, max_len] + [int(x) for x in rng.integers(1, max_len + 1, size=66)]
+    n_sent = len(lens)
+    with na.Context(0, n_layers=1, max_sentences=n_sent, n_beams=NB, max_tgt=4, max_src=max_len) as ctx:
+        mem = []
+        for s, n in enumerate(lens):
+            K, V = (rng.standard_normal((n, 1024), dtype=np.float32) for _ in range(2))
+            mem.append((K, V))
+            ctx.set_memory_host(0, s, n, K, V, 64, 1024)
+        q = rng.standard_normal((n_sent, NB, 1024), dtype=np.float32)
+        dq = torch.from_numpy(q).cuda()
+        dout = torch.zeros_like(dq)
+        ctx.cross(0, n_sent, dq, dout)
+        ctx.sync()
+        out = dout.cpu().numpy()
+    for s in range(n_sent):
+        K, V = mem[s]
+        assert_attn_close(out[s], po.cross(K, V, q[s]), f"s{s} len {lens[s]}")
