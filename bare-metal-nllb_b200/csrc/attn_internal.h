@@ -46,9 +46,9 @@ struct nllb_attn_ctx {
 namespace nllb {
 // The engine's forms of nllb_attn_decode_self / nllb_attn_cross (device
 // buffers): the output goes out as the three bf16 planes of the output
-// projection's input (planes.cuh) at the fp32 output's element offsets,
-// plane_stride elements apart.  Not exported.
+// projection's input (planes.cuh) at the fp32 output's element offsets, one
+// plane per n_sent * n_beams * H * 64 elements.  Not exported.
 int attn_decode_self_planes(nllb_attn_ctx* c, int layer, int step, int n_sent, const float* q, const float* k_new,
-                            const float* v_new, void* planes, size_t plane_stride);
-int attn_cross_planes(nllb_attn_ctx* c, int layer, int n_sent, const float* q, void* planes, size_t plane_stride);
+                            const float* v_new, void* planes);
+int attn_cross_planes(nllb_attn_ctx* c, int layer, int n_sent, const float* q, void* planes);
 }  // namespace nllb

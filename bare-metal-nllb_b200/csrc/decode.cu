@@ -43,23 +43,41 @@ constexpr int kBarBytes = 128;  // mbarriers at the start of dynamic shared memo
 // records of each beam and writes out[bb*row_stride + 0..63].  Every thread of
 // every CTA of the cluster calls this (the barriers are cluster-wide), so
 // no CTA leaves while its records may still be read.
-// Where a CTA's output rows go: fp32 rows, or the same element offsets in
-// three bf16 planes.
-struct OutRows {
-    float* out;               // row 0, column 0 of this (sentence, head)
-    __nv_bfloat16* planes;    // same offset in plane 0, or null
-    size_t row_stride, plane_stride;
+// Where a CTA's output rows go: fp32 rows, or (PLANES) the same element
+// offsets in three bf16 planes.  A template parameter, so that the fp32 form
+// compiles exactly as a kernel without the option.
+template <bool PLANES>
+struct OutRows;
+template <>
+struct OutRows<false> {
+    float* out;  // row 0, column 0 of this (sentence, head)
+    size_t row_stride;
     __device__ __forceinline__ void put(int bb, int q4, float4 v) const {
-        if (planes)
-            store_split3_x4(planes, plane_stride, (size_t)bb * row_stride + 4 * q4, v);
-        else
-            reinterpret_cast<float4*>(out + bb * row_stride)[q4] = v;
+        reinterpret_cast<float4*>(out + bb * row_stride)[q4] = v;
     }
 };
+template <>
+struct OutRows<true> {
+    __nv_bfloat16* planes;  // the same offset in plane 0
+    size_t row_stride, plane_stride;
+    __device__ __forceinline__ void put(int bb, int q4, float4 v) const {
+        store_split3_x4(planes, plane_stride, (size_t)bb * row_stride + 4 * q4, v);
+    }
+};
+// PLANES: p.out is the base of three bf16 planes covering the launch's rows
+// (gridDim.z sentences x NB beams x H heads x 64), one plane after the other.
+template <bool PLANES, int NB, typename Params>
+__device__ __forceinline__ OutRows<PLANES> out_rows(const Params& p, size_t off) {
+    if constexpr (PLANES)
+        return OutRows<true>{reinterpret_cast<__nv_bfloat16*>(p.out) + off, (size_t)p.H * 64,
+                             (size_t)gridDim.z * NB * p.H * 64};
+    else
+        return OutRows<false>{p.out + off, (size_t)p.H * 64};
+}
 
-template <int NB>
+template <int NB, typename Dst>
 __device__ __forceinline__ void cluster_merge(const float* rec, const int* abort_flag, int n_split,
-                                              const OutRows& dst) {
+                                              const Dst& dst) {
     cluster_sync_all();
     if (cluster_ctarank() == 0) {
         bool any_abort = false;
@@ -104,7 +122,7 @@ __device__ __forceinline__ void merge_local(const float* recs, int nsrc, int str
 // ---------------------------------------------------------------------------
 // Decoder self-attention
 // ---------------------------------------------------------------------------
-template <int NB>
+template <int NB, bool PLANES>
 __global__ void __launch_bounds__(kThreads) decode_self_kernel(const SelfParams p) {
     constexpr int CP = kSelfChunkRows / NB;  // positions per chunk
     constexpr int NSUB = 8 / NB;         // half-warps per beam
@@ -223,9 +241,7 @@ __global__ void __launch_bounds__(kThreads) decode_self_kernel(const SelfParams 
     float* red = sK;                    // [8 half-warps][68], overlays the ring (free after the loop)
     float* rec = sK + 8 * kPartFloats;  // [NB][68] this CTA's merged records
     const size_t out_off = (size_t)s * NB * p.H * 64 + (size_t)h * 64;
-    const OutRows dst{p.out ? p.out + out_off : nullptr,
-                      p.out_planes ? static_cast<__nv_bfloat16*>(p.out_planes) + out_off : nullptr,
-                      (size_t)p.H * 64, p.plane_stride};
+    const auto dst = out_rows<PLANES, NB>(p, out_off);
 
     if (s_abort) {
         // let copies still in flight into this CTA's shared memory land, then stop
@@ -287,7 +303,7 @@ __global__ void __launch_bounds__(kThreads) decode_self_kernel(const SelfParams 
 // ---------------------------------------------------------------------------
 // Cross-attention: all beams of a sentence share each memory row.
 // ---------------------------------------------------------------------------
-template <int NB, int CP, int kCrossStages>
+template <int NB, int CP, int kCrossStages, bool PLANES>
 __global__ void __launch_bounds__(kThreads) cross_kernel(const CrossParams p) {
     constexpr int RPH = CP / 8;  // rows per half-warp per chunk
     constexpr int KV_FLOATS = CP * 64;
@@ -405,9 +421,7 @@ __global__ void __launch_bounds__(kThreads) cross_kernel(const CrossParams p) {
     float* red = sK;                         // [8 half-warps][NB][68], overlays the ring
     float* rec = sK + 8 * NB * kPartFloats;  // [NB][68]
     const size_t out_off = (size_t)s * NB * p.H * 64 + (size_t)h * 64;
-    const OutRows dst{p.out ? p.out + out_off : nullptr,
-                      p.out_planes ? static_cast<__nv_bfloat16*>(p.out_planes) + out_off : nullptr,
-                      (size_t)p.H * 64, p.plane_stride};
+    const auto dst = out_rows<PLANES, NB>(p, out_off);
 
     if (s_abort) {
         if (tid == 0) {
@@ -557,38 +571,59 @@ cudaError_t launch_ex(void (*kernel)(Params), dim3 grid, size_t smem, int cluste
     return cudaLaunchKernelEx(&cfg, kernel, p);
 }
 
-template <int NB>
-cudaError_t configure_nb() {
-    cudaError_t e = cudaFuncSetAttribute(decode_self_kernel<NB>,
+template <int NB, bool PLANES>
+cudaError_t configure_nb_out() {
+    cudaError_t e = cudaFuncSetAttribute(decode_self_kernel<NB, PLANES>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)self_smem_bytes<NB>());
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(cross_kernel<NB, kCrossShortRows, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(cross_kernel<NB, kCrossShortRows, 3, PLANES>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)cross_smem_bytes<NB, kCrossShortRows, 3>());
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(cross_kernel<NB, kCrossLongRows, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(cross_kernel<NB, kCrossLongRows, 3, PLANES>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)cross_smem_bytes<NB, kCrossLongRows, 3>());
     if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(cross_kernel<NB, kCrossSplitRows, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    return cudaFuncSetAttribute(cross_kernel<NB, kCrossSplitRows, 2, PLANES>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)cross_smem_bytes<NB, kCrossSplitRows, 2>());
 }
 
 template <int NB>
-cudaError_t launch_self_nb(const SelfParams& p, int n_sent, cudaStream_t st) {
-    return launch_ex(decode_self_kernel<NB>, dim3(p.n_split, p.H, n_sent), self_smem_bytes<NB>(),
+cudaError_t configure_nb() {
+    cudaError_t e = configure_nb_out<NB, false>();
+    if (e != cudaSuccess) return e;
+    return configure_nb_out<NB, true>();
+}
+
+template <int NB, bool PLANES>
+cudaError_t launch_self_out(const SelfParams& p, int n_sent, cudaStream_t st) {
+    return launch_ex(decode_self_kernel<NB, PLANES>, dim3(p.n_split, p.H, n_sent), self_smem_bytes<NB>(),
                      p.n_split, st, p);
 }
 
 template <int NB>
-cudaError_t launch_cross_nb(const CrossParams& p, int n_sent, int chunk_rows, cudaStream_t st) {
+cudaError_t launch_self_nb(const SelfParams& p, int n_sent, cudaStream_t st, bool planes) {
+    return planes ? launch_self_out<NB, true>(p, n_sent, st) : launch_self_out<NB, false>(p, n_sent, st);
+}
+
+template <int NB, bool PLANES>
+cudaError_t launch_cross_out(const CrossParams& p, int n_sent, int chunk_rows, cudaStream_t st) {
     if (chunk_rows == kCrossSplitRows)
-        return launch_ex(cross_kernel<NB, kCrossSplitRows, 2>, dim3(p.n_split, p.H, n_sent),
+        return launch_ex(cross_kernel<NB, kCrossSplitRows, 2, PLANES>, dim3(p.n_split, p.H, n_sent),
                          cross_smem_bytes<NB, kCrossSplitRows, 2>(), p.n_split, st, p);
     if (chunk_rows == kCrossLongRows)
-        return launch_ex(cross_kernel<NB, kCrossLongRows, 3>, dim3(p.n_split, p.H, n_sent),
+        return launch_ex(cross_kernel<NB, kCrossLongRows, 3, PLANES>, dim3(p.n_split, p.H, n_sent),
                          cross_smem_bytes<NB, kCrossLongRows, 3>(), p.n_split, st, p);
-    return launch_ex(cross_kernel<NB, kCrossShortRows, 3>, dim3(p.n_split, p.H, n_sent),
+    return launch_ex(cross_kernel<NB, kCrossShortRows, 3, PLANES>, dim3(p.n_split, p.H, n_sent),
                      cross_smem_bytes<NB, kCrossShortRows, 3>(), p.n_split, st, p);
+}
+
+template <int NB>
+cudaError_t launch_cross_nb(const CrossParams& p, int n_sent, int chunk_rows, cudaStream_t st, bool planes) {
+    return planes ? launch_cross_out<NB, true>(p, n_sent, chunk_rows, st)
+                  : launch_cross_out<NB, false>(p, n_sent, chunk_rows, st);
 }
 
 }  // namespace
@@ -601,22 +636,23 @@ cudaError_t configure_decode_kernels() {
     return configure_nb<8>();
 }
 
-cudaError_t launch_decode_self(const SelfParams& p, int n_sent, int n_beams, cudaStream_t st) {
+cudaError_t launch_decode_self(const SelfParams& p, int n_sent, int n_beams, cudaStream_t st, bool planes) {
     switch (n_beams) {
-        case 1: return launch_self_nb<1>(p, n_sent, st);
-        case 2: return launch_self_nb<2>(p, n_sent, st);
-        case 4: return launch_self_nb<4>(p, n_sent, st);
-        case 8: return launch_self_nb<8>(p, n_sent, st);
+        case 1: return launch_self_nb<1>(p, n_sent, st, planes);
+        case 2: return launch_self_nb<2>(p, n_sent, st, planes);
+        case 4: return launch_self_nb<4>(p, n_sent, st, planes);
+        case 8: return launch_self_nb<8>(p, n_sent, st, planes);
         default: return cudaErrorInvalidValue;
     }
 }
 
-cudaError_t launch_cross(const CrossParams& p, int n_sent, int n_beams, int chunk_rows, cudaStream_t st) {
+cudaError_t launch_cross(const CrossParams& p, int n_sent, int n_beams, int chunk_rows, cudaStream_t st,
+                         bool planes) {
     switch (n_beams) {
-        case 1: return launch_cross_nb<1>(p, n_sent, chunk_rows, st);
-        case 2: return launch_cross_nb<2>(p, n_sent, chunk_rows, st);
-        case 4: return launch_cross_nb<4>(p, n_sent, chunk_rows, st);
-        case 8: return launch_cross_nb<8>(p, n_sent, chunk_rows, st);
+        case 1: return launch_cross_nb<1>(p, n_sent, chunk_rows, st, planes);
+        case 2: return launch_cross_nb<2>(p, n_sent, chunk_rows, st, planes);
+        case 4: return launch_cross_nb<4>(p, n_sent, chunk_rows, st, planes);
+        case 8: return launch_cross_nb<8>(p, n_sent, chunk_rows, st, planes);
         default: return cudaErrorInvalidValue;
     }
 }

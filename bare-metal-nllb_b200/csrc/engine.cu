@@ -636,7 +636,7 @@ int decode_step(nllb_model* m, Work& w, int step) {
         // projection's bf16 planes themselves (no fp32 output, no split pass)
         if (tp && tma_path(m, Dl.out, R)) {
             ENG_RC(nllb::attn_decode_self_planes(m->attn, l, step, w.n_sent, w.qkv, w.qkv + (size_t)R * D,
-                                                 w.qkv + (size_t)2 * R * D, m->planes, (size_t)R * D));
+                                                 w.qkv + (size_t)2 * R * D, m->planes));
             ENG_RC(run_linear(m, Dl.out, w.attn, R, w.x, w.x, 0, D, -1, m->planes));
         } else {
             ENG_RC(nllb_attn_decode_self(m->attn, l, step, w.n_sent, w.qkv, w.qkv + (size_t)R * D,
@@ -646,7 +646,7 @@ int decode_step(nllb_model* m, Work& w, int step) {
         ENG_CK(launch_layernorm(lnout, w.x, nullptr, Dl.ln2g, Dl.ln2b, R, P1, m->stream));
         ENG_RC(run_linear(m, Dl.xq, w.h, R, w.qx, nullptr, 0, D, -1, P1));
         if (tp && tma_path(m, Dl.xout, R)) {
-            ENG_RC(nllb::attn_cross_planes(m->attn, l, w.n_sent, w.qx, m->planes, (size_t)R * D));
+            ENG_RC(nllb::attn_cross_planes(m->attn, l, w.n_sent, w.qx, m->planes));
             ENG_RC(run_linear(m, Dl.xout, w.attn, R, w.x, w.x, 0, D, -1, m->planes));
         } else {
             ENG_RC(nllb_attn_cross(m->attn, l, w.n_sent, w.qx, w.attn));

@@ -52,18 +52,21 @@ struct SelfParams {
     const float* q;       // [n_sent][n_beams][H*64]
     const float* k_new;
     const float* v_new;
+    // fp32 output, or (launch_decode_self with planes) the three bf16 planes
+    // of the output (x = p0 + p1 + p2, planes.cuh) at the same element
+    // offsets, one plane per n_sent * n_beams * H * 64 elements: the A operand
+    // of the output projection
     float* out;
-    // optional: instead of out, the three bf16 planes of the output (x = p0 +
-    // p1 + p2, planes.cuh) at the same element offsets, plane_stride elements
-    // apart -- the A operand of the output projection
-    void* out_planes = nullptr;
-    size_t plane_stride = 0;
     int H, T, Tp;
     int step;             // position of the new token; cache holds 0..step-1
     int n_split, pos_per_split;
     float scale_log2;     // scale * log2(e)
     int* err;
 };
+
+// (Adding fields to SelfParams changed the register allocation of the
+// self-attention kernel -- 48 to 40 registers -- and cost 4 % of its stream
+// rate on B200; the plane output therefore reuses `out`.)
 
 // ---- cross-attention (decode.cu) ------------------------------------------
 // Memory layout of one layer: [sentence][head][max_src][64] fp32, K and V.
@@ -72,9 +75,7 @@ struct CrossParams {
     const float* vm;
     const int* n_src;     // [S] rows per sentence for this layer
     const float* q;       // [n_sent][n_beams][H*64]
-    float* out;
-    void* out_planes = nullptr;  // as in SelfParams
-    size_t plane_stride = 0;
+    float* out;           // as in SelfParams
     int H, max_src;
     int n_split, pos_per_split;
     float scale_log2;
@@ -100,9 +101,11 @@ struct PrefillParams {
 cudaError_t configure_decode_kernels();
 cudaError_t configure_prefill_kernels();
 
-cudaError_t launch_decode_self(const SelfParams& p, int n_sent, int n_beams, cudaStream_t st);
+// planes: p.out is the base of the output planes (see SelfParams::out)
+cudaError_t launch_decode_self(const SelfParams& p, int n_sent, int n_beams, cudaStream_t st, bool planes = false);
 // chunk_rows: cross_chunk_rows(longest memory of the call)
-cudaError_t launch_cross(const CrossParams& p, int n_sent, int n_beams, int chunk_rows, cudaStream_t st);
+cudaError_t launch_cross(const CrossParams& p, int n_sent, int n_beams, int chunk_rows, cudaStream_t st,
+                         bool planes = false);
 cudaError_t launch_reorder(uint8_t* hist, int Tp, const int* parent, int n_sent, int n_beams,
                            int* err, cudaStream_t st);
 cudaError_t launch_hist_init(uint8_t* hist, int Tp, int n_sent, cudaStream_t st);

@@ -403,9 +403,9 @@ static int check_beam_call(nllb_attn_ctx* c, int layer, int n_sent) {
 }
 
 // Sentences s0 .. s0 + n_sent - 1; q, k_new, v_new, out point at sentence s0.
+// planes: `out` is the base of the output planes of these n_sent sentences
 static int decode_self_dev(nllb_attn_ctx* c, int layer, int step, int s0, int n_sent, const float* q,
-                           const float* k_new, const float* v_new, float* out, void* out_planes = nullptr,
-                           size_t plane_stride = 0) {
+                           const float* k_new, const float* v_new, float* out, bool planes = false) {
     const nllb_attn_dims& d = c->d;
     const size_t layer_floats = (size_t)d.max_sentences * d.n_heads * (size_t)d.max_tgt * d.n_beams * 64;
     const size_t sent_floats = (size_t)d.n_heads * d.max_tgt * d.n_beams * 64;
@@ -420,8 +420,6 @@ static int decode_self_dev(nllb_attn_ctx* c, int layer, int step, int s0, int n_
     p.k_new = k_new;
     p.v_new = v_new;
     p.out = out;
-    p.out_planes = out_planes;
-    p.plane_stride = plane_stride;
     p.H = d.n_heads;
     p.T = d.max_tgt;
     p.Tp = c->Tp;
@@ -430,7 +428,7 @@ static int decode_self_dev(nllb_attn_ctx* c, int layer, int step, int s0, int n_
                  &p.pos_per_split);
     p.scale_log2 = (1.0f / std::sqrt(64.0f)) * kLog2e;
     p.err = c->err;
-    NLLB_CK(launch_decode_self(p, n_sent, d.n_beams, c->stream));
+    NLLB_CK(launch_decode_self(p, n_sent, d.n_beams, c->stream, planes));
     return NLLB_ATTN_OK;
 }
 
@@ -587,8 +585,7 @@ int nllb_attn_set_memory_host(nllb_attn_ctx* c, int layer, int sentence, int n_s
     return finish_host_call(c);
 }
 
-static int cross_dev(nllb_attn_ctx* c, int layer, int n_sent, const float* q, float* out,
-                     void* out_planes = nullptr, size_t plane_stride = 0) {
+static int cross_dev(nllb_attn_ctx* c, int layer, int n_sent, const float* q, float* out, bool planes = false) {
     const nllb_attn_dims& d = c->d;
     int max_len = 0;
     for (int s = 0; s < n_sent; ++s) {
@@ -603,8 +600,6 @@ static int cross_dev(nllb_attn_ctx* c, int layer, int n_sent, const float* q, fl
     p.n_src = c->n_src_dev + (size_t)layer * d.max_sentences;
     p.q = q;
     p.out = out;
-    p.out_planes = out_planes;
-    p.plane_stride = plane_stride;
     p.H = d.n_heads;
     p.max_src = d.max_src;
     int chunk_rows = cross_chunk_rows(max_len);
@@ -615,7 +610,7 @@ static int cross_dev(nllb_attn_ctx* c, int layer, int n_sent, const float* q, fl
     }
     p.scale_log2 = (1.0f / std::sqrt(64.0f)) * kLog2e;
     p.err = c->err;
-    NLLB_CK(launch_cross(p, n_sent, d.n_beams, chunk_rows, c->stream));
+    NLLB_CK(launch_cross(p, n_sent, d.n_beams, chunk_rows, c->stream, planes));
     return NLLB_ATTN_OK;
 }
 
@@ -633,21 +628,21 @@ int nllb_attn_cross(nllb_attn_ctx* c, int layer, int n_sent, const float* q, flo
 namespace nllb {
 
 int attn_decode_self_planes(nllb_attn_ctx* c, int layer, int step, int n_sent, const float* q, const float* k_new,
-                            const float* v_new, void* planes, size_t plane_stride) {
+                            const float* v_new, void* planes) {
     int rc = check_beam_call(c, layer, n_sent);
     if (rc) return rc;
     if (step < 0 || step >= c->d.max_tgt) return fail(NLLB_ATTN_EINVAL, "step out of range");
     if (!q || !k_new || !v_new || !planes) return fail(NLLB_ATTN_EINVAL, "q, k_new, v_new, planes are required");
     if ((rc = set_device(c))) return rc;
-    return decode_self_dev(c, layer, step, 0, n_sent, q, k_new, v_new, nullptr, planes, plane_stride);
+    return decode_self_dev(c, layer, step, 0, n_sent, q, k_new, v_new, static_cast<float*>(planes), true);
 }
 
-int attn_cross_planes(nllb_attn_ctx* c, int layer, int n_sent, const float* q, void* planes, size_t plane_stride) {
+int attn_cross_planes(nllb_attn_ctx* c, int layer, int n_sent, const float* q, void* planes) {
     int rc = check_beam_call(c, layer, n_sent);
     if (rc) return rc;
     if (!q || !planes) return fail(NLLB_ATTN_EINVAL, "q and planes are required");
     if ((rc = set_device(c))) return rc;
-    return cross_dev(c, layer, n_sent, q, nullptr, planes, plane_stride);
+    return cross_dev(c, layer, n_sent, q, static_cast<float*>(planes), true);
 }
 
 }  // namespace nllb
