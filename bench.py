@@ -127,7 +127,7 @@ def parse_args():
     ap.add_argument("--cpu-sample-s", type=float, default=10.0)
     ap.add_argument("--translate-sentences", type=int, default=1024,
                     help="sentences of the sentence-batched translation (0: skip translation)")
-    ap.add_argument("--ncu-case", choices=("decode", "decode1", "cross", "prefill", "linear", "translate"),
+    ap.add_argument("--ncu-case", choices=("decode", "decode1", "cross", "prefill", "linear", "translate", "topk"),
                     help="run one small fixed case for an ncu capture and exit")
     return ap.parse_args()
 
@@ -586,7 +586,17 @@ def ncu_case(which: str) -> None:
             _, _, st = m.translate(srcs, sm.LANG["fra_Latn"], max_gen=40)
         print(f"ncu case translate: ok, {st.tokens_out} tokens in {st.steps} steps")
         return
-
+    elif which == "topk":
+        # log-softmax + top-8 over the vocabulary for 512 rows (a decode step of
+        # 128 sentences x 4 beams): 525 MB of logits > L2; 3 calls
+        V, R = 256206, 512
+        logits = torch.randn((R, V), generator=g, device=dev) * 3.0
+        for _ in range(3):
+            na.logsoftmax_topk(logits, 8)
+        torch.cuda.synchronize()
+        print("ncu case topk: ok")
+        return
+    elif which == "prefill":
         B, S = 8, 128
         c = na.Context(0, n_layers=0, max_sentences=0)
         qp, kp, vp = (torch.randn((B, HEADS, S, HEAD_DIM), generator=g, device=dev) for _ in range(3))
