@@ -385,10 +385,19 @@ __global__ void __launch_bounds__(kThreads) cross_kernel(const CrossParams p) {
             const bool ok = r < np;
             float4 kv = make_float4(0.f, 0.f, 0.f, 0.f);
             if (ok) kv = reinterpret_cast<const float4*>(K + r * 64)[l16];
+            if constexpr (NB == 4) {
+                float pd[4], d[4];
 #pragma unroll
-            for (int b = 0; b < NB; ++b) {
-                const float d = halfwarp_sum(f4_dot(qv[b], kv));
-                sc[b][i] = ok ? d * p.scale_log2 : -INFINITY;
+                for (int b = 0; b < 4; ++b) pd[b] = f4_dot(qv[b], kv);
+                halfwarp_sum4(pd, d);
+#pragma unroll
+                for (int b = 0; b < 4; ++b) sc[b][i] = ok ? d[b] * p.scale_log2 : -INFINITY;
+            } else {
+#pragma unroll
+                for (int b = 0; b < NB; ++b) {
+                    const float d = halfwarp_sum(f4_dot(qv[b], kv));
+                    sc[b][i] = ok ? d * p.scale_log2 : -INFINITY;
+                }
             }
         }
         float mn[NB];

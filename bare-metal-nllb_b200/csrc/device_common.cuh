@@ -102,6 +102,29 @@ __device__ __forceinline__ float halfwarp_sum(float x) {
     return x;
 }
 
+// Four half-warp sums at once (four beams' partial dots of one row), each
+// bit for bit halfwarp_sum(v[b]): partners swap the beams they do not keep
+// (xor 8: two, xor 4: one), so every addition is one that halfwarp_sum makes
+// for that beam; two more tree steps and a broadcast follow.  9 shuffles and
+// 5 adds instead of 16 and 16.
+__device__ __forceinline__ void halfwarp_sum4(const float (&v)[4], float (&out)[4]) {
+    const int lane = threadIdx.x & 31;
+    const bool hi8 = (lane & 8) != 0, hi4 = (lane & 4) != 0;
+    const float r0 = __shfl_xor_sync(0xffffffffu, hi8 ? v[0] : v[2], 8);
+    const float r1 = __shfl_xor_sync(0xffffffffu, hi8 ? v[1] : v[3], 8);
+    const float a0 = (hi8 ? v[2] : v[0]) + r0;  // beam 2*hi8
+    const float a1 = (hi8 ? v[3] : v[1]) + r1;  // beam 2*hi8 + 1
+    const float r = __shfl_xor_sync(0xffffffffu, hi4 ? a0 : a1, 4);
+    float t = (hi4 ? a1 : a0) + r;  // beam 2*hi8 + hi4
+    t += __shfl_xor_sync(0xffffffffu, t, 2);
+    t += __shfl_xor_sync(0xffffffffu, t, 1);
+    const int base = lane & 16;
+    out[0] = __shfl_sync(0xffffffffu, t, base);
+    out[1] = __shfl_sync(0xffffffffu, t, base + 4);
+    out[2] = __shfl_sync(0xffffffffu, t, base + 8);
+    out[3] = __shfl_sync(0xffffffffu, t, base + 12);
+}
+
 // exp2 of a difference that may be -inf - -inf (empty state): weight 0.
 __device__ __forceinline__ float safe_exp2_diff(float a, float m) {
     return (a == -INFINITY) ? 0.0f : exp2f(a - m);

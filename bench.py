@@ -127,7 +127,8 @@ def parse_args():
     ap.add_argument("--cpu-sample-s", type=float, default=10.0)
     ap.add_argument("--translate-sentences", type=int, default=1024,
                     help="sentences of the sentence-batched translation (0: skip translation)")
-    ap.add_argument("--ncu-case", choices=("decode", "decode1", "cross", "prefill", "linear", "translate", "topk"),
+    ap.add_argument("--ncu-case", choices=("decode", "decode1", "cross", "cross128", "prefill", "linear", "translate",
+                                           "topk"),
                     help="run one small fixed case for an ncu capture and exit")
     return ap.parse_args()
 
@@ -586,6 +587,19 @@ def ncu_case(which: str) -> None:
             _, _, st = m.translate(srcs, sm.LANG["fra_Latn"], max_gen=40)
         print(f"ncu case translate: ok, {st.tokens_out} tokens in {st.steps} steps")
         return
+    elif which == "cross128":
+        # cross-attention at the 8-GPU shard's size: 128 sentences x 4 beams, memories of 18..130
+        # rows (config 4's source lengths + 2), written once; 3 calls
+        n = 128
+        lens = [int(len(x)) for x in config4_sources(n)]
+        c = na.Context(0, n_layers=1, max_sentences=n, n_beams=BEAMS, max_tgt=4, max_src=max(lens))
+        for s_, L in enumerate(lens):
+            Km, Vm = (torch.randn((L, DMODEL), generator=g, device=dev) for _ in range(2))
+            c.set_memory(0, s_, L, Km, Vm, HEAD_DIM, DMODEL)
+        qc = torch.randn((n, BEAMS, DMODEL), generator=g, device=dev)
+        oc = torch.empty_like(qc)
+        for _ in range(3):
+            c.cross(0, n, qc, oc)
     elif which == "topk":
         # log-softmax + top-8 over the vocabulary for 512 rows (a decode step of
         # 128 sentences x 4 beams): 525 MB of logits > L2; 3 calls
