@@ -51,4 +51,8 @@ namespace nllb {
 int attn_decode_self_planes(nllb_attn_ctx* c, int layer, int step, int n_sent, const float* q, const float* k_new,
                             const float* v_new, void* planes);
 int attn_cross_planes(nllb_attn_ctx* c, int layer, int n_sent, const float* q, void* planes);
+// nllb_attn_prefill over packed rows: sequence b's row r at row_start[b] + r
+// (device array; stride_batch unused); only its valid_len[b] >= 1 rows are
+// read and written.  Not exported.
+int attn_prefill_packed(nllb_attn_ctx* c, const nllb_attn_prefill_args* a, const int* row_start);
 }  // namespace nllb

@@ -542,6 +542,7 @@ struct Work {
     int n_sent = 0, S = 0, rows_enc = 0, rows = 0;
     float *ex = nullptr, *eh = nullptr, *eqkv = nullptr, *eattn = nullptr, *effn = nullptr, *ekv = nullptr;
     int *etok = nullptr, *epos = nullptr, *evalid = nullptr;
+    int* erow0 = nullptr;  // first encoder row of each sentence (rows packed, no padding)
     float *x = nullptr, *h = nullptr, *qkv = nullptr, *qx = nullptr, *attn = nullptr, *ffn = nullptr;
     float* logits = nullptr;
     int *tok = nullptr, *hist = nullptr, *ntok = nullptr, *parent = nullptr, *top_tok = nullptr;
@@ -592,12 +593,12 @@ int encode(nllb_model* m, Work& w, const std::vector<int>& n_src) {
         a.n_heads = H;
         a.seq_len = w.S;
         a.head_dim = 64;
-        a.stride_batch = (int64_t)w.S * D;
+        a.stride_batch = 0;  // rows packed: sentence s starts at row erow0[s]
         a.stride_head = 64;
         a.stride_row = D;
         a.valid_len = w.evalid;
         a.scale = 1.0f / sqrtf(64.0f);
-        ENG_RC(nllb_attn_prefill(m->attn, &a));
+        ENG_RC(nllb::attn_prefill_packed(m->attn, &a, w.erow0));
         ENG_RC(run_linear(m, E.out, w.eattn, R, w.ex, w.ex, 0, D));
         ENG_CK(launch_layernorm(lnout, w.ex, nullptr, E.ln2g, E.ln2b, R, P1, m->stream));
         ENG_RC(run_linear(m, E.fc1, w.eh, R, w.effn, nullptr, 1, FFN, -1, P1, P2));
@@ -611,7 +612,7 @@ int encode(nllb_model* m, Work& w, const std::vector<int>& n_src) {
         ENG_RC(run_linear(m, m->dec[l].xkv, w.eh, R, w.ekv, nullptr, 0, D, -1, P1));
         ENG_CK(launch_set_memory_batched(c->km + l * layer_floats, c->vm + l * layer_floats,
                                          c->n_src_dev + (size_t)l * c->d.max_sentences, c->d.max_src, H, w.ekv,
-                                         w.ekv + (size_t)R * D, (long long)w.S * D, w.evalid, w.n_sent, w.S,
+                                         w.ekv + (size_t)R * D, 0, w.erow0, w.evalid, w.n_sent, w.S,
                                          m->stream));
         for (int s = 0; s < w.n_sent; ++s) c->n_src_host[(size_t)l * c->d.max_sentences + s] = n_src[s];
     }
@@ -712,7 +713,10 @@ extern "C" int nllb_translate(nllb_model* m, int n_sent, const int* src_tokens, 
         max_out[s] = std::min(3 * n_src[s] + 10, o.max_gen - 4);  // main.c:315-316
     }
     w.S = S;
-    w.rows_enc = n_sent * S;
+    std::vector<int> row0(n_sent);  // encoder rows are packed: sentence s at rows row0[s] ..
+    int rows_enc = 0;
+    for (int s = 0; s < n_sent; ++s) row0[s] = rows_enc, rows_enc += n_src[s];
+    w.rows_enc = rows_enc;
     w.rows = n_sent * NB;
     const size_t RE = (size_t)w.rows_enc, R = (size_t)w.rows;
     ENG_RC(ensure_planes(m, std::max(RE, R) * FFN * 3));
@@ -725,6 +729,7 @@ extern "C" int nllb_translate(nllb_model* m, int n_sent, const int* src_tokens, 
     ENG_RC(w.alloc(&w.etok, RE));
     ENG_RC(w.alloc(&w.epos, RE));
     ENG_RC(w.alloc(&w.evalid, n_sent));
+    ENG_RC(w.alloc(&w.erow0, n_sent));
     ENG_RC(w.alloc(&w.x, R * D));
     ENG_RC(w.alloc(&w.h, R * D));
     ENG_RC(w.alloc(&w.qkv, R * 3 * D));
@@ -741,17 +746,19 @@ extern "C" int nllb_translate(nllb_model* m, int n_sent, const int* src_tokens, 
     ENG_RC(w.alloc(&w.top_lp, R * 8));
     ENG_RC(w.alloc(&w.active, R));
 
-    // ---- encoder (padded to the longest source; keys beyond n_src masked)
+    // ---- encoder: the sentences' rows back to back (no padding rows in the
+    // GEMMs); each sentence's attention over its own rows only
     {
-        std::vector<int> tok(RE, 1), pos(RE);
+        std::vector<int> tok(RE), pos(RE);
         for (int s = 0; s < n_sent; ++s)
-            for (int t = 0; t < S; ++t) {
-                if (t < n_src[s]) tok[(size_t)s * S + t] = src_tokens[src_offsets[s] + t];
-                pos[(size_t)s * S + t] = t + 2;  // NLLB position offset (encoder.c:29)
+            for (int t = 0; t < n_src[s]; ++t) {
+                tok[(size_t)row0[s] + t] = src_tokens[src_offsets[s] + t];
+                pos[(size_t)row0[s] + t] = t + 2;  // NLLB position offset (encoder.c:29)
             }
         ENG_CK(cudaMemcpyAsync(w.etok, tok.data(), RE * sizeof(int), cudaMemcpyHostToDevice, m->stream));
         ENG_CK(cudaMemcpyAsync(w.epos, pos.data(), RE * sizeof(int), cudaMemcpyHostToDevice, m->stream));
         ENG_CK(cudaMemcpyAsync(w.evalid, n_src.data(), n_sent * sizeof(int), cudaMemcpyHostToDevice, m->stream));
+        ENG_CK(cudaMemcpyAsync(w.erow0, row0.data(), n_sent * sizeof(int), cudaMemcpyHostToDevice, m->stream));
         ENG_RC(nllb_attn_reset(m->attn));
         ENG_RC(encode(m, w, n_src));
         ENG_CK(cudaStreamSynchronize(m->stream));

@@ -611,7 +611,7 @@ __global__ void __launch_bounds__(256) vocab_merge_kernel(const float* ws, int C
 // ---------------------------------------------------------------------------
 __global__ void set_memory_batched_kernel(float* km, float* vm, int* n_src_slots, int max_src, int H,
                                           const float* k, const float* v, long long sent_stride,
-                                          const int* n_src, int n_sent) {
+                                          const int* row_start, const int* n_src, int n_sent) {
     pdl_launch_dependents();
     pdl_wait_primary();  // inputs come from earlier kernels; outputs may still be read by them
     const int s = blockIdx.y;
@@ -622,7 +622,8 @@ __global__ void set_memory_batched_kernel(float* km, float* vm, int* n_src_slots
         const int q4 = (int)(i & 15);
         const size_t hr = i >> 4;
         const int r = (int)(hr % n), h = (int)(hr / n);
-        const size_t src = (size_t)s * sent_stride + (size_t)r * (H * 64) + (size_t)h * 64;
+        const size_t s0 = row_start ? (size_t)row_start[s] * (H * 64) : (size_t)s * sent_stride;
+        const size_t src = s0 + (size_t)r * (H * 64) + (size_t)h * 64;
         const size_t dst = (((size_t)s * H + h) * max_src + r) * 64;
         reinterpret_cast<float4*>(km + dst)[q4] = reinterpret_cast<const float4*>(k + src)[q4];
         reinterpret_cast<float4*>(vm + dst)[q4] = reinterpret_cast<const float4*>(v + src)[q4];
@@ -725,12 +726,12 @@ cudaError_t launch_logsoftmax_topk(const float* logits, size_t ld, int V, int ro
 }
 
 cudaError_t launch_set_memory_batched(float* km, float* vm, int* n_src_slots, int max_src, int H, const float* k,
-                                      const float* v, long long sent_stride, const int* n_src, int n_sent,
-                                      int max_n, cudaStream_t st) {
+                                      const float* v, long long sent_stride, const int* row_start,
+                                      const int* n_src, int n_sent, int max_n, cudaStream_t st) {
     if (n_sent <= 0) return cudaSuccess;
     const int bx = (int)(((size_t)H * max_n * 16 + 255) / 256);
     return launch_pdl(set_memory_batched_kernel, dim3(bx < 64 ? bx : 64, n_sent), dim3(256), 0, st, km, vm,
-                      n_src_slots, max_src, H, k, v, sent_stride, n_src, n_sent);
+                      n_src_slots, max_src, H, k, v, sent_stride, row_start, n_src, n_sent);
 }
 
 cudaError_t launch_reciprocal(float* out, const float* in, size_t n, cudaStream_t st) {

@@ -76,9 +76,10 @@ cudaError_t launch_penalties(float* logits, size_t ld, const int* hist, int hist
 size_t vocab_topk_ws_floats(int V, int rows, int k);
 cudaError_t launch_logsoftmax_topk(const float* logits, size_t ld, int V, int rows, const unsigned char* active,
                                    int k, int* out_tok, float* out_logp, float* ws, cudaStream_t st);
+// row_start (optional): sentence s's rows start at row_start[s] (packed), else at s * sent_stride
 cudaError_t launch_set_memory_batched(float* km, float* vm, int* n_src_slots, int max_src, int H, const float* k,
-                                      const float* v, long long sent_stride, const int* n_src, int n_sent,
-                                      int max_n, cudaStream_t st);
+                                      const float* v, long long sent_stride, const int* row_start,
+                                      const int* n_src, int n_sent, int max_n, cudaStream_t st);
 cudaError_t launch_reciprocal(float* out, const float* in, size_t n, cudaStream_t st);
 
 // Beam-search state of a translate call on the device (4 beams per sentence,

@@ -95,6 +95,10 @@ struct PrefillParams {
     long long msb, msh;
     float scale_log2;
     int* err;
+    // packed rows (optional): sequence b's row r is at row_start[b] + r (its
+    // base is row_start[b] * sr + h * sh, sb unused); only its valid_len[b]
+    // rows are read and written, so sequences may lie back to back
+    const int* row_start;
 };
 
 // Per-device kernel attributes (dynamic shared memory); call once per device.

@@ -326,8 +326,30 @@ static PrefillParams prefill_params(const nllb_attn_prefill_args* a, int* err) {
     p.msb = a->mask_stride_batch;
     p.msh = a->mask_stride_head;
     p.scale_log2 = a->scale * kLog2e;
+    p.row_start = nullptr;
     return p;
 }
+
+}  // extern "C"
+
+namespace nllb {
+
+int attn_prefill_packed(nllb_attn_ctx* c, const nllb_attn_prefill_args* a, const int* row_start) {
+    if (!c) return fail(NLLB_ATTN_EINVAL, "ctx is NULL");
+    int rc = check_prefill(a);
+    if (rc) return rc;
+    if (!row_start || !a->valid_len || a->mask)
+        return fail(NLLB_ATTN_EINVAL, "packed prefill needs row starts and lengths, and no mask");
+    if ((rc = set_device(c))) return rc;
+    PrefillParams p = prefill_params(a, c->err);
+    p.row_start = row_start;
+    NLLB_CK(launch_prefill(p, c->stream));
+    return NLLB_ATTN_OK;
+}
+
+}  // namespace nllb
+
+extern "C" {
 
 int nllb_attn_prefill(nllb_attn_ctx* c, const nllb_attn_prefill_args* a) {
     if (!c) return fail(NLLB_ATTN_EINVAL, "ctx is NULL");

@@ -47,7 +47,8 @@ __global__ void __launch_bounds__(kThreads) prefill_ffma_kernel(const PrefillPar
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
     const int S = p.S;
     const int q0 = qt * BQ;
-    const long long base = (long long)b * p.sb + (long long)h * p.sh;
+    const long long base = (p.row_start ? (long long)__ldg(p.row_start + b) * p.sr : (long long)b * p.sb) +
+                           (long long)h * p.sh;
     // valid_len[b] <= 0 leaves no unmasked key; the reference's additive -1e9
     // mask then makes every score equal, i.e. the plain mean of V: do that.
     int kv_len = S;
@@ -57,6 +58,8 @@ __global__ void __launch_bounds__(kThreads) prefill_ffma_kernel(const PrefillPar
         if (vl <= 0) uniform = true;
         else kv_len = min(vl, S);
     }
+    // query rows read and written: packed rows end at the sequence's length
+    const int q_lim = p.row_start ? (uniform ? 0 : kv_len) : S;
     const float* mrow0 =
         p.mask ? p.mask + (long long)b * p.msb + (long long)h * p.msh : nullptr;
 
@@ -64,7 +67,7 @@ __global__ void __launch_bounds__(kThreads) prefill_ffma_kernel(const PrefillPar
     for (int i = tid; i < BQ * 16; i += kThreads) {
         const int r = i >> 4, c4 = i & 15;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (q0 + r < S) v = __ldg(reinterpret_cast<const float4*>(p.q + base + (long long)(q0 + r) * p.sr) + c4);
+        if (q0 + r < q_lim) v = __ldg(reinterpret_cast<const float4*>(p.q + base + (long long)(q0 + r) * p.sr) + c4);
         reinterpret_cast<float4*>(Qs + r * LDS)[c4] = v;
     }
 
@@ -177,7 +180,7 @@ __global__ void __launch_bounds__(kThreads) prefill_ffma_kernel(const PrefillPar
         l += __shfl_xor_sync(0xffffffffu, l, 2);
         l += __shfl_xor_sync(0xffffffffu, l, 1);
         const int qr = q0 + ty + 8 * i;
-        if (qr < S) {
+        if (qr < q_lim) {
             float* dst = p.out + base + (long long)qr * p.sr;
             reinterpret_cast<float4*>(dst)[tx] = f4_scale(o[i], 1.0f / l);
         }
@@ -265,7 +268,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
     const int quarter = warp & 3, half = warp >> 2;  // TMEM lane quarter, column half
     const int S = p.S;
     const int q0 = qt * TC_Q;
-    const long long hbase = (long long)b * p.sb + (long long)h * p.sh;
 
     if (warp == 0) tmem_alloc(tmem_slot, TC_TMEM_COLS);
     if (tid == 0) {
@@ -281,8 +283,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
     const uint32_t tS = tmem + lane_off;             // scores: columns [0, 256)
     const uint32_t tO = tmem + lane_off + TC_MAX_S;  // output: columns [256, 320)
 
-    pdl_wait_primary();  // q, k, v, lengths and mask come from earlier kernels
+    pdl_wait_primary();  // q, k, v, lengths, row starts and mask come from earlier kernels
 
+    const long long hbase = (p.row_start ? (long long)__ldg(p.row_start + b) * p.sr : (long long)b * p.sb) +
+                            (long long)h * p.sh;
     int kv_len = S;
     bool uniform = false;  // valid_len 0: equal weights over all keys (see prefill_ffma_kernel)
     if (p.valid_len) {
@@ -290,6 +294,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
         if (vl <= 0) uniform = true;
         else kv_len = min(vl, S);
     }
+    // query rows read and written: packed rows end at the sequence's length
+    const int q_lim = p.row_start ? (uniform ? 0 : kv_len) : S;
     const int n_kg = (kv_len + TC_KG - 1) / TC_KG;  // score groups of 128 keys
     const int n_kc = (kv_len + TC_K - 1) / TC_K;    // P.V chunks of 64 keys
     const int rloc = quarter * 32 + lane;           // query row within the tile = TMEM lane
@@ -344,7 +350,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
 #pragma unroll
     for (int it = 0; it < 8; ++it) {
         const int r = (it * TC_THREADS + tid) >> 4;
-        qr[it] = ldg_row4(p.q, hbase + (long long)(q0 + r) * p.sr, tid & 15, q0 + r < S);
+        qr[it] = ldg_row4(p.q, hbase + (long long)(q0 + r) * p.sr, tid & 15, q0 + r < q_lim);
     }
     load_k_group(0, kr);
 #pragma unroll
@@ -446,7 +452,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
         sum += s_red[tid ^ 128];
         float o[32];
         tmem_ld32(tO + (uint32_t)(half * 32), o);
-        if (row < S) {
+        if (row < q_lim) {
             const float inv = 1.0f / sum;
             float4* dst = reinterpret_cast<float4*>(p.out + hbase + (long long)row * p.sr) + half * 8;
 #pragma unroll
