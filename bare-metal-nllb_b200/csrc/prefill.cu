@@ -60,6 +60,7 @@ __global__ void __launch_bounds__(kThreads) prefill_ffma_kernel(const PrefillPar
     }
     // query rows read and written: packed rows end at the sequence's length
     const int q_lim = p.row_start ? (uniform ? 0 : kv_len) : S;
+    if (q0 >= q_lim) return;  // packed rows: this query tile lies past the sequence (uniform per CTA)
     const float* mrow0 =
         p.mask ? p.mask + (long long)b * p.msb + (long long)h * p.msh : nullptr;
 
@@ -296,6 +297,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
     }
     // query rows read and written: packed rows end at the sequence's length
     const int q_lim = p.row_start ? (uniform ? 0 : kv_len) : S;
+    if (q0 >= q_lim) {  // packed rows: this query tile lies past the sequence (uniform per CTA)
+        tc_fence_before();
+        __syncthreads();
+        if (warp == 0) {
+            tc_fence_after();
+            tmem_dealloc(tmem, TC_TMEM_COLS);
+        }
+        return;
+    }
     const int n_kg = (kv_len + TC_KG - 1) / TC_KG;  // score groups of 128 keys
     const int n_kc = (kv_len + TC_K - 1) / TC_K;    // P.V chunks of 64 keys
     const int rloc = quarter * 32 + lane;           // query row within the tile = TMEM lane
