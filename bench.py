@@ -69,8 +69,12 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.lines = []
+        self.i0, self.i1 = 0, None
 
-    def __enter__(self):
+    def start(self, ready_timeout: float = 5.0):
+        """Start sampling and wait (bounded) for the first sample: nvidia-smi
+        needs a few hundred ms before it reports, longer than a short timed
+        region; call this before the region's barrier."""
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
@@ -78,26 +82,36 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            t_end = time.time() + ready_timeout
+            while not self.lines and time.time() < t_end and self.proc.poll() is None:
+                time.sleep(0.01)
         except (FileNotFoundError, OSError):
             self.proc = None
         return self
 
-    def _read(self):
-        for ln in self.proc.stdout:
-            self.lines.append(ln.strip())
+    def mark(self):
+        """The timed region starts: later samples are the region's."""
+        self.i0 = len(self.lines)
 
-    def __exit__(self, *exc):
+    def stop(self):
+        """The timed region has ended: keep one more sample, then stop."""
         if self.proc:
+            time.sleep(0.06)
+            self.i1 = len(self.lines)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
 
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for ln in self.lines:
+        for ln in self.lines[self.i0:self.i1]:
             parts = [x.strip() for x in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -215,15 +229,17 @@ def run_ours(args, rank, world, local_rank):
     vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
     smi_index = vis.split(",")[local_rank] if vis else str(local_rank)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clk = ClockSampler(smi_index).start()
     barrier()
     torch.cuda.synchronize(dev)
-    with ClockSampler(smi_index) as clk:
-        with torch.cuda.stream(stream):
-            e0.record(stream)
-            for _ in range(args.steps):
-                sweep()
-            e1.record(stream)
-        torch.cuda.synchronize(dev)
+    clk.mark()
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps):
+            sweep()
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    clk.stop()
     barrier()
     ctx.sync()
     elapsed = e0.elapsed_time(e1) / 1e3
