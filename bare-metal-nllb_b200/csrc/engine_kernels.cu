@@ -329,7 +329,7 @@ __global__ void penalties_kernel(float* logits, size_t ld, const int* hist, int 
     if (r >= rows || (active && !active[r])) return;  // uniform per warp
     float* lg = logits + (size_t)r * ld;
     const int* tk = hist + (size_t)r * hist_ld;
-    const int n = n_tokens[r];
+    const int n = min(n_tokens[r], hist_ld);  // a history longer than its row is cut to the row
     const float inv_penalty = 1.0f / penalty;
     for (int g0 = 2; g0 < n; g0 += 128) {
         int t[4], cnt[4];    // t = -1: no position, or token 2 (never penalised, never matches)
@@ -338,7 +338,7 @@ __global__ void penalties_kernel(float* logits, size_t ld, const int* hist, int 
         for (int q = 0; q < 4; ++q) {
             const int g = g0 + 32 * q + lane;
             t[q] = g < n ? __ldg(tk + g) : -1;
-            if (t[q] == 2) t[q] = -1;
+            if (t[q] == 2 || (size_t)t[q] >= ld) t[q] = -1;  // token 2, or an id outside the row: skipped
             cnt[q] = t[q] >= 0 ? 1 : 0;
         }
 #pragma unroll 4
@@ -355,10 +355,10 @@ __global__ void penalties_kernel(float* logits, size_t ld, const int* hist, int 
         float v[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q)
-            if (cnt[q] > 0 && !((seen >> q) & 1u)) v[q] = lg[t[q]];
+            if (t[q] >= 0 && cnt[q] > 0 && !((seen >> q) & 1u)) v[q] = lg[t[q]];
 #pragma unroll
         for (int q = 0; q < 4; ++q)
-            if (cnt[q] > 0 && !((seen >> q) & 1u)) {
+            if (t[q] >= 0 && cnt[q] > 0 && !((seen >> q) & 1u)) {
                 float x = v[q];
                 for (int c = 0; c < cnt[q]; ++c) x = (x > 0.f) ? x * inv_penalty : x * penalty;
                 lg[t[q]] = x;
@@ -367,8 +367,10 @@ __global__ void penalties_kernel(float* logits, size_t ld, const int* hist, int 
     __syncwarp();
     if (ngram == 2 && n >= 2) {
         const int cur = tk[n - 1];
-        for (int i = lane; i <= n - 2; i += 32)
-            if (tk[i] == cur && tk[i + 1] != 2) lg[tk[i + 1]] = -1e30f;
+        for (int i = lane; i <= n - 2; i += 32) {
+            const int nx = tk[i + 1];
+            if (tk[i] == cur && nx != 2 && (size_t)nx < ld) lg[nx] = -1e30f;
+        }
     }
 }
 

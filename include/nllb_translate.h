@@ -133,7 +133,9 @@ NLLB_ATTN_API void nllb_linear_free(nllb_linear* layer);
  * `penalty` or multiplies a non-positive one, once per occurrence -- then,
  * with no_repeat_ngram 2, apply_no_repeat_ngram (main.c:196-213): every token
  * that followed an earlier occurrence of the last token gets -1e30 (token 2
- * excepted).  no_repeat_ngram: 0 (off) or 2.
+ * excepted).  no_repeat_ngram: 0 (off) or 2.  Token ids outside [0, ld) in a
+ * history are skipped (the reference would index past the row), and a length
+ * above tokens_ld is cut to tokens_ld.
  * nllb_logsoftmax_topk: for each row, the k best entries of the row's
  * log-softmax -- log_softmax_inplace + find_topk (main.c:154-182) -- as
  * out_tok[r*k + j] / out_logp[r*k + j], best first, the lower index first

@@ -144,3 +144,28 @@ def test_search_argument_errors(cuda_device):
     with pytest.raises(na.NllbAttnError) as ei:
         na.apply_penalties(x, tk, nt, 0.0, 2)
     assert ei.value.status == na.EINVAL
+
+
+def test_penalties_skip_ids_outside_the_row(cuda_device):
+    """A history may hold ids that are no token of the row (negative, or past
+    its end) and a length longer than its row: nothing is read or written
+    outside the logits, and every other logit is what the reference gives
+    for the same history with those ids replaced by an otherwise unused token
+    (whose own column is left out of the comparison)."""
+    rows, V, T = 3, 777, 40
+    logits = po.det_uniform(801, (rows, V), 3.0)
+    tokens = po.det_ints(802, rows * T, 0, 20).reshape(rows, T)
+    tokens[:, 0] = 2
+    bad = [(0, 5, -5), (0, 9, V + 3), (1, 3, 2 ** 30), (1, 30, -1), (2, 17, V)]
+    for r, g, t in bad:
+        tokens[r, g] = t
+    lens = np.array([40, 200, 25], np.int32)  # row 1 claims more tokens than its row holds
+    out = run_penalties(logits, tokens, lens, 1.2, 2)
+    sentinel = V - 1
+    assert not (tokens == sentinel).any()
+    clean = tokens.copy()
+    for r, g, _ in bad:
+        clean[r, g] = sentinel
+    ref = po.penalties(logits, clean, np.minimum(lens, T), 1.2, 2)
+    np.testing.assert_array_equal(out[:, :sentinel], ref[:, :sentinel])
+    np.testing.assert_array_equal(out[:, sentinel], logits[:, sentinel])
