@@ -712,6 +712,18 @@ extern "C" int nllb_translate(nllb_model* m, int n_sent, const int* src_tokens, 
         S = std::max(S, n_src[s]);
         max_out[s] = std::min(3 * n_src[s] + 10, o.max_gen - 4);  // main.c:315-316
     }
+    // Internal order: sentences by decreasing max_out (stable), so that the
+    // sentences still running at any step are a prefix of the batch and a
+    // step processes only that prefix (perm: internal index -> caller's).
+    std::vector<int> perm(n_sent);
+    for (int s = 0; s < n_sent; ++s) perm[s] = s;
+    std::stable_sort(perm.begin(), perm.end(), [&](int a, int b) { return max_out[a] > max_out[b]; });
+    {
+        std::vector<int> ns(n_sent), mo(n_sent);
+        for (int s = 0; s < n_sent; ++s) ns[s] = n_src[perm[s]], mo[s] = max_out[perm[s]];
+        n_src.swap(ns);
+        max_out.swap(mo);
+    }
     w.S = S;
     std::vector<int> row0(n_sent);  // encoder rows are packed: sentence s at rows row0[s] ..
     int rows_enc = 0;
@@ -752,7 +764,7 @@ extern "C" int nllb_translate(nllb_model* m, int n_sent, const int* src_tokens, 
         std::vector<int> tok(RE), pos(RE);
         for (int s = 0; s < n_sent; ++s)
             for (int t = 0; t < n_src[s]; ++t) {
-                tok[(size_t)row0[s] + t] = src_tokens[src_offsets[s] + t];
+                tok[(size_t)row0[s] + t] = src_tokens[src_offsets[perm[s]] + t];
                 pos[(size_t)row0[s] + t] = t + 2;  // NLLB position offset (encoder.c:29)
             }
         ENG_CK(cudaMemcpyAsync(w.etok, tok.data(), RE * sizeof(int), cudaMemcpyHostToDevice, m->stream));
@@ -885,31 +897,44 @@ extern "C" int nllb_translate(nllb_model* m, int n_sent, const int* src_tokens, 
     for (int s = 0; s < n_sent; ++s) last_step = std::max(last_step, max_out[s] + 1);
     if (last_step >= m->max_gen) return nllb::set_error(NLLB_ATTN_ECAPACITY, "decode would run past max_gen");
     int cur = 0, launched_to = 1;
+    int n_live = n_sent;  // sentences processed at this step: a sentence runs at step t while t < max_out + 2
     for (int step = 2; step <= last_step; ++step) {
         if (step >= 4) {  // two steps of lookahead: the count of step - 2 decides whether to go on
             ENG_CK(cudaEventSynchronize(m->step_ev[(step - 2) & 3]));
             if (m->live_h[step - 2] == 0) break;
         }
+        while (n_live > 0 && step >= max_out[n_live - 1] + 2) --n_live;
+        if (n_live == 0) break;
+        w.n_sent = n_live;
+        w.rows = n_live * NB;
+        B.n_sent = n_live;
         ENG_RC(decode_step(m, w, step));
         ENG_RC(vocab_topk(m, w, 8, true, o, cur ? B.bt1 : B.bt0));
         ENG_CK(launch_beam_select(B, cur, w.top_tok, w.top_lp, step, m->stream));
         ENG_CK(cudaMemcpyAsync(m->live_h + step, B.live + step, sizeof(int), cudaMemcpyDeviceToHost, m->stream));
         ENG_CK(cudaEventRecord(m->step_ev[step & 3], m->stream));
-        ENG_RC(nllb_attn_reorder(m->attn, n_sent, w.parent));
+        ENG_RC(nllb_attn_reorder(m->attn, n_live, w.parent));
         cur ^= 1;
         launched_to = step;
     }
+    w.n_sent = n_sent;
+    w.rows = (int)R;
+    B.n_sent = n_sent;
     ENG_RC(nllb_attn_sync(m->attn));
     for (int t = 3; t <= launched_to; ++t) steps_run += m->live_h[t - 1] > 0;
 
     // ---- device beam state back to the host structures of the final choice
     {
-        std::vector<int> bt(R * (size_t)GD), bn(R), cn((size_t)n_sent * 8), ccnt(n_sent), mcnt(n_sent);
+        std::vector<int> bt(R * (size_t)GD), bt_other(R * (size_t)GD), bn(R), cn((size_t)n_sent * 8), ccnt(n_sent),
+            mcnt(n_sent);
         std::vector<int> ct((size_t)n_sent * 8 * GD);
         std::vector<float> bsc(R), beos(R), csc((size_t)n_sent * 8), ceos((size_t)n_sent * 8);
         std::vector<float> marg((size_t)n_sent * GD);
         std::vector<unsigned char> bfin(R);
-        ENG_CK(cudaMemcpy(bt.data(), cur ? B.bt1 : B.bt0, bt.size() * sizeof(int), cudaMemcpyDeviceToHost));
+        // the history written by a sentence's last processed step: the selection
+        // of step t writes bt1 for even t and bt0 for odd t (bt0 before step 2)
+        ENG_CK(cudaMemcpy(bt.data(), B.bt0, bt.size() * sizeof(int), cudaMemcpyDeviceToHost));
+        ENG_CK(cudaMemcpy(bt_other.data(), B.bt1, bt_other.size() * sizeof(int), cudaMemcpyDeviceToHost));
         ENG_CK(cudaMemcpy(bn.data(), B.bn, R * sizeof(int), cudaMemcpyDeviceToHost));
         ENG_CK(cudaMemcpy(bsc.data(), B.bsc, R * sizeof(float), cudaMemcpyDeviceToHost));
         ENG_CK(cudaMemcpy(beos.data(), B.beos, R * sizeof(float), cudaMemcpyDeviceToHost));
@@ -922,11 +947,13 @@ extern "C" int nllb_translate(nllb_model* m, int n_sent, const int* src_tokens, 
         ENG_CK(cudaMemcpy(marg.data(), B.margins, marg.size() * sizeof(float), cudaMemcpyDeviceToHost));
         ENG_CK(cudaMemcpy(mcnt.data(), B.mcnt, n_sent * sizeof(int), cudaMemcpyDeviceToHost));
         for (int s = 0; s < n_sent; ++s) {
+            const int last = std::min(max_out[s] + 1, launched_to);  // last step that selected for s
+            const std::vector<int>& hs = (last >= 2 && (last & 1) == 0) ? bt_other : bt;
             for (int b = 0; b < NB; ++b) {
                 const size_t r = (size_t)s * NB + b;
                 Beam& bm = beams[r];
                 bm.n = bn[r];
-                std::copy(bt.begin() + r * GD, bt.begin() + r * GD + bm.n, bm.tokens.begin());
+                std::copy(hs.begin() + r * GD, hs.begin() + r * GD + bm.n, bm.tokens.begin());
                 bm.score = bsc[r];
                 bm.eos_score = beos[r];
                 bm.finished = bfin[r] != 0;
@@ -941,7 +968,7 @@ extern "C" int nllb_translate(nllb_model* m, int n_sent, const int* src_tokens, 
                 hb.finished = true;
                 completed[s].push_back(hb);
             }
-            m->margins[s].assign(marg.begin() + (size_t)s * GD, marg.begin() + (size_t)s * GD + mcnt[s]);
+            m->margins[perm[s]].assign(marg.begin() + (size_t)s * GD, marg.begin() + (size_t)s * GD + mcnt[s]);
         }
     }
     const double t_dec = ms_since(t_dec0);
@@ -966,16 +993,17 @@ extern "C" int nllb_translate(nllb_model* m, int n_sent, const int* src_tokens, 
             }
         }
         const Beam& best = cp[bi];
+        const size_t so = (size_t)perm[s];  // the caller's index
         int n_out = 0;
         for (int i = 2; i < best.n; ++i) {
             if (best.tokens[i] == 2) break;
-            if (out_tokens) out_tokens[(size_t)s * G + n_out] = best.tokens[i];
+            if (out_tokens) out_tokens[so * G + n_out] = best.tokens[i];
             ++n_out;
         }
         if (out_tokens)
-            for (int i = n_out; i < G; ++i) out_tokens[(size_t)s * G + i] = -1;
-        if (out_len) out_len[s] = n_out;
-        if (out_score) out_score[s] = bn;
+            for (int i = n_out; i < G; ++i) out_tokens[so * G + i] = -1;
+        if (out_len) out_len[so] = n_out;
+        if (out_score) out_score[so] = bn;
         total_out += n_out;
     }
     if (stats) {
