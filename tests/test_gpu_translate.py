@@ -68,6 +68,19 @@ def test_batching_is_transparent(model):
     check_tokens(both[1], alone[0], m_alone, "batched vs alone")
 
 
+def test_running_prefix_down_to_one_sentence(model):
+    """A long and a short source: the short one stops after 64 tokens, the long
+    one runs on alone (4 beam rows, the weight-streaming linear path) -- each
+    must decode as it does alone."""
+    long_src = GOLDEN["cases"]["cfg4_len100"]["src"]
+    short_src = GOLDEN["cases"]["cfg4_len16"]["src"]
+    both, _, _ = model.translate([short_src, long_src], GOLDEN["tgt_lang_id"], max_gen=132)
+    m_short, m_long = model.margins(0), model.margins(1)
+    for i, src in enumerate((short_src, long_src)):
+        alone, _, _ = model.translate([src], GOLDEN["tgt_lang_id"], max_gen=132)
+        check_tokens(both[i], alone[0], m_short if i == 0 else m_long, f"pair vs alone, sentence {i}")
+
+
 def test_translate_argument_errors(model):
     with pytest.raises(na.NllbAttnError) as ei:
         model.translate([[256047] * 300], GOLDEN["tgt_lang_id"])
