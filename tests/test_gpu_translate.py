@@ -5,7 +5,7 @@ tests/golden/e2e_tokens.json holds the token ids the reference engine
 emits on the synthetic NLLB-600M-shaped model for seeded sources.  The GPU
 engine must emit identical ids, except after a step whose beam decision came
 within 2e-4 of a tie (the reference's own sums differ from ours in the last
-bits, so a near-tie may resolve either way; the north star exempts top-2
+bits, so a near-tie may resolve either way; the parity criterion exempts top-2
 margins below 1e-4, and 2e-4 covers the rounding of our recorded margin).
 """
 import json
