@@ -37,7 +37,7 @@ __global__ void embed_pos_kernel(float* x, const int* tokens, const int* positio
 }
 
 // ---------------------------------------------------------------------------
-// LayerNorm over 1024 (tensor.c:198-223), optionally adding a residual first:
+// LayerNorm over 1024 (layernorm, tensor.c:200-223), optionally adding a residual first:
 // x = x + res (residual_add, tensor.c:249-251), out = LN(x).  One CTA per row.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float block_sum_256(float v, float* sh) {
