@@ -187,12 +187,39 @@ def cpu_reference_rate(target_s: float, T: int):
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
+def bind_to_gpu_cpus(smi_index: str):
+    """Keep this rank on the CPUs NVML names as closest to its GPU, so that
+    its pinned host buffers and copy launches stay on that socket; returns
+    the number of CPUs kept, or None where NVML gives nothing usable."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            h = pynvml.nvmlDeviceGetHandleByIndex(int(smi_index))
+            masks = pynvml.nvmlDeviceGetCpuAffinity(h, ((os.cpu_count() or 64) + 63) // 64)
+        finally:
+            pynvml.nvmlShutdown()
+        cpus = {w * 64 + b for w, m in enumerate(masks) for b in range(64) if (int(m) >> b) & 1}
+        cpus &= os.sched_getaffinity(0)
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+            return len(cpus)
+    except Exception:
+        pass
+    return None
+
+
 def run_ours(args, rank, world, local_rank):
     import numpy as np
     import torch
     import torch.distributed as dist
     import nllb_attn as na
 
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    smi_index = vis.split(",")[local_rank] if vis else str(local_rank)
+    # several ranks share the host: each on its GPU's socket (one rank keeps all
+    # CPUs, which the CPU baseline of rank 0 at one GPU uses)
+    host_cpus = bind_to_gpu_cpus(smi_index) if world > 1 else None
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     S, T = args.sentences, args.max_len
@@ -226,8 +253,6 @@ def run_ours(args, rank, world, local_rank):
         if world > 1:
             dist.barrier()
 
-    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
-    smi_index = vis.split(",")[local_rank] if vis else str(local_rank)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clk = ClockSampler(smi_index).start()
     barrier()
@@ -305,6 +330,8 @@ def run_ours(args, rank, world, local_rank):
         "how": "nllb_attn_reorder_host + nllb_attn_decode_self_host per decode step from pinned host "
                "memory; wall clock, max over ranks",
     }
+    if host_cpus:
+        e2e["host_cpus_per_rank"] = host_cpus  # the rank's CPUs: those NVML names for its GPU
 
     result = {
         "value": value, "ms_per_step": ms_per_step, "kernel_gbs": kernel_gbs,
