@@ -187,6 +187,9 @@ def cpu_reference_rate(target_s: float, T: int):
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
+_HOST_CPUS_ALL = None  # the process's CPUs before bind_to_gpu_cpus
+
+
 def bind_to_gpu_cpus(smi_index: str):
     """Keep this rank on the CPUs NVML names as closest to its GPU, so that
     its pinned host buffers and copy launches stay on that socket; returns
@@ -200,8 +203,11 @@ def bind_to_gpu_cpus(smi_index: str):
         finally:
             pynvml.nvmlShutdown()
         cpus = {w * 64 + b for w, m in enumerate(masks) for b in range(64) if (int(m) >> b) & 1}
-        cpus &= os.sched_getaffinity(0)
+        global _HOST_CPUS_ALL
+        before = os.sched_getaffinity(0)
+        cpus &= before
         if cpus:
+            _HOST_CPUS_ALL = before
             os.sched_setaffinity(0, cpus)
             return len(cpus)
     except Exception:
@@ -217,9 +223,8 @@ def run_ours(args, rank, world, local_rank):
 
     vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
     smi_index = vis.split(",")[local_rank] if vis else str(local_rank)
-    # several ranks share the host: each on its GPU's socket (one rank keeps all
-    # CPUs, which the CPU baseline of rank 0 at one GPU uses)
-    host_cpus = bind_to_gpu_cpus(smi_index) if world > 1 else None
+    # each rank on its GPU's socket (the CPU baseline, later, gets all CPUs back)
+    host_cpus = bind_to_gpu_cpus(smi_index)
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     S, T = args.sentences, args.max_len
@@ -744,6 +749,8 @@ def main():
     cpu = None
     if rank == 0 and world == 1:
         try:
+            if _HOST_CPUS_ALL:
+                os.sched_setaffinity(0, _HOST_CPUS_ALL)  # the CPU baseline uses every host CPU
             gbs, cores, sample, kind, _ = cpu_reference_rate(args.cpu_sample_s, T)
             cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": kind, "sample": sample}
         except Exception as e:  # reported, not fatal
