@@ -190,15 +190,19 @@ def cpu_reference_rate(target_s: float, T: int):
 _HOST_CPUS_ALL = None  # the process's CPUs before bind_to_gpu_cpus
 
 
-def bind_to_gpu_cpus(smi_index: str):
-    """Keep this rank on the CPUs NVML names as closest to its GPU, so that
-    its pinned host buffers and copy launches stay on that socket; returns
-    the number of CPUs kept, or None where NVML gives nothing usable."""
+def bind_to_gpu_cpus(smi_index: str, pci_id: str = ""):
+    """Keep this rank on the CPUs NVML names as closest to its GPU (found by
+    PCI bus id, else by index), so that its pinned host buffers and copy
+    launches stay on that socket; returns the number of CPUs kept, or None
+    where NVML gives nothing usable."""
     try:
         import pynvml
         pynvml.nvmlInit()
         try:
-            h = pynvml.nvmlDeviceGetHandleByIndex(int(smi_index))
+            try:
+                h = pynvml.nvmlDeviceGetHandleByPciBusId(pci_id.encode())
+            except Exception:
+                h = pynvml.nvmlDeviceGetHandleByIndex(int(smi_index))
             masks = pynvml.nvmlDeviceGetCpuAffinity(h, ((os.cpu_count() or 64) + 63) // 64)
         finally:
             pynvml.nvmlShutdown()
@@ -224,7 +228,9 @@ def run_ours(args, rank, world, local_rank):
     vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
     smi_index = vis.split(",")[local_rank] if vis else str(local_rank)
     # each rank on its GPU's socket (the CPU baseline, later, gets all CPUs back)
-    host_cpus = bind_to_gpu_cpus(smi_index)
+    props = torch.cuda.get_device_properties(local_rank)
+    pci_id = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+    host_cpus = bind_to_gpu_cpus(smi_index, pci_id)
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     S, T = args.sentences, args.max_len
