@@ -15,6 +15,7 @@
 #include <cstdio>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <tuple>
 #include <string>
 #include <vector>
@@ -1023,6 +1024,36 @@ extern "C" int nllb_translate_margins(const nllb_model* m, int sentence, float* 
     return n;
 }
 
+// Error word of nllb_linear_int8 on device `dev` (allocated on the first call
+// there): set by a bounded wait that gave up, read and cleared only by
+// nllb_linear_int8_status.
+static int linear_err_word(int dev, int** out) {
+    static std::mutex mu;
+    static int* words[64] = {nullptr};
+    std::lock_guard<std::mutex> lock(mu);
+    if (!words[dev]) {
+        ENG_CK(cudaMalloc(&words[dev], sizeof(int)));
+        ENG_CK(cudaMemset(words[dev], 0, sizeof(int)));
+    }
+    *out = words[dev];
+    return NLLB_ATTN_OK;
+}
+
+extern "C" int nllb_linear_int8_status(void) {
+    int dev = 0;
+    ENG_CK(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return nllb::set_error(NLLB_ATTN_ENODEV, "device ordinal beyond 63");
+    int* w = nullptr;
+    const int rc = linear_err_word(dev, &w);
+    if (rc) return rc;
+    int h = 0;
+    ENG_CK(cudaDeviceSynchronize());
+    ENG_CK(cudaMemcpy(&h, w, sizeof(int), cudaMemcpyDeviceToHost));
+    ENG_CK(cudaMemset(w, 0, sizeof(int)));
+    if (h) return nllb::set_error(NLLB_ATTN_ETIMEOUT, "a bounded device wait of the linear kernel gave up");
+    return NLLB_ATTN_OK;
+}
+
 extern "C" int nllb_linear_int8(const float* x, int M, int K, const int8_t* w, const float* weight_scale,
                                 const float* bias, int N, float* out, const float* residual, int flags,
                                 void* stream) {
@@ -1046,15 +1077,14 @@ extern "C" int nllb_linear_int8(const float* x, int M, int K, const int8_t* w, c
     a.static_weights = 0;
     a.out_planes = nullptr;
     // bounded-wait error word of the current device for callers without a context
-    static int* err_words[64] = {nullptr};
     int dev = 0;
     ENG_CK(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return nllb::set_error(NLLB_ATTN_ENODEV, "device ordinal beyond 63");
-    if (!err_words[dev]) {
-        ENG_CK(cudaMalloc(&err_words[dev], sizeof(int)));
-        ENG_CK(cudaMemset(err_words[dev], 0, sizeof(int)));
+    int* err_word = nullptr;
+    {
+        const int rc = linear_err_word(dev, &err_word);
+        if (rc) return rc;
     }
-    int* err_word = err_words[dev];
     // split-K workspace of the current device, grown on demand
     static LinearWorkspace wss[64];
     LinearWorkspace& W = wss[dev];

@@ -83,8 +83,10 @@ SIGNATURES = {
                                 _fp, _fp, _fp, ctypes.POINTER(TranslateStats)]),
     "nllb_translate_margins": (_c_int, [_c_void_p, _c_int, _fp, _c_int]),
     "nllb_linear_int8": (_c_int, [_fp, _c_int, _c_int, _fp, _fp, _fp, _c_int, _fp, _fp, _c_int, _c_void_p]),
+    "nllb_linear_int8_status": (_c_int, []),
     "nllb_linear_int8_noalloc": (_c_int, [_fp, _c_int, _c_int, _fp, _fp, _fp, _c_int, _fp, _fp, _c_int,
                                           _c_void_p]),
+    "nllb_linear_int8_noalloc_status": (_c_int, [_c_void_p]),
     "nllb_linear_prepare": (_c_int, [_fp, _fp, _fp, _c_int, _c_int, _c_void_p, ctypes.POINTER(_c_void_p)]),
     "nllb_linear_run": (_c_int, [_c_void_p, _fp, _c_int, _fp, _fp, _c_int, _c_void_p]),
     "nllb_linear_status": (_c_int, [_c_void_p]),
@@ -329,6 +331,18 @@ def linear_int8_noalloc(x, w, weight_scale, out, bias=None, residual=None, relu=
                                              ptr(residual), LINEAR_RELU if relu else 0, stream),
            "nllb_linear_int8_noalloc")
     return out
+
+
+def linear_int8_status() -> int:
+    """nllb_linear_int8_status: synchronises the device, reads and clears the
+    error word of nllb_linear_int8 (returns the status, does not raise)."""
+    return load().nllb_linear_int8_status()
+
+
+def linear_int8_noalloc_status(stream=None) -> int:
+    """nllb_linear_int8_noalloc_status: waits for `stream`, reads and clears
+    the no-alloc entry point's error word (returns the status, does not raise)."""
+    return load().nllb_linear_int8_noalloc_status(stream)
 
 
 def apply_penalties(logits, tokens, n_tokens, penalty=1.2, no_repeat_ngram=2, stream=None):

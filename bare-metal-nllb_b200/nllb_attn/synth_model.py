@@ -131,6 +131,16 @@ def write_model(path: str, seed: int = 0, chunk: int = 1 << 24) -> Dict[str, int
     return offsets
 
 
+def default_model_path(seed: int = 0) -> str:
+    """Where the seeded model is kept: $NLLB_SYNTH_MODEL when set, else
+    .synth/ at the root of this repository (kept out of version control)."""
+    env = os.environ.get("NLLB_SYNTH_MODEL")
+    if env:
+        return env
+    repo = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    return os.path.join(repo, ".synth", f"synth_nllb600m_seed{seed}.safetensors")
+
+
 def ensure_model(path: str, seed: int = 0) -> str:
     """Write the model unless a complete file is already there."""
     specs = tensor_specs()
@@ -164,3 +174,11 @@ def source_ids(seed: int, n_tokens: int, src_lang: str = "eng_Latn") -> List[int
         z = z ^ (z >> np.uint64(29))
     ids = (4 + (z % np.uint64(256000 - 4))).astype(np.int64).tolist()
     return [LANG[src_lang]] + [int(t) for t in ids] + [2]
+
+
+def config4_sources(n: int = 1024, seed: int = 4) -> List[List[int]]:
+    """The sentence-batched translation workload: n sources of U[16,128]
+    tokens (ids U[4,256000)), each [eng_Latn] ... [2]; sentence i is the same
+    whatever n is."""
+    lengths = source_lengths(seed, n, 16, 129)
+    return [source_ids(seed * 1000003 + i, lengths[i]) for i in range(n)]

@@ -488,15 +488,18 @@ def measure_ops(ctx_factory, dev, hbm_peak, tflops_note=""):
     return res
 
 
-SYNTH_MODEL = os.environ.get("NLLB_SYNTH_MODEL", "/tmp/nllb_synth/synth_nllb600m_seed0.safetensors")
+def _synth_model_path() -> str:
+    from nllb_attn import synth_model as sm
+    return sm.default_model_path(0)
+
+
+SYNTH_MODEL = _synth_model_path()
 
 
 def config4_sources(n: int = 1024, seed: int = 4):
-    """Sentence-batched translation workload: n sources of U[16,128] tokens
-    (ids U[4,256000)), each [eng_Latn] ... [2]."""
+    """Sentence-batched translation workload (nllb_attn.synth_model.config4_sources)."""
     from nllb_attn import synth_model as sm
-    lengths = sm.source_lengths(seed, n, 16, 129)
-    return [sm.source_ids(seed * 1000003 + i, lengths[i]) for i in range(n)]
+    return sm.config4_sources(n, seed)
 
 
 def reference_translate_rate(model_path: str):

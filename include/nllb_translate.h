@@ -77,11 +77,18 @@ NLLB_ATTN_API int nllb_translate_margins(const nllb_model* m, int sentence, floa
  * tensor.c:249-251).  Device pointers, row-major x [M][K], w [N][K],
  * out [M][N]; asynchronous on `stream` (a cudaStream_t, NULL = default).
  * More than 16 rows run on the tensor cores (int8 weights exact in bf16,
- * activations split into three bf16 parts, fp32 accumulation). */
+ * activations split into three bf16 parts, fp32 accumulation); there K must
+ * be a multiple of 32.  A bounded device wait that gives up leaves the
+ * outputs invalid and sets a per-device error word that stays set until
+ * nllb_linear_int8_status reads it. */
 #define NLLB_LINEAR_RELU 1
 NLLB_ATTN_API int nllb_linear_int8(const float* x, int M, int K, const int8_t* w, const float* weight_scale,
                                    const float* bias, int N, float* out, const float* residual, int flags,
                                    void* stream);
+/* Synchronises the current device, then reads and clears nllb_linear_int8's
+ * error word there: NLLB_ATTN_ETIMEOUT if a call since the last query had a
+ * bounded device wait give up (its outputs are invalid), else NLLB_ATTN_OK. */
+NLLB_ATTN_API int nllb_linear_int8_status(void);
 
 /* Same computation as nllb_linear_int8, for callers that cannot have a
  * library allocate device memory while they run -- a serving process that
@@ -94,13 +101,20 @@ NLLB_ATTN_API int nllb_linear_int8(const float* x, int M, int K, const int8_t* w
  * current); make it before any stream capture.  Calls share the array:
  * calls whose kernels overlap on the GPU race.  At most
  * NLLB_LINEAR_NOALLOC_MAX_ROWS rows, _MAX_OUT outputs, _MAX_IN inputs;
- * larger shapes return NLLB_ATTN_ECAPACITY. */
+ * larger shapes return NLLB_ATTN_ECAPACITY.  Beyond 16 rows K must be a
+ * multiple of 32, as for nllb_linear_int8.  The device address and the SM
+ * count are looked up once per device ordinal: a device reset after the
+ * first call is not supported.  A bounded device wait that gives up sets an
+ * error word in the same array, which no later call clears:
+ * nllb_linear_int8_noalloc_status waits for `stream`, reads and clears it
+ * (NLLB_ATTN_ETIMEOUT if set), and allocates nothing either. */
 #define NLLB_LINEAR_NOALLOC_MAX_ROWS 256
 #define NLLB_LINEAR_NOALLOC_MAX_OUT 4096
 #define NLLB_LINEAR_NOALLOC_MAX_IN 4096
 NLLB_ATTN_API int nllb_linear_int8_noalloc(const float* x, int M, int K, const int8_t* w,
                                            const float* weight_scale, const float* bias, int N, float* out,
                                            const float* residual, int flags, void* stream);
+NLLB_ATTN_API int nllb_linear_int8_noalloc_status(void* stream);
 
 /* ---- INT8 linear layer with weights prepared once --------------------------
  * A LinearInt8 (pico.h:26-32) made resident on the current GPU: the layer

@@ -77,6 +77,7 @@ def ref_lib() -> ctypes.CDLL:
         lib.ref_prefill_flash.argtypes = [_fp] * 5 + [ctypes.c_int] * 3
         lib.attention_head_flash.argtypes = [_fp] * 5 + [ctypes.c_int] * 2
         lib.attention_head.argtypes = [_fp] * 6 + [ctypes.c_int] * 2
+        lib.ref_mat_vec_int8_rows.argtypes = [_fp, _fp, _fp, ctypes.c_int, ctypes.c_int, _fp, ctypes.c_int, _fp]
         lib.ref_time_decode_sweep.restype = ctypes.c_double
         lib.ref_time_decode_sweep.argtypes = [ctypes.c_int] * 4 + [ctypes.c_ulonglong]
         lib.ref_time_cross.restype = ctypes.c_double
@@ -210,6 +211,20 @@ def ref_prefill_flash(q, k, v, valid_len=None) -> np.ndarray:
     out = np.zeros_like(q)
     vl = None if valid_len is None else np.ascontiguousarray(valid_len, dtype=np.int32)
     ref_lib().ref_prefill_flash(_p(q), _p(k), _p(v), _p(vl), _p(out), B, H, S)
+    return out
+
+
+def ref_linear(x, w, scale, bias=None) -> np.ndarray:
+    """The reference's mat_vec_int8 (tensor.c:144-196) on each row of x [M][K]
+    with w [N][K] int8, scale [N], bias [N] or None: [M][N] fp32."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    w = np.ascontiguousarray(w, dtype=np.int8)
+    scale = np.ascontiguousarray(scale, dtype=np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    M, K = x.shape
+    N = w.shape[0]
+    out = np.zeros((M, N), np.float32)
+    ref_lib().ref_mat_vec_int8_rows(_p(w), _p(scale), _p(b), N, K, _p(x), M, _p(out))
     return out
 
 

@@ -125,6 +125,16 @@ void ref_prefill_flash(const float* Q, const float* K, const float* V,
     free(mask);
 }
 
+/* The reference's INT8 linear layer, mat_vec_int8 (tensor.c:144-196), on M
+ * input rows one after the other: out[m] = dequant(w) x[m] + bias, with the
+ * CTranslate2 convention w / scale (tensor.c:75).  w [N][K] int8, scale [N],
+ * bias [N] or NULL, x [M][K], out [M][N]. */
+void ref_mat_vec_int8_rows(const int8_t* w, const float* scale, const float* bias, int N, int K,
+                           const float* x, int M, float* out) {
+    LinearInt8 l = {w, scale, bias, N, K};
+    for (int m = 0; m < M; m++) mat_vec_int8(&l, x + (size_t)m * K, out + (size_t)m * N);
+}
+
 /* ---- timing of the reference attention on all host threads -------------- */
 
 static double now_s(void) {

@@ -14,6 +14,8 @@ Routines pinned (reference file:line):
   pen_*            apply_repetition_penalty + apply_no_repeat_ngram main.c:186-213
                    (stored as the flat indices and values of the changed logits)
   topk_*           log_softmax_inplace + find_topk main.c:154-182
+  lin_*            mat_vec_int8 tensor.c:144-196 on each input row (stored rows
+                   only for the 300-row case: every 7th)
 """
 from __future__ import annotations
 
@@ -137,6 +139,25 @@ def topk_case(name):
 
 
 TOPK_CASES = ("topk_vocab8", "topk_vocab4", "topk_ties", "topk_small")
+
+
+def linear_case(name):
+    """x [M][K], int8 w [N][K] over [-127, 127], per-row scales around the
+    synthetic model's 3666.19 (x0.5 .. x2), bias or None; the stored rows."""
+    M, K, N, seed, with_bias = {"lin_m1_n4096": (1, 1024, 4096, 701, True),
+                                "lin_m4_n1024": (4, 1024, 1024, 711, False),
+                                "lin_m17_n4096": (17, 1024, 4096, 721, True),
+                                "lin_m300_n1024": (300, 1024, 1024, 731, True)}[name]
+    x = po.det_uniform(seed, (M, K))
+    w = (po.det_ints(seed + 1, N * K, -127, 128).reshape(N, K)).astype(np.int8)
+    f = (np.float32(0.5) + po.det_ints(seed + 2, N, 0, 16).astype(np.float32) * np.float32(0.1)).astype(np.float32)
+    scale = (np.float32(127.0 / (0.02 * np.sqrt(3.0))) * f).astype(np.float32)
+    bias = po.det_uniform(seed + 3, (N,), 0.5) if with_bias else None
+    rows = np.arange(0, M, 7) if M > 32 else np.arange(M)
+    return x, w, scale, bias, rows
+
+
+LINEAR_CASES = ("lin_m1_n4096", "lin_m4_n1024", "lin_m17_n4096", "lin_m300_n1024")
 
 
 def load_golden():

@@ -4,7 +4,8 @@ Runs the reference's own attention code (tensor.c / decoder.c compiled from
 the reference sources into oracle/_ref/ by oracle/Makefile) and main.c's
 penalty / log-softmax / top-k functions (oracle/ref_search_harness.c) on the
 seeded inputs defined in cases.py and stores their outputs.  Needs the reference
-sources at build time (REF_DIR, default /root/reference); the fixtures are
+sources at build time (REF_DIR, by default the reference checkout beside
+this repository, oracle/Makefile); the fixtures are
 committed so that nothing else ever needs them.
 
     python tests/golden/make_golden.py
@@ -48,6 +49,9 @@ def main() -> None:
         tok, sc = po.ref_logsoftmax_topk(logits, k)
         out[name + "_tok"] = tok
         out[name + "_logp"] = sc
+    for name in cases.LINEAR_CASES:
+        x, w, scale, bias, rows = cases.linear_case(name)
+        out[name] = po.ref_linear(x[rows], w, scale, bias)
     np.savez_compressed(cases.GOLDEN_NPZ, **out)
     for k_, v_ in out.items():
         print(f"{k_:22s} {str(v_.shape):22s} sum={float(np.sum(v_, dtype=np.float64)):+.6f}")

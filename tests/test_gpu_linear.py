@@ -46,3 +46,29 @@ def test_linear_int8_matches_reference(cuda_device, M, K, N, epilogue):
     err = np.abs(out.cpu().numpy().astype(np.float64) - ref)
     bound = 2e-6 * (terms + 1.0) + 1e-6 * np.abs(ref)
     assert (err <= bound).all(), f"max err {err.max():.3e}, worst ratio {(err / bound).max():.2f}"
+
+
+@pytest.mark.parametrize("name", ["lin_m1_n4096", "lin_m4_n1024", "lin_m17_n4096", "lin_m300_n1024"])
+def test_linear_int8_matches_reference_golden(cuda_device, name):
+    """Op-level pin: nllb_linear_int8 against the reference's own compiled
+    mat_vec_int8 (tensor.c:144-196) on the golden inputs (tests/golden/cases.py),
+    within the fp32 accumulation bound; both the SIMT (<= 16 rows) and the
+    tensor-core (17, 300 rows) paths.  The error word stays clear."""
+    import torch
+    import cases
+    x, w, scale, bias, rows = cases.linear_case(name)
+    gold = cases.load_golden()[name].astype(np.float64)
+    dev = lambda a: None if a is None else torch.from_numpy(np.ascontiguousarray(a)).to(cuda_device)
+    out = na.linear_int8(dev(x), dev(w), dev(scale), dev(bias))
+    assert na.linear_int8_status() == na.OK
+    got = out.cpu().numpy()[rows].astype(np.float64)
+    _, terms = reference(x[rows], w, scale, bias, False, None)
+    err = np.abs(got - gold)
+    bound = 2e-6 * (terms + 1.0) + 1e-6 * np.abs(gold)
+    assert (err <= bound).all(), f"{name}: max err {err.max():.3e}, worst ratio {(err / bound).max():.2f}"
+    # the prepared-weight path (the engine's layers) on the same golden
+    with na.PreparedLinear(dev(w), dev(scale), dev(bias)) as lin:
+        out2 = lin(dev(x))
+        assert lin.status() == 0
+    err2 = np.abs(out2.cpu().numpy()[rows].astype(np.float64) - gold)
+    assert (err2 <= bound).all(), f"{name} prepared: max err {err2.max():.3e}"

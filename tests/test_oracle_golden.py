@@ -99,3 +99,25 @@ def test_logsoftmax_topk_oracle_matches_reference(golden, name):
     tok, lp = po.logsoftmax_topk(logits, k)
     np.testing.assert_array_equal(tok, golden[name + "_tok"])
     np.testing.assert_allclose(lp, golden[name + "_logp"], atol=1e-4, rtol=1e-5)
+
+
+def linear_f64(x, w, scale, bias):
+    """mat_vec_int8's arithmetic (tensor.c:144-196) in float64 -- the checker
+    of the GPU linear-layer tests -- and the sum of |terms| per output."""
+    inv = (1.0 / scale.astype(np.float32)).astype(np.float64)
+    y = (x.astype(np.float64) @ w.astype(np.float64).T) * inv
+    terms = (np.abs(x.astype(np.float64)) @ np.abs(w.astype(np.float64)).T) * inv
+    if bias is not None:
+        y = y + bias.astype(np.float64)
+    return y, terms
+
+
+@pytest.mark.parametrize("name", cases.LINEAR_CASES)
+def test_linear_restatement_matches_reference(golden, name):
+    """The float64 restatement against the reference's compiled mat_vec_int8:
+    within the fp32 accumulation bound the GPU linear tests use."""
+    x, w, scale, bias, rows = cases.linear_case(name)
+    y, terms = linear_f64(x[rows], w, scale, bias)
+    err = np.abs(golden[name].astype(np.float64) - y)
+    bound = 2e-6 * (terms + 1.0) + 1e-6 * np.abs(y)
+    assert (err <= bound).all(), f"{name}: max err {err.max():.3e}, worst ratio {(err / bound).max():.2f}"

@@ -33,7 +33,8 @@ def _bound(x, w, scale, ref):
     return 2e-6 * (terms + 1.0) + 1e-6 * np.abs(ref)
 
 
-@pytest.mark.parametrize("M,K,N", [(64, 1024, 1024), (200, 4096, 1024), (256, 1024, 4096), (8, 1024, 512)])
+@pytest.mark.parametrize("M,K,N", [(64, 1024, 1024), (200, 4096, 1024), (256, 1024, 4096), (8, 1024, 512),
+                                   (64, 96, 1024)])
 def test_noalloc_matches_allocating_entry_point_twice(cuda_device, M, K, N):
     import torch
     x, w, scale, bias = _inputs(M + K + N, M, K, N, cuda_device)
@@ -47,6 +48,8 @@ def test_noalloc_matches_allocating_entry_point_twice(cuda_device, M, K, N):
         torch.cuda.synchronize()
         err = np.abs(out.cpu().numpy().astype(np.float64) - ref)
         assert np.isfinite(err).all() and (err <= bound).all(), f"call {call}: max err {np.nanmax(err):.3e}"
+        assert na.linear_int8_noalloc_status() == na.OK  # no bounded wait gave up
+    assert na.linear_int8_status() == na.OK
 
 
 def test_noalloc_takes_no_device_memory(cuda_device):
