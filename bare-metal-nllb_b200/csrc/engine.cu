@@ -237,6 +237,18 @@ struct nllb_model {
     int num_sms = 148;
     // decision margins of the last translate call, [sentence][step]
     std::vector<std::vector<float>> margins;
+    // per-kernel-class profile (nllb_translate_profile): CUDA events around
+    // each launch of a class on the engine's stream, resolved after each call
+    struct ProfRec {
+        int cat;
+        cudaEvent_t a, b;
+        double flops, bytes;
+    };
+    bool prof_on = false;
+    std::vector<cudaEvent_t> prof_events;  // pool, reused call after call
+    size_t prof_next = 0;
+    std::vector<ProfRec> prof_recs;
+    nllb_kernel_profile prof_agg[NLLB_PROF_CLASSES] = {};
 };
 
 namespace {
@@ -248,6 +260,57 @@ int dev_alloc(nllb_model* m, T** p, size_t count) {
     m->allocs.push_back(v);
     *p = static_cast<T*>(v);
     return NLLB_ATTN_OK;
+}
+
+const char* const kProfNames[NLLB_PROF_CLASSES] = {
+    "gemm_persistent", "gemm_cluster_splitk", "linear_simt_or_tc", "decode_self", "cross",
+    "prefill",         "logsoftmax_topk",     "penalties",         "beam_select", "reorder",
+    "layernorm",       "embed_pos",           "split3",            "set_memory"};
+
+// Times the launches made in its scope as one record of class `cat` (a no-op
+// unless profiling is on).  The events order the stream around the scope, so
+// a profiled call runs without dependent-launch overlap at those points.
+struct ProfScope {
+    nllb_model* m;
+    int cat;
+    double flops, bytes;
+    cudaEvent_t b = nullptr;
+    ProfScope(nllb_model* m_, int cat_, double flops_ = 0, double bytes_ = 0)
+        : m(m_), cat(cat_), flops(flops_), bytes(bytes_) {
+        if (!m->prof_on) return;
+        cudaEvent_t a = next_event();
+        b = next_event();
+        if (a && b && cudaEventRecord(a, m->stream) == cudaSuccess)
+            m->prof_recs.push_back({cat, a, b, flops, bytes});
+        else
+            b = nullptr;
+    }
+    ~ProfScope() {
+        if (b) cudaEventRecord(b, m->stream);
+    }
+    cudaEvent_t next_event() {
+        if (m->prof_next == m->prof_events.size()) {
+            cudaEvent_t e = nullptr;
+            if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+            m->prof_events.push_back(e);
+        }
+        return m->prof_events[m->prof_next++];
+    }
+};
+
+// Fold the records of the last call into the totals (after the stream has drained).
+void prof_resolve(nllb_model* m) {
+    for (const auto& r : m->prof_recs) {
+        float ms = 0.f;
+        if (cudaEventElapsedTime(&ms, r.a, r.b) != cudaSuccess) continue;
+        nllb_kernel_profile& g = m->prof_agg[r.cat];
+        g.launches += 1;
+        g.ms += ms;
+        g.flops += r.flops;
+        g.bytes += r.bytes;
+    }
+    m->prof_recs.clear();
+    m->prof_next = 0;
 }
 
 struct Loader {
@@ -343,6 +406,7 @@ void nllb_model_free(nllb_model* m) {
         if (b.first) cudaFree(b.first);
     for (auto& e : m->step_ev)
         if (e) cudaEventDestroy(e);
+    for (auto& e : m->prof_events) cudaEventDestroy(e);
     if (m->live_h) cudaFreeHost(m->live_h);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
@@ -497,6 +561,7 @@ int run_linear(nllb_model* m, const Lin& L, const float* x, int M, float* out, c
         if (out_planes && (cblock != L.out || residual))
             return nllb::set_error(NLLB_ATTN_EINVAL, "plane output needs a plain row-major result");
         if (!in_planes) {
+            ProfScope ps(m, 12, 0, (double)M * L.in * 10);
             ENG_CK(launch_split3(x, L.in, M, L.in, m->planes, m->stream));
             in_planes = m->planes;
         }
@@ -511,14 +576,19 @@ int run_linear(nllb_model* m, const Lin& L, const float* x, int M, float* out, c
                 ENG_CK(encode_bf16_map(&tx, in_planes, L.in, M, 3));
             it = m->plane_maps.emplace(key, tx).first;
         }
-        if (pers)
+        const double flops = 2.0 * M * L.out * L.in;
+        if (pers) {
+            ProfScope ps(m, 0, flops, (double)L.out * L.in * 2);
             ENG_CK(launch_linear_tma_persistent(a, &it->second, &L.tm256, m->num_sms, m->attn->err, m->stream));
-        else
+        } else {
+            ProfScope ps(m, 1, flops, (double)L.out * L.in * 2);
             ENG_CK(launch_linear_tma(a, &it->second, &L.tm, linear_tma_splits(M, L.out, L.in, m->num_sms),
                                      m->attn->err, m->stream));
+        }
         return NLLB_ATTN_OK;
     }
     if (in_planes || out_planes) return nllb::set_error(NLLB_ATTN_EINVAL, "planes need the tensor-core path");
+    ProfScope ps(m, 2, 2.0 * M * L.out * L.in, (double)L.out * L.in);
     ENG_CK(launch_linear(a, &m->lws, m->num_sms, m->attn->err, m->stream));
     return NLLB_ATTN_OK;
 }
@@ -551,6 +621,7 @@ struct Work {
     float* topk_ws = nullptr;  // partials of the vocabulary log-softmax / top-k
     unsigned char* active = nullptr;
     bool h_planes = false;  // the last decoder step left h as bf16 planes in m->planes (else fp32 in h)
+    const int* n_src_h = nullptr;  // host: source lengths in the call's internal order (profile bytes)
     // buffers come from the model's pool in call order: a call no larger than
     // an earlier one allocates nothing (the previous call has finished: it
     // returned its results to the host)
@@ -574,7 +645,11 @@ struct Work {
 
 int encode(nllb_model* m, Work& w, const std::vector<int>& n_src) {
     const int R = w.rows_enc;
-    ENG_CK(launch_embed_pos(w.ex, w.etok, w.epos, 0, m->emb, m->emb_inv, m->pos_table, 32.0f, R, VOCAB, m->stream));
+    {
+        ProfScope ps(m, 11, 0, (double)R * D * 5);
+        ENG_CK(launch_embed_pos(w.ex, w.etok, w.epos, 0, m->emb, m->emb_inv, m->pos_table, 32.0f, R, VOCAB,
+                                m->stream));
+    }
     // LayerNorm writes the bf16 planes of the next GEMM's input directly when
     // that GEMM runs on the tensor cores, fc1 writes fc2's input planes
     const bool tp = tma_path(m, m->enc[0].qkv, R);
@@ -583,7 +658,10 @@ int encode(nllb_model* m, Work& w, const std::vector<int>& n_src) {
     float* lnout = tp ? nullptr : w.eh;
     for (int l = 0; l < LAYERS; ++l) {
         auto& E = m->enc[l];
-        ENG_CK(launch_layernorm(lnout, w.ex, nullptr, E.ln1g, E.ln1b, R, P1, m->stream));
+        {
+            ProfScope ps(m, 10, 0, (double)R * D * 10);
+            ENG_CK(launch_layernorm(lnout, w.ex, nullptr, E.ln1g, E.ln1b, R, P1, m->stream));
+        }
         ENG_RC(run_linear(m, E.qkv, w.eh, R, w.eqkv, nullptr, 0, D, -1, P1));
         nllb_attn_prefill_args a{};
         a.q = w.eqkv;
@@ -599,9 +677,17 @@ int encode(nllb_model* m, Work& w, const std::vector<int>& n_src) {
         a.stride_row = D;
         a.valid_len = w.evalid;
         a.scale = 1.0f / sqrtf(64.0f);
-        ENG_RC(nllb::attn_prefill_packed(m->attn, &a, w.erow0));
+        {
+            double fl = 0;  // dense flops of the valid rows: 4 * S_s^2 * 64 per head
+            for (int s = 0; s < w.n_sent; ++s) fl += 4.0 * H * w.n_src_h[s] * w.n_src_h[s] * 64;
+            ProfScope ps(m, 5, fl, (double)R * D * 16);
+            ENG_RC(nllb::attn_prefill_packed(m->attn, &a, w.erow0));
+        }
         ENG_RC(run_linear(m, E.out, w.eattn, R, w.ex, w.ex, 0, D));
-        ENG_CK(launch_layernorm(lnout, w.ex, nullptr, E.ln2g, E.ln2b, R, P1, m->stream));
+        {
+            ProfScope ps(m, 10, 0, (double)R * D * 10);
+            ENG_CK(launch_layernorm(lnout, w.ex, nullptr, E.ln2g, E.ln2b, R, P1, m->stream));
+        }
         ENG_RC(run_linear(m, E.fc1, w.eh, R, w.effn, nullptr, 1, FFN, -1, P1, P2));
         ENG_RC(run_linear(m, E.fc2, w.effn, R, w.ex, w.ex, 0, D, -1, P2));
     }
@@ -611,6 +697,7 @@ int encode(nllb_model* m, Work& w, const std::vector<int>& n_src) {
     const size_t layer_floats = (size_t)c->d.max_sentences * H * (size_t)c->d.max_src * 64;
     for (int l = 0; l < LAYERS; ++l) {
         ENG_RC(run_linear(m, m->dec[l].xkv, w.eh, R, w.ekv, nullptr, 0, D, -1, P1));
+        ProfScope ps(m, 13, 0, (double)R * D * 16);
         ENG_CK(launch_set_memory_batched(c->km + l * layer_floats, c->vm + l * layer_floats,
                                          c->n_src_dev + (size_t)l * c->d.max_sentences, c->d.max_src, H, w.ekv,
                                          w.ekv + (size_t)R * D, 0, w.erow0, w.evalid, w.n_sent, w.S,
@@ -624,7 +711,19 @@ int encode(nllb_model* m, Work& w, const std::vector<int>& n_src) {
 // position `step`; leaves the final-LayerNorm output in w.h.
 int decode_step(nllb_model* m, Work& w, int step) {
     const int R = w.rows;
-    ENG_CK(launch_embed_pos(w.x, w.tok, nullptr, step + 2, m->emb, m->emb_inv, m->pos_table, 32.0f, R, VOCAB, m->stream));
+    {
+        ProfScope ps(m, 11, 0, (double)R * D * 5);
+        ENG_CK(launch_embed_pos(w.x, w.tok, nullptr, step + 2, m->emb, m->emb_inv, m->pos_table, 32.0f, R, VOCAB,
+                                m->stream));
+    }
+    // algorithmic bytes of the attention launches of this step: self-attention
+    // K/V of positions 0..step, q/out, new k/v, history (per sentence), and
+    // cross-attention memory rows plus q/out
+    const double L = step + 1;
+    const double self_bytes = (double)w.n_sent * (2.0 * NB * H * L * 256 + 4.0 * NB * H * 256 + 4.0 * NB * L);
+    double xrows = 0;
+    for (int s = 0; s < w.n_sent; ++s) xrows += w.n_src_h[s];
+    const double cross_bytes = 2.0 * H * xrows * 256 + (double)w.n_sent * 2.0 * NB * H * 256;
     const bool tp = tma_path(m, m->dec[0].qkv, R);
     void* P1 = tp ? m->planes : nullptr;
     void* P2 = tp ? m->planes2 : nullptr;
@@ -632,33 +731,57 @@ int decode_step(nllb_model* m, Work& w, int step) {
     w.h_planes = tp;  // the final LayerNorm below leaves h as planes (tp) or as fp32
     for (int l = 0; l < LAYERS; ++l) {
         auto& Dl = m->dec[l];
-        ENG_CK(launch_layernorm(lnout, w.x, nullptr, Dl.ln1g, Dl.ln1b, R, P1, m->stream));
+        {
+            ProfScope ps(m, 10, 0, (double)R * D * 10);
+            ENG_CK(launch_layernorm(lnout, w.x, nullptr, Dl.ln1g, Dl.ln1b, R, P1, m->stream));
+        }
         ENG_RC(run_linear(m, Dl.qkv, w.h, R, w.qkv, nullptr, 0, D, -1, P1));
         // on the tensor-core path the attention kernels write the output
         // projection's bf16 planes themselves (no fp32 output, no split pass)
         if (tp && tma_path(m, Dl.out, R)) {
-            ENG_RC(nllb::attn_decode_self_planes(m->attn, l, step, w.n_sent, w.qkv, w.qkv + (size_t)R * D,
-                                                 w.qkv + (size_t)2 * R * D, m->planes));
+            {
+                ProfScope ps(m, 3, 0, self_bytes);
+                ENG_RC(nllb::attn_decode_self_planes(m->attn, l, step, w.n_sent, w.qkv, w.qkv + (size_t)R * D,
+                                                     w.qkv + (size_t)2 * R * D, m->planes));
+            }
             ENG_RC(run_linear(m, Dl.out, w.attn, R, w.x, w.x, 0, D, -1, m->planes));
         } else {
-            ENG_RC(nllb_attn_decode_self(m->attn, l, step, w.n_sent, w.qkv, w.qkv + (size_t)R * D,
-                                         w.qkv + (size_t)2 * R * D, w.attn));
+            {
+                ProfScope ps(m, 3, 0, self_bytes);
+                ENG_RC(nllb_attn_decode_self(m->attn, l, step, w.n_sent, w.qkv, w.qkv + (size_t)R * D,
+                                             w.qkv + (size_t)2 * R * D, w.attn));
+            }
             ENG_RC(run_linear(m, Dl.out, w.attn, R, w.x, w.x, 0, D));
         }
-        ENG_CK(launch_layernorm(lnout, w.x, nullptr, Dl.ln2g, Dl.ln2b, R, P1, m->stream));
+        {
+            ProfScope ps(m, 10, 0, (double)R * D * 10);
+            ENG_CK(launch_layernorm(lnout, w.x, nullptr, Dl.ln2g, Dl.ln2b, R, P1, m->stream));
+        }
         ENG_RC(run_linear(m, Dl.xq, w.h, R, w.qx, nullptr, 0, D, -1, P1));
         if (tp && tma_path(m, Dl.xout, R)) {
-            ENG_RC(nllb::attn_cross_planes(m->attn, l, w.n_sent, w.qx, m->planes));
+            {
+                ProfScope ps(m, 4, 0, cross_bytes);
+                ENG_RC(nllb::attn_cross_planes(m->attn, l, w.n_sent, w.qx, m->planes));
+            }
             ENG_RC(run_linear(m, Dl.xout, w.attn, R, w.x, w.x, 0, D, -1, m->planes));
         } else {
-            ENG_RC(nllb_attn_cross(m->attn, l, w.n_sent, w.qx, w.attn));
+            {
+                ProfScope ps(m, 4, 0, cross_bytes);
+                ENG_RC(nllb_attn_cross(m->attn, l, w.n_sent, w.qx, w.attn));
+            }
             ENG_RC(run_linear(m, Dl.xout, w.attn, R, w.x, w.x, 0, D));
         }
-        ENG_CK(launch_layernorm(lnout, w.x, nullptr, Dl.ln3g, Dl.ln3b, R, P1, m->stream));
+        {
+            ProfScope ps(m, 10, 0, (double)R * D * 10);
+            ENG_CK(launch_layernorm(lnout, w.x, nullptr, Dl.ln3g, Dl.ln3b, R, P1, m->stream));
+        }
         ENG_RC(run_linear(m, Dl.fc1, w.h, R, w.ffn, nullptr, 1, FFN, -1, P1, P2));
         ENG_RC(run_linear(m, Dl.fc2, w.ffn, R, w.x, w.x, 0, D, -1, P2));
     }
-    ENG_CK(launch_layernorm(lnout, w.x, nullptr, m->dec_lng, m->dec_lnb, R, P1, m->stream));
+    {
+        ProfScope ps(m, 10, 0, (double)R * D * 10);
+        ENG_CK(launch_layernorm(lnout, w.x, nullptr, m->dec_lng, m->dec_lnb, R, P1, m->stream));
+    }
     return NLLB_ATTN_OK;
 }
 
@@ -668,9 +791,12 @@ int vocab_topk(nllb_model* m, Work& w, int k, bool penalties, const nllb_transla
                const int* hist = nullptr) {
     ENG_RC(run_linear(m, m->vocab, w.h, w.rows, w.logits, nullptr, 0, VOCAB_LD, LANG_START,
                       w.h_planes ? m->planes : nullptr));
-    if (penalties)
+    if (penalties) {
+        ProfScope ps(m, 7, 0, (double)w.rows * m->max_gen * 4);
         ENG_CK(launch_penalties(w.logits, VOCAB_LD, hist ? hist : w.hist, m->max_gen, w.ntok, w.active, w.rows,
                                 o.repetition_penalty, o.no_repeat_ngram, m->stream));
+    }
+    ProfScope ps(m, 6, 0, (double)w.rows * VOCAB * 4);
     ENG_CK(launch_logsoftmax_topk(w.logits, VOCAB_LD, VOCAB, w.rows, w.active, k, w.top_tok, w.top_lp, w.topk_ws,
                                   m->stream));
     return NLLB_ATTN_OK;
@@ -726,6 +852,7 @@ extern "C" int nllb_translate(nllb_model* m, int n_sent, const int* src_tokens, 
         max_out.swap(mo);
     }
     w.S = S;
+    w.n_src_h = n_src.data();
     std::vector<int> row0(n_sent);  // encoder rows are packed: sentence s at rows row0[s] ..
     int rows_enc = 0;
     for (int s = 0; s < n_sent; ++s) row0[s] = rows_enc, rows_enc += n_src[s];
@@ -911,10 +1038,16 @@ extern "C" int nllb_translate(nllb_model* m, int n_sent, const int* src_tokens, 
         B.n_sent = n_live;
         ENG_RC(decode_step(m, w, step));
         ENG_RC(vocab_topk(m, w, 8, true, o, cur ? B.bt1 : B.bt0));
-        ENG_CK(launch_beam_select(B, cur, w.top_tok, w.top_lp, step, m->stream));
+        {
+            ProfScope ps(m, 8);
+            ENG_CK(launch_beam_select(B, cur, w.top_tok, w.top_lp, step, m->stream));
+        }
         ENG_CK(cudaMemcpyAsync(m->live_h + step, B.live + step, sizeof(int), cudaMemcpyDeviceToHost, m->stream));
         ENG_CK(cudaEventRecord(m->step_ev[step & 3], m->stream));
-        ENG_RC(nllb_attn_reorder(m->attn, n_live, w.parent));
+        {
+            ProfScope ps(m, 9, 0, (double)n_live * (step + 1) * 8);
+            ENG_RC(nllb_attn_reorder(m->attn, n_live, w.parent));
+        }
         cur ^= 1;
         launched_to = step;
     }
@@ -922,6 +1055,7 @@ extern "C" int nllb_translate(nllb_model* m, int n_sent, const int* src_tokens, 
     w.rows = (int)R;
     B.n_sent = n_sent;
     ENG_RC(nllb_attn_sync(m->attn));
+    if (m->prof_on) prof_resolve(m);
     for (int t = 3; t <= launched_to; ++t) steps_run += m->live_h[t - 1] > 0;
 
     // ---- device beam state back to the host structures of the final choice
@@ -1052,6 +1186,25 @@ extern "C" int nllb_linear_int8_status(void) {
     ENG_CK(cudaMemset(w, 0, sizeof(int)));
     if (h) return nllb::set_error(NLLB_ATTN_ETIMEOUT, "a bounded device wait of the linear kernel gave up");
     return NLLB_ATTN_OK;
+}
+
+extern "C" int nllb_translate_profile(nllb_model* m, int enable) {
+    if (!m) return nllb::set_error(NLLB_ATTN_EINVAL, "model required");
+    m->prof_on = enable != 0;
+    for (int c = 0; c < NLLB_PROF_CLASSES; ++c) {
+        m->prof_agg[c] = nllb_kernel_profile{};
+        std::snprintf(m->prof_agg[c].name, sizeof(m->prof_agg[c].name), "%s", kProfNames[c]);
+    }
+    m->prof_recs.clear();
+    m->prof_next = 0;
+    return NLLB_ATTN_OK;
+}
+
+extern "C" int nllb_translate_profile_read(const nllb_model* m, nllb_kernel_profile* out, int max_classes) {
+    if (!m || !out) return 0;
+    const int n = std::min(max_classes, (int)NLLB_PROF_CLASSES);
+    for (int c = 0; c < n; ++c) out[c] = m->prof_agg[c];
+    return n;
 }
 
 extern "C" int nllb_linear_int8(const float* x, int M, int K, const int8_t* w, const float* weight_scale,

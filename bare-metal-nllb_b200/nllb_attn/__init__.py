@@ -50,6 +50,13 @@ class TranslateStats(ctypes.Structure):
                 ("steps", ctypes.c_int), ("tokens_out", ctypes.c_longlong)]
 
 
+class KernelProfile(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char * 32), ("launches", ctypes.c_longlong), ("ms", ctypes.c_double),
+                ("flops", ctypes.c_double), ("bytes", ctypes.c_double)]
+
+
+PROF_CLASSES = 14
+
 SIGNATURES = {
     "nllb_attn_create": (_c_int, [_c_int, ctypes.POINTER(Dims), ctypes.POINTER(_c_void_p)]),
     "nllb_attn_destroy": (None, [_c_void_p]),
@@ -82,6 +89,8 @@ SIGNATURES = {
     "nllb_translate": (_c_int, [_c_void_p, _c_int, _fp, _fp, _c_int, ctypes.POINTER(TranslateOpts),
                                 _fp, _fp, _fp, ctypes.POINTER(TranslateStats)]),
     "nllb_translate_margins": (_c_int, [_c_void_p, _c_int, _fp, _c_int]),
+    "nllb_translate_profile": (_c_int, [_c_void_p, _c_int]),
+    "nllb_translate_profile_read": (_c_int, [_c_void_p, ctypes.POINTER(KernelProfile), _c_int]),
     "nllb_linear_int8": (_c_int, [_fp, _c_int, _c_int, _fp, _fp, _fp, _c_int, _fp, _fp, _c_int, _c_void_p]),
     "nllb_linear_int8_status": (_c_int, []),
     "nllb_linear_int8_noalloc": (_c_int, [_fp, _c_int, _c_int, _fp, _fp, _fp, _c_int, _fp, _fp, _c_int,
@@ -297,6 +306,19 @@ class Model:
                                                  ctypes.byref(st)), "nllb_translate")
         toks = [out[i, :lens[i]].tolist() for i in range(len(sources))]
         return toks, scores, st
+
+    def profile(self, enable: bool = True) -> None:
+        """nllb_translate_profile: time the following translate calls' kernel
+        launches by class (clears the totals)."""
+        _check(self.lib, self.lib.nllb_translate_profile(self.handle, 1 if enable else 0), "nllb_translate_profile")
+
+    def profile_read(self):
+        """Per-class totals: {name: {launches, ms, flops, bytes}}."""
+        buf = (KernelProfile * PROF_CLASSES)()
+        n = self.lib.nllb_translate_profile_read(self.handle, buf, PROF_CLASSES)
+        return {buf[i].name.decode(): {"launches": int(buf[i].launches), "ms": float(buf[i].ms),
+                                       "flops": float(buf[i].flops), "bytes": float(buf[i].bytes)}
+                for i in range(n)}
 
     def margins(self, sentence: int, max_steps: int = 1024):
         import numpy as np

@@ -68,6 +68,28 @@ NLLB_ATTN_API int nllb_translate(nllb_model* m, int n_sentences, const int* src_
  * written (at most max_steps). */
 NLLB_ATTN_API int nllb_translate_margins(const nllb_model* m, int sentence, float* out, int max_steps);
 
+/* Kernel time by class.  nllb_translate_profile(m, 1) clears the totals and
+ * makes the following nllb_translate calls time every launch of each kernel
+ * class with a pair of CUDA events on the engine's stream (which orders the
+ * stream at those points: a profiled call runs somewhat slower, without the
+ * overlap of dependent launches there); 0 turns it off and clears.
+ * nllb_translate_profile_read copies the totals of up to max_classes classes
+ * and returns how many it wrote: per class its name, launches, summed
+ * milliseconds, and algorithmic work -- dense FLOPs (2*M*N*K for a linear
+ * layer, 4*S^2*64 per head for the encoder attention) and bytes (the
+ * attention kernels: K/V rows, q/out, new k/v and beam history for
+ * self-attention; memory rows and q/out for cross-attention). */
+#define NLLB_PROF_CLASSES 14
+typedef struct {
+    char name[32];
+    long long launches;
+    double ms;
+    double flops;
+    double bytes;
+} nllb_kernel_profile;
+NLLB_ATTN_API int nllb_translate_profile(nllb_model* m, int enable);
+NLLB_ATTN_API int nllb_translate_profile_read(const nllb_model* m, nllb_kernel_profile* out, int max_classes);
+
 /* ---- INT8-weight linear layer -------------------------------------------
  * out[m][n] = sum_k x[m][k] * (w[n][k] * (1.0f / weight_scale[n])) + bias[n]
  * for M rows at once: mat_vec_int8 (tensor.c:144-196) batched, with the

@@ -36,3 +36,12 @@ def cuda_device():
     if not torch.cuda.is_available():
         pytest.fail("GPU test selected but no CUDA device is visible")
     return torch.device("cuda:0")
+
+
+@pytest.fixture(scope="session")
+def synth_model_path(tmp_path_factory):
+    """The seeded synthetic model: $NLLB_SYNTH_MODEL when set, else written
+    once per session outside the repository (about 860 MB, ~30 s)."""
+    from nllb_attn import synth_model as sm
+    path = os.environ.get("NLLB_SYNTH_MODEL") or str(tmp_path_factory.mktemp("synth") / "synth_seed0.safetensors")
+    return sm.ensure_model(path, seed=0)

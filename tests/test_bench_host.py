@@ -55,3 +55,14 @@ def test_cpu_placement_without_nvml_changes_nothing():
         assert os.sched_getaffinity(0) == before
     else:
         os.sched_setaffinity(0, before)
+
+
+@pytest.mark.skipif(not os.path.exists(bench.REF_PROGRAM), reason="reference program not built")
+def test_reference_program_sample(synth_model_path):
+    """The reference arm's bounded sample: one reference program on the first
+    workload sentence, encode then a 1 s window of beam-search steps; its
+    rate is a whole-sentence rate below the window's step rate."""
+    rate, per = bench.reference_program_rate(synth_model_path, bench.reference_sample(0, 1), 1.0, 1)
+    assert len(per) == 1 and per[0]["steps_in_window"] >= 2
+    assert 0 < rate < per[0]["step_rate"]
+    assert per[0]["n_src"] == len(bench.reference_sample(0, 1)[0])
