@@ -18,15 +18,23 @@ struct nllb_attn_ctx {
     cudaStream_t stream = nullptr;
     float* kc = nullptr;  // [L][S][H][T][NB][64]
     float* vc = nullptr;
-    unsigned char* hist = nullptr;  // [S][Tp][8]
+    unsigned char* hist = nullptr;      // [S][Tp][8], the current beam history
+    unsigned char* hist_alt = nullptr;  // the other history buffer (a fused reorder writes it)
+    // a reorder not applied yet: the next self-attention launch over all
+    // max_sentences sentences applies it on the way (then the buffers swap);
+    // anything else applies it with the reorder kernel first
+    const int* pending_parent = nullptr;  // device [pending_n][n_beams]
+    int pending_n = 0;
+    bool expire_next_wait = false;  // test: the next self-attention launch's wait runs out
     float* km = nullptr;  // [L][S][H][max_src][64]
     float* vm = nullptr;
     int* n_src_dev = nullptr;  // [L][S]
     std::vector<int> n_src_host;
     int* err = nullptr;
     // staging for *_host calls, grown on demand
-    void* stg[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
-    size_t stg_bytes[6] = {0, 0, 0, 0, 0, 0};
+    // (slot 6: reorder_host's parents, which a pending reorder may still read)
+    void* stg[7] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+    size_t stg_bytes[7] = {0, 0, 0, 0, 0, 0, 0};
     // pipelined host-buffer decode: input copies on copy_in, kernels on stream,
     // output copies on copy_out, chunk by chunk of sentences (created on first use)
 // Measured on B200 (128 sentences x 4 beams, pinned buffers): 1 chunk 288 us
@@ -53,6 +61,6 @@ int attn_decode_self_planes(nllb_attn_ctx* c, int layer, int step, int n_sent, c
 int attn_cross_planes(nllb_attn_ctx* c, int layer, int n_sent, const float* q, void* planes);
 // nllb_attn_prefill over packed rows: sequence b's row r at row_start[b] + r
 // (device array; stride_batch unused); only its valid_len[b] >= 1 rows are
-// read and written.  Not exported.
-int attn_prefill_packed(nllb_attn_ctx* c, const nllb_attn_prefill_args* a, const int* row_start);
+// read and written; the q/k/v buffers hold rows_total rows.  Not exported.
+int attn_prefill_packed(nllb_attn_ctx* c, const nllb_attn_prefill_args* a, const int* row_start, int rows_total);
 }  // namespace nllb

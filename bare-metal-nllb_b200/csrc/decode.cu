@@ -122,8 +122,17 @@ __device__ __forceinline__ void merge_local(const float* recs, int nsrc, int str
 // ---------------------------------------------------------------------------
 // Decoder self-attention
 // ---------------------------------------------------------------------------
-template <int NB, bool PLANES>
-__global__ void __launch_bounds__(kThreads) decode_self_kernel(const SelfParams p) {
+// MODE 0: the history as it is.  MODE 1 (P = SelfParamsR): a pending beam
+// reorder is applied on the way -- logical beam b reads the slot of its
+// parent, hist[p][parent[b]], from the current history p.hist, and the
+// head-0 CTAs write the composed rows of their positions, plus the new
+// position, to the other history buffer p.hist_w; no reorder launch.
+// MODE 2: the bounded-wait test -- chunk 0 is never requested and the main
+// loop waits for it with a ~1 ms budget, so the wait runs out; the kernel
+// takes its timeout path (error bit, drain of the copies it did issue, no
+// output).
+template <int NB, bool PLANES, int MODE, typename P>
+__global__ void __launch_bounds__(kThreads) decode_self_kernel(const P p) {
     constexpr int CP = kSelfChunkRows / NB;  // positions per chunk
     constexpr int NSUB = 8 / NB;         // half-warps per beam
     constexpr int RPH = CP / NSUB;       // positions per half-warp per chunk
@@ -136,6 +145,7 @@ __global__ void __launch_bounds__(kThreads) decode_self_kernel(const SelfParams 
     float* sV = sK + kSelfStages * KV_FLOATS;
     unsigned char* sH = reinterpret_cast<unsigned char*>(sV + kSelfStages * KV_FLOATS);
     __shared__ int s_abort;
+    __shared__ int s_par[8];  // MODE 1: parent of each logical beam
 
     pdl_launch_dependents();
 
@@ -175,7 +185,20 @@ __global__ void __launch_bounds__(kThreads) decode_self_kernel(const SelfParams 
         bulk_g2s(sH + st * H_BYTES, gH + (size_t)pc0 * 8, hb, &bar[st]);
     };
     if (tid == 0) {
-        for (int c = 0; c < kSelfStages - 1 && c < nchunk; ++c) issue(c);
+        for (int c = 0; c < kSelfStages - 1 && c < nchunk; ++c)
+            if (MODE != 2 || c != 0) issue(c);
+    }
+    if constexpr (MODE == 1) {
+        // parents come from an earlier kernel (after the wait above); seen by
+        // all threads after the first chunk's barrier
+        if (tid < NB) {
+            int v = p.parent[(size_t)s * NB + tid];
+            if (v < 0 || v >= NB) {
+                if (split == 0 && h == 0) atomicOr(p.err, NLLB_DEV_ERR_BAD_PARENT);
+                v = tid;  // stays in bounds; the call reports the error
+            }
+            s_par[tid] = v;
+        }
     }
 
     const float4 qv = __ldg(reinterpret_cast<const float4*>(p.q + qrow) + l16);
@@ -193,7 +216,7 @@ __global__ void __launch_bounds__(kThreads) decode_self_kernel(const SelfParams 
     for (int c = 0; c < nchunk; ++c) {
         const int st = c % kSelfStages;
         const uint32_t par = (uint32_t)((c / kSelfStages) & 1);
-        if (!mbar_wait_bounded(&bar[st], par)) s_abort = 1;
+        if (!mbar_wait_bounded(&bar[st], par, MODE == 2 ? kTestWaitBudgetCycles : kWaitBudgetCycles)) s_abort = 1;
         __syncthreads();  // stage (c-1) fully consumed; abort flag visible
         if (s_abort) break;
         consumed = c + 1;
@@ -203,6 +226,19 @@ __global__ void __launch_bounds__(kThreads) decode_self_kernel(const SelfParams 
         const float* K = sK + st * KV_FLOATS;
         const float* V = sV + st * KV_FLOATS;
         const unsigned char* Hs = sH + st * H_BYTES;
+        int hb = b;  // the byte of a history row naming this beam's slot
+        if constexpr (MODE == 1) {
+            hb = s_par[b];
+            if (h == 0 && tid < np) {  // composed row of position p0 + c*CP + tid
+                const unsigned char* src = Hs + tid * 8;
+                unsigned char row[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) row[j] = (j < NB) ? src[s_par[j]] : src[j];
+                uint2 v;
+                memcpy(&v, row, 8);
+                *reinterpret_cast<uint2*>(p.hist_w + ((size_t)s * p.Tp + (p0 + c * CP + tid)) * 8) = v;
+            }
+        }
 
         float sc[RPH];
         int slot[RPH];
@@ -210,7 +246,7 @@ __global__ void __launch_bounds__(kThreads) decode_self_kernel(const SelfParams 
         for (int i = 0; i < RPH; ++i) {
             const int pl = sub + i * NSUB;
             const bool ok = pl < np;
-            slot[i] = ok ? Hs[pl * 8 + b] : 0;
+            slot[i] = ok ? Hs[pl * 8 + hb] : 0;
             float4 kv = make_float4(0.f, 0.f, 0.f, 0.f);
             if (ok) kv = reinterpret_cast<const float4*>(K + (pl * NB + slot[i]) * 64)[l16];
             const float d = halfwarp_sum(f4_dot(qv, kv));
@@ -249,7 +285,8 @@ __global__ void __launch_bounds__(kThreads) decode_self_kernel(const SelfParams 
             atomicOr(p.err, NLLB_DEV_ERR_TIMEOUT);
             const int issued = min(nchunk, consumed + kSelfStages - 1);
             for (int c = consumed; c < issued; ++c)
-                (void)mbar_wait_bounded(&bar[c % kSelfStages], (uint32_t)((c / kSelfStages) & 1));
+                if (MODE != 2 || c != 0)  // the test mode never requested chunk 0
+                    (void)mbar_wait_bounded(&bar[c % kSelfStages], (uint32_t)((c / kSelfStages) & 1));
         }
     } else {
         // The new token at position `step`: every beam attends to its own k_new.
@@ -325,8 +362,12 @@ __global__ void __launch_bounds__(kThreads) cross_kernel(const CrossParams p) {
         s_abort = 0;
     }
     __syncthreads();
-    pdl_wait_primary();  // memory, lengths and q come from earlier kernels
-
+    // The memory rows and lengths are read before the wait on the previous
+    // kernel: their writers (set_memory_kernel, set_memory_batched_kernel)
+    // let no dependent start before they complete, so every kernel after
+    // them in the stream starts after the memory is written.  The first
+    // chunks' copies thus overlap the previous kernel's tail; q comes after
+    // the wait.
     const int len = __ldg(p.n_src + s);
     const int p0 = split * p.pos_per_split;
     const int p1 = min(len, p0 + p.pos_per_split);
@@ -348,6 +389,7 @@ __global__ void __launch_bounds__(kThreads) cross_kernel(const CrossParams p) {
     if (tid == 0) {
         for (int c = 0; c < kCrossStages - 1 && c < nchunk; ++c) issue(c);
     }
+    pdl_wait_primary();  // q comes from the previous kernel; the output may still be read by it
 
     float4 qv[NB];
 #pragma unroll
@@ -517,7 +559,9 @@ __global__ void hist_init_kernel(unsigned char* hist, size_t n_rows) {
 }
 
 // k[r*stride_row + h*stride_head + d] -> km[h][r][d] (one layer, one sentence);
-// thread 0 of block 0 also records the row count.
+// thread 0 of block 0 also records the row count.  Launched without
+// programmatic dependent launch and never triggering its dependents early
+// (cross_kernel reads the memory before its wait on the previous kernel).
 __global__ void set_memory_kernel(float* km, float* vm, int max_src, int H, const float* k,
                                   const float* v, long long stride_head, long long stride_row,
                                   int n_src, int* n_src_slot) {
@@ -582,10 +626,18 @@ cudaError_t launch_ex(void (*kernel)(Params), dim3 grid, size_t smem, int cluste
 
 template <int NB, bool PLANES>
 cudaError_t configure_nb_out() {
-    cudaError_t e = cudaFuncSetAttribute(decode_self_kernel<NB, PLANES>,
+    cudaError_t e = cudaFuncSetAttribute(decode_self_kernel<NB, PLANES, 0, SelfParams>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)self_smem_bytes<NB>());
     if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(decode_self_kernel<NB, PLANES, 1, SelfParamsR>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)self_smem_bytes<NB>());
+    if (e != cudaSuccess) return e;
+    if constexpr (NB == 4 && !PLANES) {
+        e = cudaFuncSetAttribute(decode_self_kernel<4, false, 2, SelfParams>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)self_smem_bytes<4>());
+        if (e != cudaSuccess) return e;
+    }
     e = cudaFuncSetAttribute(cross_kernel<NB, kCrossShortRows, 3, PLANES>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)cross_smem_bytes<NB, kCrossShortRows, 3>());
@@ -607,14 +659,30 @@ cudaError_t configure_nb() {
 }
 
 template <int NB, bool PLANES>
-cudaError_t launch_self_out(const SelfParams& p, int n_sent, cudaStream_t st) {
-    return launch_ex(decode_self_kernel<NB, PLANES>, dim3(p.n_split, p.H, n_sent), self_smem_bytes<NB>(),
-                     p.n_split, st, p);
+cudaError_t launch_self_out(const SelfParams& p, int n_sent, cudaStream_t st, SelfMode mode, const int* parent) {
+    const dim3 grid(p.n_split, p.H, n_sent);
+    if (mode == SelfMode::reorder) {
+        SelfParamsR r;
+        static_cast<SelfParams&>(r) = p;
+        r.parent = parent;
+        return launch_ex(decode_self_kernel<NB, PLANES, 1, SelfParamsR>, grid, self_smem_bytes<NB>(), p.n_split,
+                         st, r);
+    }
+    if (mode == SelfMode::expire_wait) {
+        if constexpr (NB == 4 && !PLANES)
+            return launch_ex(decode_self_kernel<4, false, 2, SelfParams>, grid, self_smem_bytes<4>(), p.n_split,
+                             st, p);
+        else
+            return cudaErrorInvalidValue;
+    }
+    return launch_ex(decode_self_kernel<NB, PLANES, 0, SelfParams>, grid, self_smem_bytes<NB>(), p.n_split, st, p);
 }
 
 template <int NB>
-cudaError_t launch_self_nb(const SelfParams& p, int n_sent, cudaStream_t st, bool planes) {
-    return planes ? launch_self_out<NB, true>(p, n_sent, st) : launch_self_out<NB, false>(p, n_sent, st);
+cudaError_t launch_self_nb(const SelfParams& p, int n_sent, cudaStream_t st, bool planes, SelfMode mode,
+                           const int* parent) {
+    return planes ? launch_self_out<NB, true>(p, n_sent, st, mode, parent)
+                  : launch_self_out<NB, false>(p, n_sent, st, mode, parent);
 }
 
 template <int NB, bool PLANES>
@@ -645,12 +713,13 @@ cudaError_t configure_decode_kernels() {
     return configure_nb<8>();
 }
 
-cudaError_t launch_decode_self(const SelfParams& p, int n_sent, int n_beams, cudaStream_t st, bool planes) {
+cudaError_t launch_decode_self(const SelfParams& p, int n_sent, int n_beams, cudaStream_t st, bool planes,
+                               SelfMode mode, const int* parent) {
     switch (n_beams) {
-        case 1: return launch_self_nb<1>(p, n_sent, st, planes);
-        case 2: return launch_self_nb<2>(p, n_sent, st, planes);
-        case 4: return launch_self_nb<4>(p, n_sent, st, planes);
-        case 8: return launch_self_nb<8>(p, n_sent, st, planes);
+        case 1: return launch_self_nb<1>(p, n_sent, st, planes, mode, parent);
+        case 2: return launch_self_nb<2>(p, n_sent, st, planes, mode, parent);
+        case 4: return launch_self_nb<4>(p, n_sent, st, planes, mode, parent);
+        case 8: return launch_self_nb<8>(p, n_sent, st, planes, mode, parent);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -23,6 +23,8 @@ constexpr int NLLB_DEV_ERR_BAD_PARENT = 2;
 
 // ~1 s at 2 GHz: far above any legitimate wait for a copy of a few KB.
 constexpr long long kWaitBudgetCycles = 2000000000LL;
+// ~1 ms: the budget of the one wait the bounded-wait test makes run out.
+constexpr long long kTestWaitBudgetCycles = 2000000LL;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -71,12 +73,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait for phase `parity` of `bar`; false if the budget ran out.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+// Bounded wait for phase `parity` of `bar`; false if the budget (clock64
+// cycles) ran out.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  long long budget = kWaitBudgetCycles) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     while (!mbar_try_wait(bar, parity)) {
-        if (clock64() - t0 > kWaitBudgetCycles) return false;
+        if (clock64() - t0 > budget) return false;
     }
     return true;
 }

@@ -681,7 +681,7 @@ int encode(nllb_model* m, Work& w, const std::vector<int>& n_src) {
             double fl = 0;  // dense flops of the valid rows: 4 * S_s^2 * 64 per head
             for (int s = 0; s < w.n_sent; ++s) fl += 4.0 * H * w.n_src_h[s] * w.n_src_h[s] * 64;
             ProfScope ps(m, 5, fl, (double)R * D * 16);
-            ENG_RC(nllb::attn_prefill_packed(m->attn, &a, w.erow0));
+            ENG_RC(nllb::attn_prefill_packed(m->attn, &a, w.erow0, w.rows_enc));
         }
         ENG_RC(run_linear(m, E.out, w.eattn, R, w.ex, w.ex, 0, D));
         {

@@ -614,7 +614,9 @@ __global__ void __launch_bounds__(256) vocab_merge_kernel(const float* ws, int C
 __global__ void set_memory_batched_kernel(float* km, float* vm, int* n_src_slots, int max_src, int H,
                                           const float* k, const float* v, long long sent_stride,
                                           const int* row_start, const int* n_src, int n_sent) {
-    pdl_launch_dependents();
+    // No early pdl_launch_dependents: the cross-attention kernel reads the
+    // memory before its own wait on the previous kernel, which is safe only
+    // because no kernel after this one starts before it completes.
     pdl_wait_primary();  // inputs come from earlier kernels; outputs may still be read by them
     const int s = blockIdx.y;
     const int n = n_src[s];

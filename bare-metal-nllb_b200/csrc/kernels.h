@@ -4,6 +4,8 @@
 #pragma once
 #include <cstddef>
 #include <cstdint>
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 namespace nllb {
@@ -48,7 +50,8 @@ struct SelfParams {
     float* kc_w;          // same as kc (written at `step`)
     float* vc_w;
     const uint8_t* hist;  // [S][Tp][8]
-    uint8_t* hist_w;      // same buffer, written at `step` (head 0 only)
+    uint8_t* hist_w;      // same buffer, written at `step` (head 0 only); the other
+                          // history buffer in the reorder form (SelfParamsR)
     const float* q;       // [n_sent][n_beams][H*64]
     const float* k_new;
     const float* v_new;
@@ -66,7 +69,19 @@ struct SelfParams {
 
 // (Adding fields to SelfParams changed the register allocation of the
 // self-attention kernel -- 48 to 40 registers -- and cost 4 % of its stream
-// rate on B200; the plane output therefore reuses `out`.)
+// rate on B200; the plane output therefore reuses `out`, and the reorder
+// form below is a separate type that only its own instantiation takes.)
+
+// A launch that applies a pending beam reorder on the way: logical beam b of
+// sentence s reads position p from slot hist[p][parent[s*n_beams + b]] of the
+// current history (hist) and the composed rows go to the other history
+// buffer (hist_w), which becomes the current one.
+struct SelfParamsR : SelfParams {
+    const int* parent;  // [n_sent][n_beams], device
+};
+
+// Which form of the self-attention kernel a launch uses.
+enum class SelfMode { plain = 0, reorder = 1, expire_wait = 2 };
 
 // ---- cross-attention (decode.cu) ------------------------------------------
 // Memory layout of one layer: [sentence][head][max_src][64] fp32, K and V.
@@ -99,14 +114,25 @@ struct PrefillParams {
     // base is row_start[b] * sr + h * sh, sb unused); only its valid_len[b]
     // rows are read and written, so sequences may lie back to back
     const int* row_start;
+    int rows_total;  // packed rows: rows in the q/k/v buffers (the tensor maps' extent)
+    // (set by the launcher) positions 0..2 of the row, head and sequence axes
+    // among the outer axes of the tensor-core kernel's tensor maps
+    int map_pos_row, map_pos_head, map_pos_seq;
 };
+
+// cuTensorMapEncodeTiled from the driver (nullptr if unavailable); linear_tma.cu.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
 // Per-device kernel attributes (dynamic shared memory); call once per device.
 cudaError_t configure_decode_kernels();
 cudaError_t configure_prefill_kernels();
 
-// planes: p.out is the base of the output planes (see SelfParams::out)
-cudaError_t launch_decode_self(const SelfParams& p, int n_sent, int n_beams, cudaStream_t st, bool planes = false);
+// planes: p.out is the base of the output planes (see SelfParams::out).
+// mode reorder: `parent` is the pending reorder (SelfParamsR::parent) and
+// p.hist_w the other history buffer.  mode expire_wait: the bounded-wait
+// test (4 beams, fp32 output only).
+cudaError_t launch_decode_self(const SelfParams& p, int n_sent, int n_beams, cudaStream_t st, bool planes = false,
+                               SelfMode mode = SelfMode::plain, const int* parent = nullptr);
 // chunk_rows: cross_chunk_rows(longest memory of the call)
 cudaError_t launch_cross(const CrossParams& p, int n_sent, int n_beams, int chunk_rows, cudaStream_t st,
                          bool planes = false);

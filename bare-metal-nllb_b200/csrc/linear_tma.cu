@@ -567,11 +567,7 @@ cudaError_t configure_linear_tma() {
     return cudaFuncSetAttribute(linear_tma_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
 }
 
-// Tensor map of a row-major bf16 matrix stack: `planes` matrices of
-// [rows][cols] (K-major), box box_cols x box_rows (x planes), with the
-// 128-byte swizzle (box_cols 64) or the 64-byte swizzle (box_cols 32).
-cudaError_t encode_bf16_map_box(CUtensorMap* map, const void* base, int cols, int rows, int planes, int box_cols,
-                                int box_rows) {
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     std::call_once(g_encode_once, [] {
         cudaDriverEntryPointQueryResult q;
         void* fn = nullptr;
@@ -579,7 +575,15 @@ cudaError_t encode_bf16_map_box(CUtensorMap* map, const void* base, int cols, in
             q == cudaDriverEntryPointSuccess)
             g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     });
-    if (!g_encode) return cudaErrorNotSupported;
+    return g_encode;
+}
+
+// Tensor map of a row-major bf16 matrix stack: `planes` matrices of
+// [rows][cols] (K-major), box box_cols x box_rows (x planes), with the
+// 128-byte swizzle (box_cols 64) or the 64-byte swizzle (box_cols 32).
+cudaError_t encode_bf16_map_box(CUtensorMap* map, const void* base, int cols, int rows, int planes, int box_cols,
+                                int box_rows) {
+    if (!tensor_map_encoder()) return cudaErrorNotSupported;
     if (box_cols != 64 && box_cols != 32) return cudaErrorInvalidValue;
     const cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)planes};
     const cuuint64_t strides[2] = {(cuuint64_t)cols * 2, (cuuint64_t)cols * rows * 2};

@@ -75,7 +75,7 @@ size_t device_bytes(const nllb_attn_dims& d) {
     size_t b = 0;
     b += 2 * cache_floats(d) * sizeof(float);
     b += 2 * mem_floats(d) * sizeof(float);
-    b += (size_t)d.max_sentences * hist_rows(d) * 8;
+    b += 2 * (size_t)d.max_sentences * hist_rows(d) * 8;  // current and other beam history
     b += (size_t)d.n_layers * d.max_sentences * sizeof(int);
     b += sizeof(int);
     return b;
@@ -127,6 +127,18 @@ int finish_host_call(nllb_attn_ctx* c) {
     return check_device_error(c);
 }
 
+// Apply a pending reorder with the reorder kernel (in place on the current
+// history) and forget it.
+int flush_reorder(nllb_attn_ctx* c) {
+    if (!c->pending_parent) return NLLB_ATTN_OK;
+    const int* par = c->pending_parent;
+    const int n = c->pending_n;
+    c->pending_parent = nullptr;
+    c->pending_n = 0;
+    NLLB_CK(launch_reorder(c->hist, c->Tp, par, n, c->d.n_beams, c->err, c->stream));
+    return NLLB_ATTN_OK;
+}
+
 // Split count for a (sentence, head) grid of `units` over `len` rows in
 // chunks of `chunk` rows: enough CTAs to cover the SMs twice, each split at
 // least one chunk, at most one cluster (kMaxSplit CTAs) per (sentence, head).
@@ -173,7 +185,7 @@ void nllb_attn_destroy(nllb_attn_ctx* c) {
     if (!c) return;
     cudaSetDevice(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
-    for (void* p : {(void*)c->kc, (void*)c->vc, (void*)c->hist, (void*)c->km, (void*)c->vm,
+    for (void* p : {(void*)c->kc, (void*)c->vc, (void*)c->hist, (void*)c->hist_alt, (void*)c->km, (void*)c->vm,
                     (void*)c->n_src_dev, (void*)c->err})
         if (p) cudaFree(p);
     for (void* p : c->stg)
@@ -240,6 +252,7 @@ int nllb_attn_create(int device, const nllb_attn_dims* dims, nllb_attn_ctx** out
         NLLB_CKC(cudaMalloc(&c->km, mf * sizeof(float)));
         NLLB_CKC(cudaMalloc(&c->vm, mf * sizeof(float)));
         NLLB_CKC(cudaMalloc(&c->hist, (size_t)d.max_sentences * c->Tp * 8));
+        NLLB_CKC(cudaMalloc(&c->hist_alt, (size_t)d.max_sentences * c->Tp * 8));
         NLLB_CKC(cudaMalloc(&c->n_src_dev, (size_t)d.n_layers * d.max_sentences * sizeof(int)));
         NLLB_CKC(cudaMemsetAsync(c->kc, 0, cf * sizeof(float), c->stream));
         NLLB_CKC(cudaMemsetAsync(c->vc, 0, cf * sizeof(float), c->stream));
@@ -248,6 +261,7 @@ int nllb_attn_create(int device, const nllb_attn_dims* dims, nllb_attn_ctx** out
         NLLB_CKC(cudaMemsetAsync(c->n_src_dev, 0, (size_t)d.n_layers * d.max_sentences * sizeof(int),
                                  c->stream));
         NLLB_CKC(launch_hist_init(c->hist, c->Tp, d.max_sentences, c->stream));
+        NLLB_CKC(launch_hist_init(c->hist_alt, c->Tp, d.max_sentences, c->stream));
         c->n_src_host.assign((size_t)d.n_layers * d.max_sentences, 0);
     }
     NLLB_CKC(cudaMalloc(&c->err, sizeof(int)));
@@ -270,6 +284,7 @@ int nllb_attn_sync(nllb_attn_ctx* c) {
     if (!c) return fail(NLLB_ATTN_EINVAL, "ctx is NULL");
     int rc = set_device(c);
     if (rc) return rc;
+    if ((rc = flush_reorder(c))) return rc;  // the caller's parent buffer is free afterwards
     return finish_host_call(c);
 }
 
@@ -277,6 +292,8 @@ int nllb_attn_reset(nllb_attn_ctx* c) {
     if (!c) return fail(NLLB_ATTN_EINVAL, "ctx is NULL");
     int rc = set_device(c);
     if (rc) return rc;
+    c->pending_parent = nullptr;
+    c->pending_n = 0;
     if (c->d.max_sentences > 0) {
         NLLB_CK(launch_hist_init(c->hist, c->Tp, c->d.max_sentences, c->stream));
         NLLB_CK(cudaMemsetAsync(c->n_src_dev, 0,
@@ -327,6 +344,8 @@ static PrefillParams prefill_params(const nllb_attn_prefill_args* a, int* err) {
     p.msh = a->mask_stride_head;
     p.scale_log2 = a->scale * kLog2e;
     p.row_start = nullptr;
+    p.rows_total = 0;
+    p.map_pos_row = p.map_pos_head = p.map_pos_seq = 0;
     return p;
 }
 
@@ -334,15 +353,17 @@ static PrefillParams prefill_params(const nllb_attn_prefill_args* a, int* err) {
 
 namespace nllb {
 
-int attn_prefill_packed(nllb_attn_ctx* c, const nllb_attn_prefill_args* a, const int* row_start) {
+int attn_prefill_packed(nllb_attn_ctx* c, const nllb_attn_prefill_args* a, const int* row_start, int rows_total) {
     if (!c) return fail(NLLB_ATTN_EINVAL, "ctx is NULL");
     int rc = check_prefill(a);
     if (rc) return rc;
     if (!row_start || !a->valid_len || a->mask)
         return fail(NLLB_ATTN_EINVAL, "packed prefill needs row starts and lengths, and no mask");
     if ((rc = set_device(c))) return rc;
+    if (rows_total < 1) return fail(NLLB_ATTN_EINVAL, "packed prefill needs the buffers' row count");
     PrefillParams p = prefill_params(a, c->err);
     p.row_start = row_start;
+    p.rows_total = rows_total;
     NLLB_CK(launch_prefill(p, c->stream));
     return NLLB_ATTN_OK;
 }
@@ -426,8 +447,12 @@ static int check_beam_call(nllb_attn_ctx* c, int layer, int n_sent) {
 
 // Sentences s0 .. s0 + n_sent - 1; q, k_new, v_new, out point at sentence s0.
 // planes: `out` is the base of the output planes of these n_sent sentences
+// mode reorder: the pending reorder's parents for these sentences are applied
+// on the way and the composed history goes to c->hist_alt (the caller swaps
+// the buffers once every sentence has been launched).
 static int decode_self_dev(nllb_attn_ctx* c, int layer, int step, int s0, int n_sent, const float* q,
-                           const float* k_new, const float* v_new, float* out, bool planes = false) {
+                           const float* k_new, const float* v_new, float* out, bool planes = false,
+                           SelfMode mode = SelfMode::plain) {
     const nllb_attn_dims& d = c->d;
     const size_t layer_floats = (size_t)d.max_sentences * d.n_heads * (size_t)d.max_tgt * d.n_beams * 64;
     const size_t sent_floats = (size_t)d.n_heads * d.max_tgt * d.n_beams * 64;
@@ -437,7 +462,7 @@ static int decode_self_dev(nllb_attn_ctx* c, int layer, int step, int s0, int n_
     p.kc_w = c->kc + (size_t)layer * layer_floats + (size_t)s0 * sent_floats;
     p.vc_w = c->vc + (size_t)layer * layer_floats + (size_t)s0 * sent_floats;
     p.hist = c->hist + (size_t)s0 * c->Tp * 8;
-    p.hist_w = c->hist + (size_t)s0 * c->Tp * 8;
+    p.hist_w = (mode == SelfMode::reorder ? c->hist_alt : c->hist) + (size_t)s0 * c->Tp * 8;
     p.q = q;
     p.k_new = k_new;
     p.v_new = v_new;
@@ -450,8 +475,38 @@ static int decode_self_dev(nllb_attn_ctx* c, int layer, int step, int s0, int n_
                  &p.pos_per_split);
     p.scale_log2 = (1.0f / std::sqrt(64.0f)) * kLog2e;
     p.err = c->err;
-    NLLB_CK(launch_decode_self(p, n_sent, d.n_beams, c->stream, planes));
+    const int* parent = mode == SelfMode::reorder ? c->pending_parent + (size_t)s0 * d.n_beams : nullptr;
+    NLLB_CK(launch_decode_self(p, n_sent, d.n_beams, c->stream, planes, mode, parent));
     return NLLB_ATTN_OK;
+}
+
+// Before a self-attention call over sentences [0, n_sent): the form of its
+// launches.  A pending reorder is applied on the way when it covers exactly
+// the call's sentences and those are all of the context's (the other buffer
+// then holds every sentence's history after the call); otherwise the reorder
+// kernel applies it first.  The bounded-wait test form is taken once.
+static int self_mode(nllb_attn_ctx* c, int n_sent, SelfMode* mode) {
+    *mode = SelfMode::plain;
+    if (c->expire_next_wait) {
+        c->expire_next_wait = false;
+        if (c->d.n_beams != 4) return fail(NLLB_ATTN_EINVAL, "the bounded-wait test takes 4 beams");
+        *mode = SelfMode::expire_wait;
+        return flush_reorder(c);
+    }
+    if (!c->pending_parent) return NLLB_ATTN_OK;
+    if (c->pending_n == n_sent && n_sent == c->d.max_sentences) {
+        *mode = SelfMode::reorder;
+        return NLLB_ATTN_OK;
+    }
+    return flush_reorder(c);
+}
+
+// After the launches of a call made in the reorder form.
+static void self_done(nllb_attn_ctx* c, SelfMode mode) {
+    if (mode != SelfMode::reorder) return;
+    std::swap(c->hist, c->hist_alt);
+    c->pending_parent = nullptr;
+    c->pending_n = 0;
 }
 
 int nllb_attn_decode_self(nllb_attn_ctx* c, int layer, int step, int n_sent, const float* q,
@@ -464,7 +519,11 @@ int nllb_attn_decode_self(nllb_attn_ctx* c, int layer, int step, int n_sent, con
     if (!aligned16(q) || !aligned16(k_new) || !aligned16(v_new) || !aligned16(out))
         return fail(NLLB_ATTN_EINVAL, "q, k_new, v_new, out must be 16-byte aligned");
     if ((rc = set_device(c))) return rc;
-    return decode_self_dev(c, layer, step, 0, n_sent, q, k_new, v_new, out);
+    SelfMode mode;
+    if ((rc = self_mode(c, n_sent, &mode))) return rc;
+    rc = decode_self_dev(c, layer, step, 0, n_sent, q, k_new, v_new, out, false, mode);
+    if (rc == NLLB_ATTN_OK) self_done(c, mode);
+    return rc;
 }
 
 int nllb_attn_decode_self_host(nllb_attn_ctx* c, int layer, int step, int n_sent, const float* q,
@@ -484,6 +543,8 @@ int nllb_attn_decode_self_host(nllb_attn_ctx* c, int layer, int step, int n_sent
     float* dk = static_cast<float*>(c->stg[1]);
     float* dv = static_cast<float*>(c->stg[2]);
     float* dout = static_cast<float*>(c->stg[3]);
+    SelfMode mode;
+    if ((rc = self_mode(c, n_sent, &mode))) return rc;
     // chunks of sentences: the input copy of chunk j + 1 and the output copy of
     // chunk j - 1 run while chunk j's kernel runs (separate copy streams)
     const int C = std::min(nllb_attn_ctx::kHostChunks, n_sent);
@@ -495,17 +556,26 @@ int nllb_attn_decode_self_host(nllb_attn_ctx* c, int layer, int step, int n_sent
         NLLB_CK(cudaMemcpyAsync(dv + off, v_new + off, cb, cudaMemcpyHostToDevice, c->copy_in));
         NLLB_CK(cudaEventRecord(c->ev_in[j], c->copy_in));
         NLLB_CK(cudaStreamWaitEvent(c->stream, c->ev_in[j], 0));
-        if ((rc = decode_self_dev(c, layer, step, s0, s1 - s0, dq + off, dk + off, dv + off, dout + off)))
+        if ((rc = decode_self_dev(c, layer, step, s0, s1 - s0, dq + off, dk + off, dv + off, dout + off, false,
+                                  mode)))
             return rc;
         NLLB_CK(cudaEventRecord(c->ev_k[j], c->stream));
         NLLB_CK(cudaStreamWaitEvent(c->copy_out, c->ev_k[j], 0));
         NLLB_CK(cudaMemcpyAsync(out + off, dout + off, cb, cudaMemcpyDeviceToHost, c->copy_out));
     }
+    self_done(c, mode);
     // the error word after the last kernel, with the outputs
     NLLB_CK(cudaMemcpyAsync(c->err_h, c->err, sizeof(int), cudaMemcpyDeviceToHost, c->copy_out));
     NLLB_CK(cudaStreamSynchronize(c->copy_out));
     if (*c->err_h == 0) return NLLB_ATTN_OK;
     return check_device_error(c);  // reads, reports and clears the word
+}
+
+int nllb_attn_test_expire_next_wait(nllb_attn_ctx* c) {
+    if (!c) return fail(NLLB_ATTN_EINVAL, "ctx is NULL");
+    if (c->d.n_beams != 4) return fail(NLLB_ATTN_EINVAL, "the bounded-wait test takes 4 beams");
+    c->expire_next_wait = true;
+    return NLLB_ATTN_OK;
 }
 
 int nllb_attn_reorder(nllb_attn_ctx* c, int n_sent, const int* parent) {
@@ -516,7 +586,9 @@ int nllb_attn_reorder(nllb_attn_ctx* c, int n_sent, const int* parent) {
     if (!parent) return fail(NLLB_ATTN_EINVAL, "parent is NULL");
     int rc = set_device(c);
     if (rc) return rc;
-    NLLB_CK(launch_reorder(c->hist, c->Tp, parent, n_sent, c->d.n_beams, c->err, c->stream));
+    if ((rc = flush_reorder(c))) return rc;  // two reorders in a row: the first one now
+    c->pending_parent = parent;
+    c->pending_n = n_sent;
     return NLLB_ATTN_OK;
 }
 
@@ -531,8 +603,9 @@ int nllb_attn_reorder_host(nllb_attn_ctx* c, int n_sent, const int* parent) {
             return fail(NLLB_ATTN_EINVAL, "parent index outside [0, n_beams)");
     int rc = set_device(c);
     if (rc) return rc;
+    if ((rc = flush_reorder(c))) return rc;  // it may read the staging buffer refilled below
     const size_t n = (size_t)n_sent * c->d.n_beams;
-    if ((rc = ensure_stage(c, 4, n * sizeof(int)))) return rc;
+    if ((rc = ensure_stage(c, 6, n * sizeof(int)))) return rc;
     if ((rc = ensure_host_pipeline(c))) return rc;
     // The parents (checked above) go through a pinned copy, so the call returns
     // once the reorder is enqueued and the caller's buffer is free at once;
@@ -546,10 +619,10 @@ int nllb_attn_reorder_host(nllb_attn_ctx* c, int n_sent, const int* parent) {
         c->par_h_ints = n;
     }
     std::memcpy(c->par_h, parent, n * sizeof(int));
-    NLLB_CK(cudaMemcpyAsync(c->stg[4], c->par_h, n * sizeof(int), cudaMemcpyHostToDevice, c->stream));
+    NLLB_CK(cudaMemcpyAsync(c->stg[6], c->par_h, n * sizeof(int), cudaMemcpyHostToDevice, c->stream));
     NLLB_CK(cudaEventRecord(c->ev_parent, c->stream));
-    NLLB_CK(launch_reorder(c->hist, c->Tp, static_cast<int*>(c->stg[4]), n_sent, c->d.n_beams, c->err,
-                           c->stream));
+    c->pending_parent = static_cast<int*>(c->stg[6]);
+    c->pending_n = n_sent;
     return NLLB_ATTN_OK;
 }
 
@@ -656,7 +729,11 @@ int attn_decode_self_planes(nllb_attn_ctx* c, int layer, int step, int n_sent, c
     if (step < 0 || step >= c->d.max_tgt) return fail(NLLB_ATTN_EINVAL, "step out of range");
     if (!q || !k_new || !v_new || !planes) return fail(NLLB_ATTN_EINVAL, "q, k_new, v_new, planes are required");
     if ((rc = set_device(c))) return rc;
-    return decode_self_dev(c, layer, step, 0, n_sent, q, k_new, v_new, static_cast<float*>(planes), true);
+    SelfMode mode;
+    if ((rc = self_mode(c, n_sent, &mode))) return rc;
+    rc = decode_self_dev(c, layer, step, 0, n_sent, q, k_new, v_new, static_cast<float*>(planes), true, mode);
+    if (rc == NLLB_ATTN_OK) self_done(c, mode);
+    return rc;
 }
 
 int attn_cross_planes(nllb_attn_ctx* c, int layer, int n_sent, const float* q, void* planes) {

@@ -21,6 +21,8 @@
 //   pays about two DRAM latencies, not one per tile.
 // prefill_ffma_kernel (other lengths): SIMT fp32 flash attention with an
 //   online softmax over 64-key tiles.
+#include <algorithm>
+
 #include "device_common.cuh"
 #include "kernels.h"
 
@@ -192,19 +194,23 @@ __global__ void __launch_bounds__(kThreads) prefill_ffma_kernel(const PrefillPar
 // ---------------------------------------------------------------------------
 // tcgen05 kernel
 // ---------------------------------------------------------------------------
+constexpr int TC_THREADS = 256;  // two threads per query row / TMEM lane
+constexpr int TC_THREADS_SPLIT = TC_THREADS;
 constexpr int TC_Q = 128;      // queries per CTA (MMA M)
 constexpr int TC_KG = 128;     // keys per score group (MMA N of Q.K^T)
 constexpr int TC_K = 64;       // keys per P.V chunk (MMA K of P.V)
 constexpr int TC_MAX_S = 256;  // score columns held in TMEM
 constexpr uint32_t TC_TMEM_COLS = 512;
 // shared-memory plan (bytes from a 1024-byte aligned base); every operand is
-// K-major, 128-byte swizzled, in 32-column k-blocks of rows*128 bytes
-constexpr uint32_t SQH = 0, SQL = 32768;        // Q hi/lo   [2][128 rows][128 B]
-constexpr uint32_t SKH = 65536, SKL = 98304;    // K hi/lo   [2][128 keys][128 B]
+// K-major, 128-byte swizzled, in 32-column k-blocks of rows*128 bytes -- the
+// layout a TMA box of [rows][32 fp32] lands in with the 128-byte swizzle
+constexpr uint32_t SQH = 0, SQL = 32768;        // Q hi/lo [2][128 rows][128 B]; P hi/lo after the scores
+constexpr uint32_t SKH = 65536, SKL = 98304;    // K hi/lo [2][128 keys][128 B]
 constexpr uint32_t SVH = 131072, SVL = 147456;  // V^T hi/lo [2][64 dims][128 B]
-constexpr uint32_t SPH = 163840, SPL = 196608;  // P hi/lo   [2][128 rows][128 B]
-constexpr uint32_t SBAR = 229376;
+constexpr uint32_t SVR = 163840;                // V as loaded: [2][128 keys][128 B] (two P.V chunks)
+constexpr uint32_t SBAR = 196608;
 constexpr uint32_t TC_SMEM = SBAR + 64 + 1024;  // + alignment slack
+constexpr uint32_t TC_BOX_BYTES = 128 * 128;    // one [128 rows][32 fp32] box
 
 // byte offset of (row, col) in a K-major SWIZZLE_128B operand of `nrows`
 // rows x 64 fp32 columns: 32-column k-blocks of nrows*128 B, 128-B rows,
@@ -212,14 +218,6 @@ constexpr uint32_t TC_SMEM = SBAR + 64 + 1024;  // + alignment slack
 __device__ __forceinline__ uint32_t sw128_off(int row, int col, int nrows) {
     return (uint32_t)((col >> 5) * nrows * 128 + row * 128 + ((((col & 31) >> 2) ^ (row & 7)) << 4) +
                       ((col & 3) << 2));
-}
-
-__device__ __forceinline__ void split_store4(unsigned char* hi_base, unsigned char* lo_base, uint32_t off,
-                                             float4 x) {
-    float4 h = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
-    float4 l = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
-    *reinterpret_cast<float4*>(hi_base + off) = h;
-    *reinterpret_cast<float4*>(lo_base + off) = l;
 }
 
 // D[128 x N] (+)= A[128 x 64] . B[N x 64]^T with both operands split:
@@ -240,11 +238,49 @@ __device__ __forceinline__ void mma_3xtf32(uint32_t d, uint32_t ah, uint32_t al,
     }
 }
 
-__device__ __forceinline__ float4 ldg_row4(const float* base, long long row_off, int c4, bool valid) {
-    return valid ? __ldg(reinterpret_cast<const float4*>(base + row_off) + c4) : make_float4(0.f, 0.f, 0.f, 0.f);
+// TMA: a box of the 4-D fp32 tensor map (d, then the row/head/sequence axes
+// in the order of their strides) into shared memory, completing on `bar`.
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+        "[%6];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+        : "memory");
 }
 
-constexpr int TC_THREADS = 256;  // two threads per query row / TMEM lane
+__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// The two 32-column boxes of rows [r0, r0 + 128) of (sequence b, head h):
+// coordinates (column, then the three outer axes in map order).
+__device__ __forceinline__ void tma_rows128(uint32_t dst, const CUtensorMap* map, const PrefillParams& p, int r0,
+                                            int h, int b, uint64_t* bar) {
+    auto at = [&](int i) { return p.map_pos_row == i ? r0 : (p.map_pos_head == i ? h : b); };
+    const int c0 = at(0), c1 = at(1), c2 = at(2);
+    tma_load_4d(dst, map, 0, c0, c1, c2, bar);
+    tma_load_4d(dst + TC_BOX_BYTES, map, 32, c0, c1, c2, bar);
+}
+
+// In place over `bytes` of loaded fp32 at hi: hi = x with the low 13 mantissa
+// bits cleared (exact in tf32), lo (same offset at lo) = x - hi.
+__device__ __forceinline__ void split_in_place(unsigned char* hi, unsigned char* lo, uint32_t bytes, int tid) {
+    for (uint32_t off = (uint32_t)tid * 16; off < bytes; off += TC_THREADS_SPLIT * 16) {
+        const float4 x = *reinterpret_cast<const float4*>(hi + off);
+        const float4 h = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
+        *reinterpret_cast<float4*>(hi + off) = h;
+        *reinterpret_cast<float4*>(lo + off) = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
+    }
+}
+
+__device__ __forceinline__ void split_store4(unsigned char* hi_base, unsigned char* lo_base, uint32_t off,
+                                             float4 x) {
+    float4 h = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
+    float4 l = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
+    *reinterpret_cast<float4*>(hi_base + off) = h;
+    *reinterpret_cast<float4*>(lo_base + off) = l;
+}
 
 __device__ __forceinline__ float ex2_approx(float x) {  // 2^x, -inf -> +0
     float y;
@@ -252,14 +288,24 @@ __device__ __forceinline__ float ex2_approx(float x) {  // 2^x, -inf -> +0
     return y;
 }
 
-__global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const PrefillParams p) {
+// One CTA per (128-query tile, head, sequence), 8 warps.  Q, K and V tiles
+// arrive by TMA (one thread issues the boxes after the wait on the previous
+// kernel; V for the first 128 keys travels while the scores are computed)
+// in the 128-byte-swizzled K-major layout the MMAs read; the threads then
+// split Q and K in place (hi, lo) and transpose-split V chunk by chunk.
+__global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const PrefillParams p,
+                                                                   const __grid_constant__ CUtensorMap map_q,
+                                                                   const __grid_constant__ CUtensorMap map_k,
+                                                                   const __grid_constant__ CUtensorMap map_v) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
     const uint32_t base_addr = (raw_addr + 1023u) & ~1023u;
     unsigned char* base = smem_raw + (base_addr - raw_addr);
     uint64_t* mma_bar = reinterpret_cast<uint64_t*>(base + SBAR);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + SBAR + 8);
-    volatile int* s_abort = reinterpret_cast<volatile int*>(base + SBAR + 16);
+    uint64_t* qk_bar = reinterpret_cast<uint64_t*>(base + SBAR + 8);  // Q and K group loads
+    uint64_t* v_bar = reinterpret_cast<uint64_t*>(base + SBAR + 16);  // V loads
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + SBAR + 24);
+    volatile int* s_abort = reinterpret_cast<volatile int*>(base + SBAR + 32);
     __shared__ float s_red[TC_THREADS];
 
     pdl_launch_dependents();
@@ -273,8 +319,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
     if (warp == 0) tmem_alloc(tmem_slot, TC_TMEM_COLS);
     if (tid == 0) {
         mbar_init(mma_bar, 1);
+        mbar_init(qk_bar, 1);
+        mbar_init(v_bar, 1);
         fence_barrier_init();
         *s_abort = 0;
+        prefetch_map(&map_q);
+        prefetch_map(&map_k);
+        prefetch_map(&map_v);
     }
     tc_fence_before();
     __syncthreads();
@@ -286,8 +337,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
 
     pdl_wait_primary();  // q, k, v, lengths, row starts and mask come from earlier kernels
 
-    const long long hbase = (p.row_start ? (long long)__ldg(p.row_start + b) * p.sr : (long long)b * p.sb) +
-                            (long long)h * p.sh;
+    // row coordinate of the sequence's row 0 in the tensor maps (packed rows:
+    // its first row in the buffer; the sequence axis is then unused)
+    const int row0 = p.row_start ? __ldg(p.row_start + b) : 0;
+    const int bq = p.row_start ? 0 : b;
+    const long long hbase = (p.row_start ? (long long)row0 * p.sr : (long long)b * p.sb) + (long long)h * p.sh;
     int kv_len = S;
     bool uniform = false;  // valid_len 0: equal weights over all keys (see prefill_ffma_kernel)
     if (p.valid_len) {
@@ -315,10 +369,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
                             : nullptr;
     const float sl2 = p.scale_log2;
 
-    uint32_t phase = 0;
-    auto wait_mma = [&]() -> bool {
-        if (!mbar_wait_bounded(mma_bar, phase & 1u)) *s_abort = 1;
-        ++phase;
+    // Q, K group 0 and V keys 0..127: every box issued at once.  A box counts
+    // its full bytes toward the barrier, rows outside the tensor included
+    // (they arrive as zeros).
+    if (tid == 0) {
+        mbar_arrive_expect_tx(qk_bar, 4 * TC_BOX_BYTES);
+        tma_rows128(base_addr + SQH, &map_q, p, row0 + q0, h, bq, qk_bar);
+        tma_rows128(base_addr + SKH, &map_k, p, row0, h, bq, qk_bar);
+        mbar_arrive_expect_tx(v_bar, 2 * TC_BOX_BYTES);
+        tma_rows128(base_addr + SVR, &map_v, p, row0, h, bq, v_bar);
+    }
+
+    uint32_t phase = 0, qk_phase = 0, v_phase = 0;         // waits completed per barrier
+    uint32_t mma_issued = 0, qk_issued = 1, v_issued = 1;  // (thread 0) phases armed per barrier
+    auto wait_bar = [&](uint64_t* bar, uint32_t& ph) -> bool {
+        if (!mbar_wait_bounded(bar, ph & 1u)) *s_abort = 1;
+        ++ph;
         __syncthreads();
         return *s_abort == 0;
     };
@@ -337,46 +403,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
             for (int i = 0; i < 32; ++i) v[i] = (j0 + i < kv_len) ? v[i] * sl2 : -INFINITY;
         }
     };
-    // K group g: 128 keys x 16 float4 = 8 float4 per thread
-    auto load_k_group = [&](int g, float4* kr) {
-#pragma unroll
-        for (int it = 0; it < 8; ++it) {
-            const int r = (it * TC_THREADS + tid) >> 4, key = g * TC_KG + r;
-            kr[it] = ldg_row4(p.k, hbase + (long long)key * p.sr, tid & 15, key < kv_len);
-        }
-    };
-    // V chunk c: 64 keys x 16 float4 = 4 float4 per thread; a warp covers 32 keys of one float4 column
-    auto load_v_chunk = [&](int c, float4* vr) {
-#pragma unroll
-        for (int it = 0; it < 4; ++it) {
-            const int idx = it * TC_THREADS + tid;
-            const int jj = (idx & 31) + 32 * (idx >> 9), c4 = (idx >> 5) & 15, key = c * TC_K + jj;
-            vr[it] = ldg_row4(p.v, hbase + (long long)key * p.sr, c4, key < kv_len);
-        }
-    };
 
-    // every load of Q and of the first K group is issued before any is stored
-    float4 qr[8], kr[8];
-#pragma unroll
-    for (int it = 0; it < 8; ++it) {
-        const int r = (it * TC_THREADS + tid) >> 4;
-        qr[it] = ldg_row4(p.q, hbase + (long long)(q0 + r) * p.sr, tid & 15, q0 + r < q_lim);
-    }
-    load_k_group(0, kr);
-#pragma unroll
-    for (int it = 0; it < 8; ++it)
-        split_store4(base + SQH, base + SQL, sw128_off((it * TC_THREADS + tid) >> 4, (tid & 15) * 4, TC_Q), qr[it]);
-
-    bool ok = true;
+    bool ok = wait_bar(qk_bar, qk_phase);  // Q and K group 0 have landed
+    if (ok) split_in_place(base + SQH, base + SQL, 2 * TC_BOX_BYTES, tid);
     for (int g = 0; g < n_kg && ok; ++g) {
         if (g > 0) {
-            if (!(ok = wait_mma())) break;  // group g-1 has read KH/KL
-            load_k_group(g, kr);
+            if (!(ok = wait_bar(mma_bar, phase))) break;  // group g-1's MMAs have read KH/KL
+            if (tid == 0) {
+                mbar_arrive_expect_tx(qk_bar, 2 * TC_BOX_BYTES);
+                tma_rows128(base_addr + SKH, &map_k, p, row0 + g * TC_KG, h, bq, qk_bar);
+                ++qk_issued;
+            }
+            if (!(ok = wait_bar(qk_bar, qk_phase))) break;
         }
-#pragma unroll
-        for (int it = 0; it < 8; ++it)
-            split_store4(base + SKH, base + SKL, sw128_off((it * TC_THREADS + tid) >> 4, (tid & 15) * 4, TC_KG),
-                         kr[it]);
+        split_in_place(base + SKH, base + SKL, 2 * TC_BOX_BYTES, tid);
         fence_async_smem();
         tc_fence_before();
         __syncthreads();
@@ -385,13 +425,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
             mma_3xtf32<TC_KG>(tmem + (uint32_t)(g * TC_KG), base_addr + SQH, base_addr + SQL, base_addr + SKH,
                               base_addr + SKL, false);
             tc_commit(mma_bar);
+            ++mma_issued;
         }
     }
-    // the first two V chunks travel while the score MMAs run
-    float4 vr0[4], vr1[4];
-    load_v_chunk(0, vr0);
-    if (n_kc > 1) load_v_chunk(1, vr1);
-    if (ok) ok = wait_mma();
+    if (ok) ok = wait_bar(mma_bar, phase);  // scores in TMEM; Q's buffers are free (P goes there)
     tc_fence_after();
 
     // pass 1: row max (this thread: columns half*32 + 64c .. +31 of every chunk)
@@ -411,7 +448,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
     // pass 2: P chunk by chunk, O += P . V_chunk
     float sum = 0.f;
     for (int kc = 0; kc < n_kc && ok; ++kc) {
-        if (kc > 0 && !(ok = wait_mma())) break;  // previous chunk's MMAs have read P and V^T
+        if (kc > 0 && !(ok = wait_bar(mma_bar, phase))) break;  // previous chunk's MMAs have read P and V^T
+        if ((kc & 1) == 0) {  // V keys 128*(kc/2) .. +127 have landed in SVR
+            if (kc > 0 && tid == 0) {
+                mbar_arrive_expect_tx(v_bar, 2 * TC_BOX_BYTES);
+                tma_rows128(base_addr + SVR, &map_v, p, row0 + kc * TC_K, h, bq, v_bar);
+                ++v_issued;
+            }
+            if (!(ok = wait_bar(v_bar, v_phase))) break;
+        }
         {
             float v[32];
             scores32(kc * TC_K + half * 32, v);
@@ -423,41 +468,43 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
                     e[i] = ex2_approx(v[c4 * 4 + i] - mx);
                     sum += e[i];
                 }
-                split_store4(base + SPH, base + SPL, sw128_off(rloc, half * 32 + c4 * 4, TC_Q),
+                split_store4(base + SQH, base + SQL, sw128_off(rloc, half * 32 + c4 * 4, TC_Q),
                              make_float4(e[0], e[1], e[2], e[3]));
             }
         }
-        // V chunk kc (in vr0 for even kc, vr1 for odd), transposed: row = head dim, column = key
-        float4* vr = (kc & 1) ? vr1 : vr0;
+        // V chunk kc, transposed (row = head dim, column = key) and split;
+        // keys past the sequence's length as zeros
 #pragma unroll
         for (int it = 0; it < 4; ++it) {
-            const int idx = it * TC_THREADS + tid;
-            const int jj = (idx & 31) + 32 * (idx >> 9), c4 = (idx >> 5) & 15;
-            const float xs[4] = {vr[it].x, vr[it].y, vr[it].z, vr[it].w};
+            const int jj = tid & 63, d4 = (tid >> 6) + 4 * it;  // key within the chunk, head-dim quad
+            const int jr = (kc & 1) * TC_K + jj;                 // key row within SVR
+            float4 x = *reinterpret_cast<const float4*>(base + SVR + sw128_off(jr, d4 * 4, 128));
+            if (kc * TC_K + jj >= kv_len) x = make_float4(0.f, 0.f, 0.f, 0.f);
+            const float xs[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const uint32_t off = sw128_off(c4 * 4 + i, jj, 64);
+                const uint32_t off = sw128_off(d4 * 4 + i, jj, 64);
                 const float hv = tf32_hi(xs[i]);
                 *reinterpret_cast<float*>(base + SVH + off) = hv;
                 *reinterpret_cast<float*>(base + SVL + off) = xs[i] - hv;
             }
         }
-        if (kc + 2 < n_kc) load_v_chunk(kc + 2, vr);  // two chunks ahead
         fence_async_smem();
         tc_fence_before();
-        __syncthreads();
+        __syncthreads();  // also: every thread is done reading SVR for this chunk
         if (tid == 0) {
             tc_fence_after();
-            mma_3xtf32<TC_K>(tmem + TC_MAX_S, base_addr + SPH, base_addr + SPL, base_addr + SVH, base_addr + SVL,
+            mma_3xtf32<TC_K>(tmem + TC_MAX_S, base_addr + SQH, base_addr + SQL, base_addr + SVH, base_addr + SVL,
                              kc > 0);
             tc_commit(mma_bar);
+            ++mma_issued;
         }
     }
-    if (ok) ok = wait_mma();
+    if (ok) ok = wait_bar(mma_bar, phase);
     tc_fence_after();
 
     if (ok) {
-        s_red[tid] = sum;  // wait_mma ended with a barrier, pass-1 values are consumed
+        s_red[tid] = sum;  // wait_bar ended with a barrier, pass-1 values are consumed
         __syncthreads();
         sum += s_red[tid ^ 128];
         float o[32];
@@ -471,7 +518,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
         }
     } else if (tid == 0) {
         atomicOr(p.err, NLLB_DEV_ERR_TIMEOUT);
-        (void)mbar_wait_bounded(mma_bar, phase & 1u);  // last chance for MMAs in flight
+        // let what is still in flight land (MMAs, TMA boxes): each barrier's
+        // armed phases not waited for yet, oldest first
+        for (; phase < mma_issued; ++phase) (void)mbar_wait_bounded(mma_bar, phase & 1u);
+        for (; qk_phase < qk_issued; ++qk_phase) (void)mbar_wait_bounded(qk_bar, qk_phase & 1u);
+        for (; v_phase < v_issued; ++v_phase) (void)mbar_wait_bounded(v_bar, v_phase & 1u);
     }
     tc_fence_before();
     __syncthreads();
@@ -482,6 +533,43 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
 }
 
 }  // namespace
+
+// The fp32 tensor map of q, k or v for the tensor-core kernel: 4-D, column
+// (64, contiguous) first, then the row, head and sequence axes in the order
+// of their strides, box [32 columns][128 rows], 128-byte swizzle.  Rows
+// outside the tensor read as zeros.  False where the layout does not fit a
+// tensor map (overlapping or zero strides): the SIMT kernel runs instead.
+bool prefill_map(const PrefillParams& p, const float* base, CUtensorMap* map, int pos[3]) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (!enc) return false;
+    struct Axis {
+        long long stride, extent;
+        int which;  // 0 row, 1 head, 2 sequence
+    } ax[3] = {{p.sr, p.row_start ? (long long)p.rows_total : (long long)p.S, 0},
+               {p.sh, p.H, 1},
+               {p.sb, p.row_start ? 1LL : (long long)p.B, 2}};
+    // axes of extent 1 go last, with a stride that keeps the strides ordered
+    std::sort(ax, ax + 3, [](const Axis& x, const Axis& y) {
+        if ((x.extent == 1) != (y.extent == 1)) return y.extent == 1;
+        return x.stride < y.stride;
+    });
+    long long span = 64;  // elements covered by the axes so far
+    cuuint64_t dims[4] = {64, 1, 1, 1}, strides[3];
+    cuuint32_t box[4] = {32, 1, 1, 1}, estr[4] = {1, 1, 1, 1};
+    for (int i = 0; i < 3; ++i) {
+        long long st = ax[i].stride;
+        if (ax[i].extent == 1) st = std::max(st, span);
+        if (ax[i].extent < 1 || st < span || st % 4) return false;
+        dims[i + 1] = (cuuint64_t)ax[i].extent;
+        strides[i] = (cuuint64_t)st * 4;
+        span = st * ax[i].extent;
+        pos[ax[i].which] = i;
+        if (ax[i].which == 0) box[i + 1] = 128;
+    }
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 cudaError_t configure_prefill_kernels() {
     const int smem = 4 * BQ * LDS * (int)sizeof(float);
@@ -502,10 +590,18 @@ cudaError_t launch_prefill(const PrefillParams& p, cudaStream_t st) {
     cfg.stream = st;
     cfg.blockDim = dim3(128, 1, 1);
     if (prefill_uses_tensor_cores(p.S)) {
-        cfg.blockDim = dim3(TC_THREADS, 1, 1);
-        cfg.gridDim = dim3((p.S + TC_Q - 1) / TC_Q, p.H, p.B);
-        cfg.dynamicSmemBytes = TC_SMEM;
-        return cudaLaunchKernelEx(&cfg, prefill_tc_kernel, p);
+        PrefillParams q = p;
+        CUtensorMap mq, mk, mv;
+        int pos[3], pos_k[3], pos_v[3];
+        if (prefill_map(p, p.q, &mq, pos) && prefill_map(p, p.k, &mk, pos_k) && prefill_map(p, p.v, &mv, pos_v)) {
+            q.map_pos_row = pos[0] + 0;
+            q.map_pos_head = pos[1];
+            q.map_pos_seq = pos[2];
+            cfg.blockDim = dim3(TC_THREADS, 1, 1);
+            cfg.gridDim = dim3((p.S + TC_Q - 1) / TC_Q, p.H, p.B);
+            cfg.dynamicSmemBytes = TC_SMEM;
+            return cudaLaunchKernelEx(&cfg, prefill_tc_kernel, q, mq, mk, mv);
+        }
     }
     cfg.gridDim = dim3((p.S + BQ - 1) / BQ, p.H, p.B);
     cfg.dynamicSmemBytes = 4 * BQ * LDS * sizeof(float);

@@ -73,6 +73,7 @@ SIGNATURES = {
     "nllb_attn_decode_self_host": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _fp, _fp, _fp, _fp]),
     "nllb_attn_reorder": (_c_int, [_c_void_p, _c_int, _fp]),
     "nllb_attn_reorder_host": (_c_int, [_c_void_p, _c_int, _fp]),
+    "nllb_attn_test_expire_next_wait": (_c_int, [_c_void_p]),
     "nllb_attn_set_memory": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _fp, _fp,
                                       ctypes.c_int64, ctypes.c_int64]),
     "nllb_attn_set_memory_host": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _fp, _fp,
@@ -224,7 +225,14 @@ class Context:
             "decode_self_host")
 
     def reorder(self, n_sent, parent) -> None:
+        """nllb_attn_reorder: `parent` (a device tensor) must stay unchanged
+        until the next decode_self, reorder, sync or reset on this context."""
         _check(self.lib, self.lib.nllb_attn_reorder(self.handle, n_sent, ptr(parent)), "reorder")
+
+    def test_expire_next_wait(self) -> None:
+        """nllb_attn_test_expire_next_wait: the next self-attention launch's
+        bounded wait runs out (a chunk that is never requested)."""
+        _check(self.lib, self.lib.nllb_attn_test_expire_next_wait(self.handle), "test_expire_next_wait")
 
     def reorder_host(self, n_sent, parent) -> None:
         _check(self.lib, self.lib.nllb_attn_reorder_host(self.handle, n_sent, ptr(parent)),

@@ -18,12 +18,23 @@ def decode_steps(n_src: int, max_gen: int) -> int:
     return min(3 * n_src + 10, max_gen - 4)
 
 
-def sentence_cost(n_src: int, max_gen: int) -> int:
-    """Relative GPU work of one sentence: encoder rows plus decode steps, each
-    step touching the encoder memory once (cross-attention) and the growing
-    cache (self-attention)."""
+BEAMS = 4
+# Costs in units of one decoder row-step: one beam row through the 12 decoder
+# layers' linear layers (14M weights each) and the tied vocabulary projection
+# (262M), 424M multiply-adds, which the GEMMs stream for every step.
+ENCODER_ROW = 0.34       # an encoder row: 12 layers of 12M weights = 144M multiply-adds
+SELF_PER_POSITION = 7e-4  # 4 beams x 16 heads x 512 B of cache per position, at HBM speed
+CROSS_PER_ROW = 1.8e-4    # 16 heads x 512 B of memory per source row, read once for all beams
+
+
+def sentence_cost(n_src: int, max_gen: int) -> float:
+    """Relative GPU work of one sentence in decoder row-steps: its encoder
+    rows, then per decode step its beams' rows through the weights (the
+    dominant term) plus the attention reads of that step (the cache so far
+    and the encoder memory)."""
     steps = decode_steps(n_src, max_gen)
-    return n_src * n_src + steps * (n_src + steps)
+    attention = steps * (SELF_PER_POSITION * (steps + 1) / 2 + CROSS_PER_ROW * n_src)
+    return ENCODER_ROW * n_src + BEAMS * steps + attention
 
 
 def plan_shards(src_lengths: Sequence[int], world: int, max_gen: int = 132) -> List[List[int]]:
@@ -45,7 +56,7 @@ def plan_shards(src_lengths: Sequence[int], world: int, max_gen: int = 132) -> L
     return [sorted(s) for s in shards]
 
 
-def shard_loads(src_lengths: Sequence[int], shards: Sequence[Sequence[int]], max_gen: int = 132) -> List[int]:
+def shard_loads(src_lengths: Sequence[int], shards: Sequence[Sequence[int]], max_gen: int = 132) -> List[float]:
     return [sum(sentence_cost(int(src_lengths[i]), max_gen) for i in s) for s in shards]
 
 

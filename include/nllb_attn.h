@@ -149,11 +149,26 @@ NLLB_ATTN_API int nllb_attn_decode_self_host(nllb_attn_ctx* ctx, int layer, int 
  * continues the history of old beam parent[s*n_beams + b], for every layer.
  * Applies to positions already written; costs O(n_sentences*max_tgt) bytes,
  * independent of the cache size.  parent: [n_sentences][n_beams] int32.
- * nllb_attn_reorder_host checks the parents on the host and returns once the
- * reorder is enqueued (the caller may reuse its buffer at once); later calls
- * on the context run after it. */
+ * The reorder takes effect for every later call on the context.  It is
+ * applied lazily: when the next nllb_attn_decode_self covers exactly these
+ * n_sentences and they are all of the context's max_sentences, that launch
+ * reads each beam's rows through its parent and writes the composed history
+ * itself (one launch per step instead of two); otherwise a reorder kernel
+ * runs first.  So nllb_attn_reorder's device buffer `parent` must stay valid
+ * and unchanged until the next nllb_attn_decode_self, nllb_attn_reorder,
+ * nllb_attn_sync or nllb_attn_reset call on the context.
+ * nllb_attn_reorder_host checks the parents on the host and returns once
+ * they are copied (the caller may reuse its buffer at once). */
 NLLB_ATTN_API int nllb_attn_reorder(nllb_attn_ctx* ctx, int n_sentences, const int* parent);
 NLLB_ATTN_API int nllb_attn_reorder_host(nllb_attn_ctx* ctx, int n_sentences, const int* parent);
+
+/* Test of the bounded device waits: the next self-attention launch on this
+ * context (nllb_attn_decode_self or _host, 4 beams) waits for a cache chunk
+ * that it never requests, with a budget of about 1 ms, so that the wait runs
+ * out.  That launch writes no output and sets the device error word, which
+ * the call (_host) or the next nllb_attn_sync reports as NLLB_ATTN_ETIMEOUT;
+ * the context stays usable.  No counterpart in the reference. */
+NLLB_ATTN_API int nllb_attn_test_expire_next_wait(nllb_attn_ctx* ctx);
 
 /* ---- cross-attention over the shared encoder memory ---------------------
  * Stores one sentence's projected encoder keys/values for one layer

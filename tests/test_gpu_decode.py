@@ -120,7 +120,8 @@ def test_decode_errors(cuda_device):
             ctx.reorder_host(1, np.array([0, 1, 4, 0], np.int32))
         assert ei.value.status == na.EINVAL
         # an out-of-range parent that only the device sees: flagged, not applied
-        ctx.reorder(1, torch.tensor([0, 1, 9, 0], dtype=torch.int32, device="cuda"))
+        bad = torch.tensor([0, 1, 9, 0], dtype=torch.int32, device="cuda")
+        ctx.reorder(1, bad)
         with pytest.raises(na.NllbAttnError) as ei:
             ctx.sync()
         assert ei.value.status == na.EINVAL
@@ -128,6 +129,70 @@ def test_decode_errors(cuda_device):
         with pytest.raises(na.NllbAttnError) as ei:
             ctx.cross(0, 1, x, x)
         assert ei.value.status == na.ESTATE
+
+
+def test_reorder_applied_in_the_decode_launch(cuda_device):
+    """With every sentence of the context in the call, a pending reorder is
+    applied by the self-attention launch itself (no reorder kernel); with a
+    spare sentence slot the reorder kernel runs first.  Both must give the
+    same results, bit for bit, and the oracle's."""
+    rng = np.random.default_rng(77)
+    T, NB, S = 60, 4, 3
+    q, k, v = (rng.standard_normal((T, S, NB, 1024), dtype=np.float32) for _ in range(3))
+    parents = rng.integers(0, NB, size=(T, S, NB)).astype(np.int32)
+    outs = []
+    for max_sent in (S, S + 1):
+        with na.Context(0, n_layers=1, max_sentences=max_sent, n_beams=NB, max_tgt=T, max_src=1) as ctx:
+            outs.append(gpu_decode_sweep(ctx, q, k, v, parents, n_sent=S))
+    assert np.array_equal(outs[0], outs[1])
+    for s in range(S):
+        assert_attn_close(outs[0][:, s], po.decode_sweep(q[:, s], k[:, s], v[:, s], parents[:, s]), f"sentence {s}")
+
+
+def test_bad_parent_seen_by_the_decode_launch(cuda_device):
+    """An out-of-range parent applied inside the self-attention launch is
+    flagged like the reorder kernel flags it."""
+    import torch
+    with na.Context(0, n_layers=1, max_sentences=1, n_beams=4, max_tgt=8, max_src=4) as ctx:
+        x = torch.zeros(1, 4, 1024, device="cuda")
+        ctx.decode_self(0, 0, 1, x, x, x, x)
+        bad = torch.tensor([0, 5, 1, 2], dtype=torch.int32, device="cuda")
+        ctx.reorder(1, bad)
+        ctx.decode_self(0, 1, 1, x, x, x, x)
+        with pytest.raises(na.NllbAttnError) as ei:
+            ctx.sync()
+        assert ei.value.status == na.EINVAL
+
+
+@pytest.mark.parametrize("n_sent", [1, 40])
+def test_bounded_wait_runs_out_and_context_recovers(cuda_device, n_sent):
+    """The self-attention launch's wait for a cache chunk runs out (a chunk
+    that is never requested, ~1 ms budget): the call reports
+    NLLB_ATTN_ETIMEOUT, and the same step made again on the same context gives
+    the oracle's outputs, as do the steps after it.  1 sentence splits the
+    cache over a cluster of CTAs; 40 sentences do not split."""
+    import torch
+    rng = np.random.default_rng(91 + n_sent)
+    T, NB, t_out = 24, 4, 17
+    q, k, v = (rng.standard_normal((T, n_sent, NB, 1024), dtype=np.float32) for _ in range(3))
+    parents = rng.integers(0, NB, size=(T, n_sent, NB)).astype(np.int32)
+    with na.Context(0, n_layers=1, max_sentences=n_sent, n_beams=NB, max_tgt=T, max_src=1) as ctx:
+        dq, dk, dv = (torch.from_numpy(a).cuda() for a in (q, k, v))
+        dout = torch.zeros_like(dq)
+        dpar = torch.from_numpy(parents).cuda()
+        for t in range(T):
+            ctx.reorder(n_sent, dpar[t])
+            if t == t_out:
+                ctx.test_expire_next_wait()
+                ctx.decode_self(0, t, n_sent, dq[t], dk[t], dv[t], dout[t])
+                with pytest.raises(na.NllbAttnError) as ei:
+                    ctx.sync()
+                assert ei.value.status == na.ETIMEOUT
+            ctx.decode_self(0, t, n_sent, dq[t], dk[t], dv[t], dout[t])
+        ctx.sync()
+        out = dout.cpu().numpy()
+    for s in range(0, n_sent, max(1, n_sent // 4)):
+        assert_attn_close(out[:, s], po.decode_sweep(q[:, s], k[:, s], v[:, s], parents[:, s]), f"sentence {s}")
 
 
 # ---------------------------------------------------------------------------
