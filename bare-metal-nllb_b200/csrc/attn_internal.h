@@ -53,7 +53,7 @@ struct nllb_attn_ctx {
 
 namespace nllb {
 // The engine's forms of nllb_attn_decode_self / nllb_attn_cross (device
-// buffers): the output goes out as the three bf16 planes of the output
+// buffers): the output goes out as the two fp16 planes of the output
 // projection's input (planes.cuh) at the fp32 output's element offsets, one
 // plane per n_sent * n_beams * H * 64 elements.  Not exported.
 int attn_decode_self_planes(nllb_attn_ctx* c, int layer, int step, int n_sent, const float* q, const float* k_new,

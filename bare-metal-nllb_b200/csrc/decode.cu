@@ -44,7 +44,7 @@ constexpr int kBarBytes = 128;  // mbarriers at the start of dynamic shared memo
 // every CTA of the cluster calls this (the barriers are cluster-wide), so
 // no CTA leaves while its records may still be read.
 // Where a CTA's output rows go: fp32 rows, or (PLANES) the same element
-// offsets in three bf16 planes.  A template parameter, so that the fp32 form
+// offsets in the two fp16 planes.  A template parameter, so that the fp32 form
 // compiles exactly as a kernel without the option.
 template <bool PLANES>
 struct OutRows;
@@ -58,18 +58,18 @@ struct OutRows<false> {
 };
 template <>
 struct OutRows<true> {
-    __nv_bfloat16* planes;  // the same offset in plane 0
+    plane_t* planes;  // the same offset in plane 0
     size_t row_stride, plane_stride;
     __device__ __forceinline__ void put(int bb, int q4, float4 v) const {
-        store_split3_x4(planes, plane_stride, (size_t)bb * row_stride + 4 * q4, v);
+        store_planes_x4(planes, plane_stride, (size_t)bb * row_stride + 4 * q4, v);
     }
 };
-// PLANES: p.out is the base of three bf16 planes covering the launch's rows
+// PLANES: p.out is the base of the fp16 planes covering the launch's rows
 // (gridDim.z sentences x NB beams x H heads x 64), one plane after the other.
 template <bool PLANES, int NB, typename Params>
 __device__ __forceinline__ OutRows<PLANES> out_rows(const Params& p, size_t off) {
     if constexpr (PLANES)
-        return OutRows<true>{reinterpret_cast<__nv_bfloat16*>(p.out) + off, (size_t)p.H * 64,
+        return OutRows<true>{reinterpret_cast<plane_t*>(p.out) + off, (size_t)p.H * 64,
                              (size_t)gridDim.z * NB * p.H * 64};
     else
         return OutRows<false>{p.out + off, (size_t)p.H * 64};

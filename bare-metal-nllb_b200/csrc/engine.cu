@@ -20,10 +20,11 @@
 #include <string>
 #include <vector>
 
-#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "attn_internal.h"
 #include "engine_kernels.h"
+#include "planes.cuh"
 #include "nllb_translate.h"
 
 using namespace nllb;
@@ -193,7 +194,7 @@ struct Lin {
     float* scale = nullptr;  // CT2 weight_scale (weight = int8 / scale)
     float* b = nullptr;
     int out = 0, in = 0;
-    void* wb = nullptr;  // bf16 copy of w (exact), operand of the TMA-fed tensor-core kernel
+    void* wb = nullptr;  // fp16 copy of w (exact), operand of the TMA-fed tensor-core kernel
     CUtensorMap tm{};    // tensor map of wb: [out][in], box 64 x 128, 128-byte swizzle
     CUtensorMap tm256{}; // the same, box 32 x 256, 64-byte swizzle (persistent kernel)
 };
@@ -222,7 +223,7 @@ struct nllb_model {
     nllb_attn_ctx* attn = nullptr;
     LinearWorkspace lws;  // split-K workspace of the tensor-core linear kernel
     Lin vocab;            // tied output projection: the shared embedding (decoder.c:319-354)
-    // activations split into bf16 planes for the TMA-fed linear kernel ([3][M][K]),
+    // activations split into fp16 planes for the TMA-fed linear kernel ([2][M][K]),
     // grow-only, with its tensor maps per (M, K)
     // (two buffers: a GEMM that writes planes for the next one reads the other)
     void* planes = nullptr;
@@ -265,7 +266,7 @@ int dev_alloc(nllb_model* m, T** p, size_t count) {
 const char* const kProfNames[NLLB_PROF_CLASSES] = {
     "gemm_persistent", "gemm_cluster_splitk", "linear_simt_or_tc", "decode_self", "cross",
     "prefill",         "logsoftmax_topk",     "penalties",         "beam_select", "reorder",
-    "layernorm",       "embed_pos",           "split3",            "set_memory"};
+    "layernorm",       "embed_pos",           "split_planes",      "set_memory"};
 
 // Times the launches made in its scope as one record of class `cat` (a no-op
 // unless profiling is on).  The events order the stream around the scope, so
@@ -343,16 +344,16 @@ struct Loader {
         ENG_RC(upload(prefix + "/weight", "I8", (long long)out_f * in_f, &L->w));
         ENG_RC(upload(prefix + "/weight_scale", "F32", out_f, &L->scale));
         if (tensors.count(prefix + "/bias")) ENG_RC(upload(prefix + "/bias", "F32", out_f, &L->b));
-        return bf16_copy(L);
+        return half_copy(L);
     }
-    // bf16 copy of the int8 weight (every int8 is exact in bf16) and its tensor map
-    int bf16_copy(Lin* L) {
+    // fp16 copy of the int8 weight (every int8 is exact in fp16) and its tensor map
+    int half_copy(Lin* L) {
         if (L->in % 64) return NLLB_ATTN_OK;  // the TMA kernel takes K % 64 == 0 only
-        __nv_bfloat16* wb = nullptr;
+        plane_t* wb = nullptr;
         ENG_RC(dev_alloc(m, &wb, (size_t)L->out * L->in));
-        ENG_CK(launch_int8_to_bf16(L->w, wb, (size_t)L->out * L->in, m->stream));
-        ENG_CK(encode_bf16_map(&L->tm, wb, L->in, L->out, 1));
-        ENG_CK(encode_bf16_maps_persistent(nullptr, nullptr, L->in, 0, &L->tm256, wb, L->out));
+        ENG_CK(launch_int8_to_f16(L->w, wb, (size_t)L->out * L->in, m->stream));
+        ENG_CK(encode_half_map(&L->tm, wb, L->in, L->out, 1));
+        ENG_CK(encode_half_maps_persistent(nullptr, nullptr, L->in, 0, &L->tm256, wb, L->out));
         L->wb = wb;
         return NLLB_ATTN_OK;
     }
@@ -479,7 +480,7 @@ int nllb_model_load(const char* path, int device, int max_sentences, int max_src
         m->vocab.scale = m->emb_scale;
         m->vocab.out = VOCAB;
         m->vocab.in = D;
-        ENG_RC(L.bf16_copy(&m->vocab));
+        ENG_RC(L.half_copy(&m->vocab));
         for (int i = 0; i < LAYERS; ++i) {
             const std::string p = "encoder/layer_" + std::to_string(i);
             auto& E = m->enc[i];
@@ -531,11 +532,11 @@ namespace {
 // the split-K tensor-core kernel; 4 rows x 1024 -> 256206 in 220 us against
 // a persistent kernel over one row tile.
 bool tma_path(const nllb_model* m, const Lin& L, int M) {
-    return M >= 1 && (M > 4 || L.out >= 65536) && L.wb && (size_t)M * L.in * 3 <= m->planes_elems;
+    return M >= 1 && (M > 4 || L.out >= 65536) && L.wb && (size_t)M * L.in * kPlanes <= m->planes_elems;
 }
 
 // out = x W^T / scale + bias (+ relu, + residual).  On the tensor-core path
-// the activations are read as bf16 planes: in_planes when the producer wrote
+// the activations are read as fp16 planes: in_planes when the producer wrote
 // them already (LayerNorm, the previous GEMM), else x is split into
 // m->planes first; with out_planes the result is written as planes for the
 // next GEMM instead of to out.
@@ -562,7 +563,7 @@ int run_linear(nllb_model* m, const Lin& L, const float* x, int M, float* out, c
             return nllb::set_error(NLLB_ATTN_EINVAL, "plane output needs a plain row-major result");
         if (!in_planes) {
             ProfScope ps(m, 12, 0, (double)M * L.in * 10);
-            ENG_CK(launch_split3(x, L.in, M, L.in, m->planes, m->stream));
+            ENG_CK(launch_split_planes(x, L.in, M, L.in, m->planes, m->stream));
             in_planes = m->planes;
         }
         const bool pers = linear_tma_use_persistent(M, L.out, L.in, m->num_sms);
@@ -571,9 +572,9 @@ int run_linear(nllb_model* m, const Lin& L, const float* x, int M, float* out, c
         if (it == m->plane_maps.end()) {
             CUtensorMap tx;
             if (pers)
-                ENG_CK(encode_bf16_maps_persistent(&tx, in_planes, L.in, M, nullptr, nullptr, 0));
+                ENG_CK(encode_half_maps_persistent(&tx, in_planes, L.in, M, nullptr, nullptr, 0));
             else
-                ENG_CK(encode_bf16_map(&tx, in_planes, L.in, M, 3));
+                ENG_CK(encode_half_map(&tx, in_planes, L.in, M, kPlanes));
             it = m->plane_maps.emplace(key, tx).first;
         }
         const double flops = 2.0 * M * L.out * L.in;
@@ -593,7 +594,7 @@ int run_linear(nllb_model* m, const Lin& L, const float* x, int M, float* out, c
     return NLLB_ATTN_OK;
 }
 
-// Grow the activation-plane buffer to `elems` bf16 values.
+// Grow the activation-plane buffer to `elems` fp16 values.
 int ensure_planes(nllb_model* m, size_t elems) {
     if (elems <= m->planes_elems) return NLLB_ATTN_OK;
     ENG_CK(cudaStreamSynchronize(m->stream));
@@ -602,8 +603,8 @@ int ensure_planes(nllb_model* m, size_t elems) {
     m->planes = m->planes2 = nullptr;
     m->planes_elems = 0;
     m->plane_maps.clear();
-    ENG_CK(cudaMalloc(&m->planes, elems * sizeof(__nv_bfloat16)));
-    ENG_CK(cudaMalloc(&m->planes2, elems * sizeof(__nv_bfloat16)));
+    ENG_CK(cudaMalloc(&m->planes, elems * sizeof(plane_t)));
+    ENG_CK(cudaMalloc(&m->planes2, elems * sizeof(plane_t)));
     m->planes_elems = elems;
     return NLLB_ATTN_OK;
 }
@@ -620,7 +621,7 @@ struct Work {
     float* top_lp = nullptr;
     float* topk_ws = nullptr;  // partials of the vocabulary log-softmax / top-k
     unsigned char* active = nullptr;
-    bool h_planes = false;  // the last decoder step left h as bf16 planes in m->planes (else fp32 in h)
+    bool h_planes = false;  // the last decoder step left h as fp16 planes in m->planes (else fp32 in h)
     const int* n_src_h = nullptr;  // host: source lengths in the call's internal order (profile bytes)
     // buffers come from the model's pool in call order: a call no larger than
     // an earlier one allocates nothing (the previous call has finished: it
@@ -650,7 +651,7 @@ int encode(nllb_model* m, Work& w, const std::vector<int>& n_src) {
         ENG_CK(launch_embed_pos(w.ex, w.etok, w.epos, 0, m->emb, m->emb_inv, m->pos_table, 32.0f, R, VOCAB,
                                 m->stream));
     }
-    // LayerNorm writes the bf16 planes of the next GEMM's input directly when
+    // LayerNorm writes the fp16 planes of the next GEMM's input directly when
     // that GEMM runs on the tensor cores, fc1 writes fc2's input planes
     const bool tp = tma_path(m, m->enc[0].qkv, R);
     void* P1 = tp ? m->planes : nullptr;
@@ -737,7 +738,7 @@ int decode_step(nllb_model* m, Work& w, int step) {
         }
         ENG_RC(run_linear(m, Dl.qkv, w.h, R, w.qkv, nullptr, 0, D, -1, P1));
         // on the tensor-core path the attention kernels write the output
-        // projection's bf16 planes themselves (no fp32 output, no split pass)
+        // projection's fp16 planes themselves (no fp32 output, no split pass)
         if (tp && tma_path(m, Dl.out, R)) {
             {
                 ProfScope ps(m, 3, 0, self_bytes);
@@ -859,7 +860,7 @@ extern "C" int nllb_translate(nllb_model* m, int n_sent, const int* src_tokens, 
     w.rows_enc = rows_enc;
     w.rows = n_sent * NB;
     const size_t RE = (size_t)w.rows_enc, R = (size_t)w.rows;
-    ENG_RC(ensure_planes(m, std::max(RE, R) * FFN * 3));
+    ENG_RC(ensure_planes(m, std::max(RE, R) * FFN * kPlanes));
     ENG_RC(w.alloc(&w.ex, RE * D));
     ENG_RC(w.alloc(&w.eh, RE * D));
     ENG_RC(w.alloc(&w.eqkv, RE * 3 * D));

@@ -55,7 +55,7 @@ __device__ __forceinline__ float block_sum_256(float v, float* sh) {
 
 __global__ void __launch_bounds__(256) layernorm_kernel(float* out, float* x, const float* res,
                                                          const float* gamma, const float* beta, int rows,
-                                                         __nv_bfloat16* planes) {
+                                                         plane_t* planes) {
     pdl_launch_dependents();
     pdl_wait_primary();  // inputs come from earlier kernels; outputs may still be read by them
     __shared__ float sh[8];
@@ -77,7 +77,7 @@ __global__ void __launch_bounds__(256) layernorm_kernel(float* out, float* x, co
     const float4 y = make_float4(d.x * inv_std * g.x + b.x, d.y * inv_std * g.y + b.y, d.z * inv_std * g.z + b.z,
                                  d.w * inv_std * g.w + b.w);
     if (out) reinterpret_cast<float4*>(out + (size_t)r * 1024)[threadIdx.x] = y;
-    if (planes) store_split3_x4(planes, (size_t)rows * 1024, (size_t)r * 1024 + 4 * threadIdx.x, y);
+    if (planes) store_planes_x4(planes, (size_t)rows * 1024, (size_t)r * 1024 + 4 * threadIdx.x, y);
 }
 
 // ---------------------------------------------------------------------------
@@ -655,7 +655,7 @@ cudaError_t launch_layernorm(float* out, float* x, const float* res, const float
                              int rows, void* planes, cudaStream_t st) {
     if (rows <= 0) return cudaSuccess;
     return launch_pdl(layernorm_kernel, dim3(rows), dim3(256), 0, st, out, x, res, gamma, beta, rows,
-                      static_cast<__nv_bfloat16*>(planes));
+                      static_cast<plane_t*>(planes));
 }
 
 cudaError_t launch_linear(const LinearArgs& a, const LinearWorkspace* wsp, int num_sms, int* err, cudaStream_t st) {

@@ -22,14 +22,14 @@ struct LinearArgs {
     int mask_from;           // columns >= mask_from are set to -1e30 (-1: none)
     int static_weights;      // 1: w, scale, bias are not written by earlier kernels of the stream
                              // (a kernel may fetch them before waiting for its predecessor)
-    void* out_planes;        // TMA kernels only: write bf16 planes [3][M][N] (split3 of the result)
+    void* out_planes;        // TMA kernels only: write fp16 planes [2][M][N] (planes.cuh split of the result)
                              // instead of out; requires cblock == N and no residual
 };
 
 cudaError_t launch_embed_pos(float* x, const int* tokens, const int* positions, int pos_const, const int8_t* emb,
                              const float* emb_inv_scale, const float* pos_table, float embed_scale, int rows,
                              int vocab, cudaStream_t st);
-// out (fp32, may be null) and/or planes (bf16 [3][rows][1024], may be null)
+// out (fp32, may be null) and/or planes (fp16 [2][rows][1024], may be null)
 cudaError_t launch_layernorm(float* out, float* x, const float* res, const float* gamma, const float* beta,
                              int rows, void* planes, cudaStream_t st);
 // Split-K workspace of the tensor-core linear kernel: partial tiles and one
@@ -52,22 +52,22 @@ size_t linear_tc_workspace_floats(const LinearArgs& a, int splits);
 size_t linear_tc_tiles(const LinearArgs& a);
 cudaError_t launch_linear_tc(const LinearArgs& a, int splits, float* ws, int* tile_count, int* err,
                              cudaStream_t st);
-// TMA-fed tcgen05 linear layer over bf16 operands (linear_tma.cu): weights
-// kept as a bf16 copy of the int8 matrix, activations split into three bf16
-// planes [3][M][K] by launch_split3.  K % 64 == 0, K >= 64.
+// TMA-fed tcgen05 linear layer over fp16 operands (linear_tma.cu): weights
+// kept as an fp16 copy of the int8 matrix, activations split into two fp16
+// planes [2][M][K] by launch_split_planes.  K % 64 == 0, K >= 64.
 cudaError_t configure_linear_tma();
-cudaError_t encode_bf16_map(CUtensorMap* map, const void* base, int cols, int rows, int planes);
+cudaError_t encode_half_map(CUtensorMap* map, const void* base, int cols, int rows, int planes);
 int linear_tma_splits(int M, int N, int K, int num_sms);
 // Persistent 128 x 256-tile form (K % 32 == 0), used when the output has
-// enough tiles for its K (linear_tma_use_persistent); its tensor maps: planes box 32 x 128 x 3,
+// enough tiles for its K (linear_tma_use_persistent); its tensor maps: planes box 32 x 128 x 2,
 // weight box 32 x 256 (64-byte swizzle).  Either map pointer may be null.
 bool linear_tma_use_persistent(int M, int N, int K, int num_sms);
-cudaError_t encode_bf16_maps_persistent(CUtensorMap* x_map, const void* planes, int K, int M, CUtensorMap* w_map,
+cudaError_t encode_half_maps_persistent(CUtensorMap* x_map, const void* planes, int K, int M, CUtensorMap* w_map,
                                         const void* wb, int N);
 cudaError_t launch_linear_tma_persistent(const LinearArgs& a, const CUtensorMap* tx, const CUtensorMap* tw,
                                          int num_sms, int* err, cudaStream_t st);
-cudaError_t launch_split3(const float* x, int ldx, int M, int K, void* planes, cudaStream_t st);
-cudaError_t launch_int8_to_bf16(const int8_t* w, void* out, size_t n, cudaStream_t st);
+cudaError_t launch_split_planes(const float* x, int ldx, int M, int K, void* planes, cudaStream_t st);
+cudaError_t launch_int8_to_f16(const int8_t* w, void* out, size_t n, cudaStream_t st);
 cudaError_t launch_linear_tma(const LinearArgs& a, const CUtensorMap* tx, const CUtensorMap* tw, int splits, int* err,
                               cudaStream_t st);
 cudaError_t launch_penalties(float* logits, size_t ld, const int* hist, int hist_ld, const int* n_tokens,

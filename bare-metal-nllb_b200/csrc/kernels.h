@@ -55,8 +55,8 @@ struct SelfParams {
     const float* q;       // [n_sent][n_beams][H*64]
     const float* k_new;
     const float* v_new;
-    // fp32 output, or (launch_decode_self with planes) the three bf16 planes
-    // of the output (x = p0 + p1 + p2, planes.cuh) at the same element
+    // fp32 output, or (launch_decode_self with planes) the two fp16 planes
+    // of the output (x = p0 + p1, planes.cuh) at the same element
     // offsets, one plane per n_sent * n_beams * H * 64 elements: the A operand
     // of the output projection
     float* out;

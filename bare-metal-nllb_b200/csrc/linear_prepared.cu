@@ -2,16 +2,17 @@
 //
 // The reference holds each layer as a LinearInt8 (pico.h:26-32) pointing into
 // the mmap'd model and dequantises inside every mat-vec (tensor.c:144-196).
-// nllb_linear_prepare is the resident form of one LinearInt8: it keeps a bf16
-// copy of the int8 matrix (every int8 value is exact in bf16) with its TMA
+// nllb_linear_prepare is the resident form of one LinearInt8: it keeps an fp16
+// copy of the int8 matrix (every int8 value is exact in fp16) with its TMA
 // tensor map, so nllb_linear_run feeds the tcgen05 GEMM straight from DRAM
 // through TMA (linear_tma.cu).  Up to 16 rows run on the SIMT kernel over the
 // int8 matrix, which moves half the bytes.
-#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include <string>
 
 #include "engine_kernels.h"
+#include "planes.cuh"
 #include "nllb_translate.h"
 
 namespace nllb {
@@ -27,10 +28,10 @@ struct nllb_linear {
     const float* bias = nullptr;
     int N = 0, K = 0;
     int num_sms = 148;
-    void* wb = nullptr;       // [N][K] bf16
+    void* wb = nullptr;       // [N][K] fp16
     CUtensorMap tm{};         // of wb, box 64 x 128 (split-K kernel)
     CUtensorMap tm256{};      // of wb, box 32 x 256 (persistent kernel)
-    void* planes = nullptr;   // [3][M][K] bf16, grow-only
+    void* planes = nullptr;   // [2][M][K] fp16, grow-only
     size_t planes_elems = 0;
     int map_rows = -1;        // rows the plane maps were encoded for
     CUtensorMap tx{}, tx_pers{};
@@ -86,13 +87,13 @@ int nllb_linear_prepare(const int8_t* w, const float* weight_scale, const float*
         return rc;
     };
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (cudaMalloc(&L->wb, (size_t)N * K * sizeof(__nv_bfloat16)) != cudaSuccess ||
+    if (cudaMalloc(&L->wb, (size_t)N * K * sizeof(plane_t)) != cudaSuccess ||
         cudaMalloc(&L->err, sizeof(int)) != cudaSuccess || cudaMemsetAsync(L->err, 0, sizeof(int), st) != cudaSuccess)
-        return fail(nllb::set_error(NLLB_ATTN_ECUDA, "cannot allocate the bf16 weight copy"));
-    if (launch_int8_to_bf16(w, L->wb, (size_t)N * K, st) != cudaSuccess)
+        return fail(nllb::set_error(NLLB_ATTN_ECUDA, "cannot allocate the fp16 weight copy"));
+    if (launch_int8_to_f16(w, L->wb, (size_t)N * K, st) != cudaSuccess)
         return fail(nllb::set_error(NLLB_ATTN_ECUDA, "weight conversion launch failed"));
-    if (encode_bf16_map(&L->tm, L->wb, K, N, 1) != cudaSuccess ||
-        encode_bf16_maps_persistent(nullptr, nullptr, K, 0, &L->tm256, L->wb, N) != cudaSuccess)
+    if (encode_half_map(&L->tm, L->wb, K, N, 1) != cudaSuccess ||
+        encode_half_maps_persistent(nullptr, nullptr, K, 0, &L->tm256, L->wb, N) != cudaSuccess)
         return fail(nllb::set_error(NLLB_ATTN_ECUDA, "cuTensorMapEncodeTiled failed for the weight"));
     *out = L;
     return NLLB_ATTN_OK;
@@ -128,22 +129,22 @@ int nllb_linear_run(nllb_linear* L, const float* x, int M, float* out, const flo
         LP_CK(launch_linear(a, nullptr, L->num_sms, L->err, st));
         return NLLB_ATTN_OK;
     }
-    const size_t need = (size_t)M * L->K * 3;
+    const size_t need = (size_t)M * L->K * kPlanes;
     if (need > L->planes_elems) {
         LP_CK(cudaStreamSynchronize(st));  // the previous planes may still be read
         if (L->planes) cudaFree(L->planes);
         L->planes = nullptr;
         L->planes_elems = 0;
         L->map_rows = -1;
-        LP_CK(cudaMalloc(&L->planes, need * sizeof(__nv_bfloat16)));
+        LP_CK(cudaMalloc(&L->planes, need * sizeof(plane_t)));
         L->planes_elems = need;
     }
     if (L->map_rows != M) {
-        LP_CK(encode_bf16_map(&L->tx, L->planes, L->K, M, 3));
-        LP_CK(encode_bf16_maps_persistent(&L->tx_pers, L->planes, L->K, M, nullptr, nullptr, 0));
+        LP_CK(encode_half_map(&L->tx, L->planes, L->K, M, kPlanes));
+        LP_CK(encode_half_maps_persistent(&L->tx_pers, L->planes, L->K, M, nullptr, nullptr, 0));
         L->map_rows = M;
     }
-    LP_CK(launch_split3(x, L->K, M, L->K, L->planes, st));
+    LP_CK(launch_split_planes(x, L->K, M, L->K, L->planes, st));
     if (linear_tma_use_persistent(M, L->N, L->K, L->num_sms))
         LP_CK(launch_linear_tma_persistent(a, &L->tx_pers, &L->tm256, L->num_sms, L->err, st));
     else

@@ -1,16 +1,17 @@
 // linear_tma.cu -- INT8-weight linear layer for the translation engine on
 // tcgen05 tensor cores, fed by TMA (sm_100a).
 //
-// Same arithmetic as linear_tc.cu (int8 weights exact in bf16, fp32
-// activations as three bf16 parts x1 + x2 + x3, three MMAs per k-step, fp32
-// accumulation in TMEM), with the conversions moved out of the GEMM: the
-// engine keeps a bf16 copy of every weight matrix (converted once at load)
-// and splits each activation matrix into its three planes once per GEMM
-// (split3_kernel), so the GEMM's operands are plain bf16 matrices that TMA
-// tensor maps load straight into 128-byte-swizzled shared memory.
+// int8 weights are exact in fp16 and fp32 activations are taken as two fp16
+// parts x = x1 + x2 (planes.cuh, 22 significant bits): two MMAs per k-step
+// (kind::f16), fp32 accumulation in TMEM.  The engine keeps an fp16 copy of
+// every weight matrix (converted once at load) and the producers of the
+// activations write them as planes (LayerNorm, the attention kernels, the
+// previous GEMM's epilogue; split_planes_kernel otherwise), so the GEMM's
+// operands are plain fp16 matrices that TMA tensor maps load straight into
+// swizzled shared memory.
 //
 // CTA: warps 0-7 epilogue, warp 8 lane 0 TMA producer, warp 9 lane 0 MMA
-// issuer; 128 x 128 output tile; K in stages of 64 (3 X planes + W = 64 KB
+// issuer; 128 x 128 output tile; K in stages of 64 (2 X planes + W = 48 KB
 // per stage, 3 stages).  Split-K over a thread-block cluster along x: the S
 // CTAs of a tile each leave their 128 x 128 partial sum in shared memory and
 // cluster rank z reduces rows [z*128/S, (z+1)*128/S) over all S partials in
@@ -18,7 +19,7 @@
 // Grid x = (row tile, split) fastest, so the row tiles that share a weight
 // tile run together and the weight tile is read from DRAM once.
 #include <cuda.h>
-#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -33,18 +34,20 @@ namespace {
 
 constexpr int TM = 128, TN = 128, TK = 64, STAGES = 3;
 constexpr int EPI_WARPS = 8, THREADS = (EPI_WARPS + 2) * 32;
-constexpr uint32_t PLANE = TM * TK * 2;      // 16 KB
-constexpr uint32_t STAGE_BYTES = 4 * PLANE;  // x1, x2, x3, w
+constexpr uint32_t PLANE = TM * TK * 2;                 // 16 KB
+constexpr uint32_t W_OFF = kPlanes * PLANE;             // the weight tile follows the X planes
+constexpr uint32_t STAGE_BYTES = (kPlanes + 1) * PLANE;  // x1, x2, w
 constexpr uint32_t SMEM_BAR = STAGES * STAGE_BYTES;
 constexpr uint32_t SMEM_TOTAL = SMEM_BAR + 128 + 1024;
 constexpr uint32_t TMEM_COLS = 128;
 constexpr int PART_STRIDE = TN + 4;  // floats per row of the partial tile in shared memory
 
-__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+// Instruction descriptor, kind::f16: fp32 accumulator, A and B fp16, both K-major.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
-__device__ __forceinline__ void mma_bf16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+__device__ __forceinline__ void mma_f16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
@@ -80,7 +83,7 @@ __device__ __forceinline__ void epilogue_store(const LinearArgs& a, int m, int n
     const size_t o = (size_t)(n / a.cblock) * ((size_t)a.M * a.cblock) + (size_t)m * a.cblock + (n % a.cblock);
     if (a.residual) y += a.residual[o];
     if (a.out_planes)
-        store_split3_x1(static_cast<__nv_bfloat16*>(a.out_planes), (size_t)a.M * a.N, o, y);
+        store_planes_x1(static_cast<plane_t*>(a.out_planes), (size_t)a.M * a.N, o, y);
     else
         a.out[o] = y;
 }
@@ -140,16 +143,16 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (a.static_weights)
             for (int c = 0; c < pre; ++c) {
                 mbar_arrive_expect_tx(&full[c], STAGE_BYTES);
-                tma_load_2d(base + c * STAGE_BYTES + 3 * PLANE, &tw, (kc0 + c) * TK, n0, &full[c]);
+                tma_load_2d(base + c * STAGE_BYTES + W_OFF, &tw, (kc0 + c) * TK, n0, &full[c]);
             }
         pdl_wait_primary();
         for (int c = 0; c < pre; ++c) {
             unsigned char* st = base + c * STAGE_BYTES;
             if (!a.static_weights) {
                 mbar_arrive_expect_tx(&full[c], STAGE_BYTES);
-                tma_load_2d(st + 3 * PLANE, &tw, (kc0 + c) * TK, n0, &full[c]);
+                tma_load_2d(st + W_OFF, &tw, (kc0 + c) * TK, n0, &full[c]);
             }
-            tma_load_3d(st, &tx, (kc0 + c) * TK, m0, 0, &full[c]);  // box 64 x 128 x 3: the three planes
+            tma_load_3d(st, &tx, (kc0 + c) * TK, m0, 0, &full[c]);  // box 64 x 128 x 2: the planes
         }
         for (int c = pre; c < nk; ++c) {
             const int s = c % STAGES;
@@ -160,12 +163,12 @@ __global__ void __launch_bounds__(THREADS, 1)
             unsigned char* st = base + s * STAGE_BYTES;
             const int k = (kc0 + c) * TK;
             mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-            tma_load_3d(st, &tx, k, m0, 0, &full[s]);  // box 64 x 128 x 3: the three planes
-            tma_load_2d(st + 3 * PLANE, &tw, k, n0, &full[s]);
+            tma_load_3d(st, &tx, k, m0, 0, &full[s]);  // box 64 x 128 x 2: the planes
+            tma_load_2d(st + W_OFF, &tw, k, n0, &full[s]);
         }
     } else if (warp == EPI_WARPS + 1 && lane == 0) {
         // ---- MMA issuer
-        constexpr uint32_t idesc = idesc_bf16(TM, TN);
+        constexpr uint32_t idesc = idesc_f16(TM, TN);
         for (int c = 0; c < nk; ++c) {
             const int s = c % STAGES;
             if (!mbar_wait_bounded(&full[s], (uint32_t)((c / STAGES) & 1))) {
@@ -176,10 +179,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint32_t st = base_addr + s * STAGE_BYTES;
 #pragma unroll
             for (int ks = 0; ks < TK / 16; ++ks) {
-                const uint64_t bw = umma_desc_k_sw128(st + 3 * PLANE + ks * 32);
-                mma_bf16(tmem, umma_desc_k_sw128(st + 0 * PLANE + ks * 32), bw, idesc, (c > 0 || ks > 0) ? 1u : 0u);
-                mma_bf16(tmem, umma_desc_k_sw128(st + 1 * PLANE + ks * 32), bw, idesc, 1u);
-                mma_bf16(tmem, umma_desc_k_sw128(st + 2 * PLANE + ks * 32), bw, idesc, 1u);
+                const uint64_t bw = umma_desc_k_sw128(st + W_OFF + ks * 32);
+                mma_f16(tmem, umma_desc_k_sw128(st + 0 * PLANE + ks * 32), bw, idesc, (c > 0 || ks > 0) ? 1u : 0u);
+                mma_f16(tmem, umma_desc_k_sw128(st + 1 * PLANE + ks * 32), bw, idesc, 1u);
             }
             tc_commit(&empty[s]);
         }
@@ -275,7 +277,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         const size_t o = tile_off + (size_t)m * a.cblock;
                         const float4 yv = make_float4(y[0], y[1], y[2], y[3]);
                         if (a.out_planes) {
-                            store_split3_x4(static_cast<__nv_bfloat16*>(a.out_planes), (size_t)a.M * a.N, o, yv);
+                            store_planes_x4(static_cast<plane_t*>(a.out_planes), (size_t)a.M * a.N, o, yv);
                         } else {
                             *reinterpret_cast<float4*>(a.out + o) = yv;
                         }
@@ -324,18 +326,19 @@ __global__ void __launch_bounds__(THREADS, 1)
 // Persistent form for outputs with at least one 128 x 256 tile per SM: one CTA
 // per SM walks tiles t = blockIdx.x, + gridDim.x, ... (row tile fastest, so
 // CTAs running at the same time share a weight tile in L2).  Warp 0 lane 0
-// streams 32-wide K chunks (3 planes 8 KB + weight 16 KB, 64-byte swizzle)
-// through a 4-stage ring, warp 1 lane 0 issues 128 x 256 x 16 MMAs into one
+// streams 32-wide K chunks (2 planes 8 KB + weight 16 KB, 64-byte swizzle)
+// through a 5-stage ring, warp 1 lane 0 issues 128 x 256 x 16 MMAs into one
 // of two TMEM accumulators (2 x 256 columns), and warps 2-9 drain the other
 // accumulator meanwhile: TMEM -> registers -> a per-warp transpose buffer ->
 // stores of 32 consecutive columns per row.
 // ---------------------------------------------------------------------------
 namespace pers {
-constexpr int TM = 128, TN = 256, TK = 32, STAGES = 4;
+constexpr int TM = 128, TN = 256, TK = 32, STAGES = 5;
 constexpr int EPI_WARPS = 8, THREADS = (EPI_WARPS + 2) * 32;
 constexpr uint32_t A_PLANE = TM * TK * 2;                // 8 KB
 constexpr uint32_t B_BYTES = TN * TK * 2;                // 16 KB
-constexpr uint32_t STAGE_BYTES = 3 * A_PLANE + B_BYTES;  // 40 KB
+constexpr uint32_t W_OFF = kPlanes * A_PLANE;                 // weight tile after the X planes
+constexpr uint32_t STAGE_BYTES = kPlanes * A_PLANE + B_BYTES;  // 32 KB
 constexpr int BUF_LD = 33;                               // transpose buffer row stride (floats)
 constexpr uint32_t SMEM_EPI = STAGES * STAGE_BYTES;
 constexpr uint32_t SMEM_BAR = SMEM_EPI + EPI_WARPS * 32 * BUF_LD * 4;
@@ -343,7 +346,7 @@ constexpr uint32_t SMEM_TOTAL = SMEM_BAR + 256 + 1024;
 constexpr uint32_t TMEM_COLS = 512;
 }  // namespace pers
 
-// K-major operand in the 64-byte swizzled layout: rows of 64 B (32 bf16),
+// K-major operand in the 64-byte swizzled layout: rows of 64 B (32 fp16),
 // 8-row atoms 512 B apart (stride byte offset), descriptor version 1.
 __device__ __forceinline__ uint64_t umma_desc_k_sw64(uint32_t smem_addr) {
     return (uint64_t)((smem_addr >> 4) & 0x3FFFu) | ((uint64_t)1u << 16) | ((uint64_t)(512u >> 4) << 32) |
@@ -363,6 +366,7 @@ __global__ void __launch_bounds__(pers::THREADS, 1)
     constexpr int TM = pers::TM, TN = pers::TN, TK = pers::TK, STAGES = pers::STAGES, EPI_WARPS = pers::EPI_WARPS;
     constexpr int BUF_LD = pers::BUF_LD;
     constexpr uint32_t A_PLANE = pers::A_PLANE, STAGE_BYTES = pers::STAGE_BYTES, SMEM_EPI = pers::SMEM_EPI;
+    constexpr uint32_t W_OFF = pers::W_OFF;
     constexpr uint32_t SMEM_BAR = pers::SMEM_BAR, TMEM_COLS = pers::TMEM_COLS;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -409,7 +413,7 @@ __global__ void __launch_bounds__(pers::THREADS, 1)
             if (a.static_weights)
                 for (int c = 0; c < pre; ++c) {
                     mbar_arrive_expect_tx(&full[c], STAGE_BYTES);
-                    tma_load_2d(base + c * STAGE_BYTES + 3 * A_PLANE, &tw, c * TK, ((int)blockIdx.x / MT) * TN,
+                    tma_load_2d(base + c * STAGE_BYTES + W_OFF, &tw, c * TK, ((int)blockIdx.x / MT) * TN,
                                 &full[c]);
                 }
             pdl_wait_primary();
@@ -422,9 +426,9 @@ __global__ void __launch_bounds__(pers::THREADS, 1)
                         unsigned char* st = base + s * STAGE_BYTES;
                         if (!a.static_weights) {
                             mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-                            tma_load_2d(st + 3 * A_PLANE, &tw, c * TK, n0, &full[s]);
+                            tma_load_2d(st + W_OFF, &tw, c * TK, n0, &full[s]);
                         }
-                        tma_load_3d(st, &tx, c * TK, m0, 0, &full[s]);  // box 32 x 128 x 3: the three planes
+                        tma_load_3d(st, &tx, c * TK, m0, 0, &full[s]);  // box 32 x 128 x 2: the planes
                         continue;
                     }
                     if (!mbar_wait_bounded(&empty[s], (use & 1u) ^ 1u)) {
@@ -433,14 +437,14 @@ __global__ void __launch_bounds__(pers::THREADS, 1)
                     }
                     unsigned char* st = base + s * STAGE_BYTES;
                     mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-                    tma_load_3d(st, &tx, c * TK, m0, 0, &full[s]);  // box 32 x 128 x 3: the three planes
-                    tma_load_2d(st + 3 * A_PLANE, &tw, c * TK, n0, &full[s]);
+                    tma_load_3d(st, &tx, c * TK, m0, 0, &full[s]);  // box 32 x 128 x 2: the planes
+                    tma_load_2d(st + W_OFF, &tw, c * TK, n0, &full[s]);
                 }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {  // ---- MMA issuer
-            constexpr uint32_t idesc = idesc_bf16(TM, TN);
+            constexpr uint32_t idesc = idesc_f16(TM, TN);
             uint32_t g = 0, i = 0;
             for (int t = blockIdx.x; t < tiles && !*s_abort; t += gridDim.x, ++i) {
                 const uint32_t acc = i & 1u;
@@ -461,10 +465,9 @@ __global__ void __launch_bounds__(pers::THREADS, 1)
                     const uint32_t sa = base_addr + s * STAGE_BYTES;
 #pragma unroll
                     for (int ks = 0; ks < TK / 16; ++ks) {
-                        const uint64_t bw = umma_desc_k_sw64(sa + 3 * A_PLANE + ks * 32);
-                        mma_bf16(d, umma_desc_k_sw64(sa + 0 * A_PLANE + ks * 32), bw, idesc, (c > 0 || ks > 0) ? 1u : 0u);
-                        mma_bf16(d, umma_desc_k_sw64(sa + 1 * A_PLANE + ks * 32), bw, idesc, 1u);
-                        mma_bf16(d, umma_desc_k_sw64(sa + 2 * A_PLANE + ks * 32), bw, idesc, 1u);
+                        const uint64_t bw = umma_desc_k_sw64(sa + W_OFF + ks * 32);
+                        mma_f16(d, umma_desc_k_sw64(sa + 0 * A_PLANE + ks * 32), bw, idesc, (c > 0 || ks > 0) ? 1u : 0u);
+                        mma_f16(d, umma_desc_k_sw64(sa + 1 * A_PLANE + ks * 32), bw, idesc, 1u);
                     }
                     tc_commit(&empty[s]);
                 }
@@ -514,7 +517,7 @@ __global__ void __launch_bounds__(pers::THREADS, 1)
                         const size_t o = colbase + (size_t)(mrow + r) * a.cblock;
                         if (a.residual) y += a.residual[o];
                         if (a.out_planes)
-                            store_split3_x1(static_cast<__nv_bfloat16*>(a.out_planes), (size_t)a.M * a.N, o, y);
+                            store_planes_x1(static_cast<plane_t*>(a.out_planes), (size_t)a.M * a.N, o, y);
                         else
                             a.out[o] = y;
                     }
@@ -535,8 +538,8 @@ __global__ void __launch_bounds__(pers::THREADS, 1)
     if (tid == 0 && *s_abort) atomicOr(err, NLLB_DEV_ERR_TIMEOUT);
 }
 
-// x [M][ldx] fp32 -> planes [3][M][K] bf16 with x = p0 + p1 + p2 (to 24 bits)
-__global__ void split3_kernel(const float* x, int ldx, int M, int K, __nv_bfloat16* planes) {
+// x [M][ldx] fp32 -> planes [2][M][K] fp16 with x = p0 + p1 (planes.cuh)
+__global__ void split_planes_kernel(const float* x, int ldx, int M, int K, plane_t* planes) {
     pdl_launch_dependents();
     pdl_wait_primary();  // x comes from the previous kernel; the planes may still be read by the previous GEMM
     const size_t n4 = (size_t)M * (K / 4);
@@ -544,13 +547,13 @@ __global__ void split3_kernel(const float* x, int ldx, int M, int K, __nv_bfloat
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
         const int m = (int)(i / (K / 4)), k = (int)(i % (K / 4)) * 4;
         const float4 v = *reinterpret_cast<const float4*>(x + (size_t)m * ldx + k);
-        store_split3_x4(planes, plane, (size_t)m * K + k, v);
+        store_planes_x4(planes, plane, (size_t)m * K + k, v);
     }
 }
 
-__global__ void int8_to_bf16_kernel(const int8_t* w, __nv_bfloat16* out, size_t n) {
+__global__ void int8_to_f16_kernel(const int8_t* w, plane_t* out, size_t n) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-        out[i] = __float2bfloat16_rn((float)w[i]);
+        out[i] = __float2half_rn((float)w[i]);  // exact: |w| <= 127
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
@@ -578,10 +581,10 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return g_encode;
 }
 
-// Tensor map of a row-major bf16 matrix stack: `planes` matrices of
+// Tensor map of a row-major fp16 matrix stack: `planes` matrices of
 // [rows][cols] (K-major), box box_cols x box_rows (x planes), with the
 // 128-byte swizzle (box_cols 64) or the 64-byte swizzle (box_cols 32).
-cudaError_t encode_bf16_map_box(CUtensorMap* map, const void* base, int cols, int rows, int planes, int box_cols,
+cudaError_t encode_half_map_box(CUtensorMap* map, const void* base, int cols, int rows, int planes, int box_cols,
                                 int box_rows) {
     if (!tensor_map_encoder()) return cudaErrorNotSupported;
     if (box_cols != 64 && box_cols != 32) return cudaErrorInvalidValue;
@@ -590,22 +593,22 @@ cudaError_t encode_bf16_map_box(CUtensorMap* map, const void* base, int cols, in
     const cuuint32_t box[3] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows, (cuuint32_t)planes};
     const cuuint32_t estr[3] = {1, 1, 1};
     const CUresult r =
-        g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, planes > 1 ? 3 : 2, const_cast<void*>(base), dims, strides,
+        g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, planes > 1 ? 3 : 2, const_cast<void*>(base), dims, strides,
                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                  box_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-cudaError_t encode_bf16_map(CUtensorMap* map, const void* base, int cols, int rows, int planes) {
-    return encode_bf16_map_box(map, base, cols, rows, planes, TK, TM);
+cudaError_t encode_half_map(CUtensorMap* map, const void* base, int cols, int rows, int planes) {
+    return encode_half_map_box(map, base, cols, rows, planes, TK, TM);
 }
 
-cudaError_t encode_bf16_maps_persistent(CUtensorMap* x_map, const void* planes, int K, int M, CUtensorMap* w_map,
+cudaError_t encode_half_maps_persistent(CUtensorMap* x_map, const void* planes, int K, int M, CUtensorMap* w_map,
                                         const void* wb, int N) {
     cudaError_t e = cudaSuccess;
-    if (x_map) e = encode_bf16_map_box(x_map, planes, K, M, 3, pers::TK, pers::TM);
-    if (e == cudaSuccess && w_map) e = encode_bf16_map_box(w_map, wb, K, N, 1, pers::TK, pers::TN);
+    if (x_map) e = encode_half_map_box(x_map, planes, K, M, kPlanes, pers::TK, pers::TM);
+    if (e == cudaSuccess && w_map) e = encode_half_map_box(w_map, wb, K, N, 1, pers::TK, pers::TN);
     return e;
 }
 
@@ -674,19 +677,19 @@ int linear_tma_splits(int M, int N, int K, int num_sms) {
     return S;
 }
 
-cudaError_t launch_split3(const float* x, int ldx, int M, int K, void* planes, cudaStream_t st) {
+cudaError_t launch_split_planes(const float* x, int ldx, int M, int K, void* planes, cudaStream_t st) {
     const size_t n4 = (size_t)M * (K / 4);
     int blocks = (int)((n4 + 255) / 256);
     blocks = blocks < 4096 ? blocks : 4096;
     if (blocks < 1) return cudaSuccess;
-    return launch_pdl(split3_kernel, dim3(blocks), dim3(256), 0, st, x, ldx, M, K,
-                      static_cast<__nv_bfloat16*>(planes));
+    return launch_pdl(split_planes_kernel, dim3(blocks), dim3(256), 0, st, x, ldx, M, K,
+                      static_cast<plane_t*>(planes));
 }
 
-cudaError_t launch_int8_to_bf16(const int8_t* w, void* out, size_t n, cudaStream_t st) {
+cudaError_t launch_int8_to_f16(const int8_t* w, void* out, size_t n, cudaStream_t st) {
     int blocks = (int)((n + 255) / 256);
     blocks = blocks < 8192 ? blocks : 8192;
-    int8_to_bf16_kernel<<<blocks, 256, 0, st>>>(w, static_cast<__nv_bfloat16*>(out), n);
+    int8_to_f16_kernel<<<blocks, 256, 0, st>>>(w, static_cast<plane_t*>(out), n);
     return cudaGetLastError();
 }
 

@@ -1,38 +1,44 @@
-// planes.cuh -- fp32 -> three bf16 planes, x = p0 + p1 + p2 to 24 bits.
+// planes.cuh -- fp32 -> two fp16 planes, x = p0 + p1 to 22 bits.
 //
-// Every int8 weight is exact in bf16, so x * w is three bf16 MMAs with fp32
-// accumulation.  The split is the same wherever it is made (split3_kernel,
-// LayerNorm, GEMM epilogues), so a value gives the same planes on every path.
+// Every int8 weight is exact in fp16, so x * w is two fp16 MMAs (kind::f16)
+// with fp32 accumulation, each product exact in fp32.  p0 = fp16(x) keeps 11
+// significant bits, p1 = fp16(x - p0) the next 11: |x - p0 - p1| <= 2^-22 |x|
+// while |x - p0| >= 2^-14 (below that p1 is subnormal and the error is at most
+// 2^-25 in absolute terms).  Valid for |x| < 65504, the fp16 range; the
+// engine's activations (LayerNorm outputs, attention outputs, the FFN's
+// hidden layer) stay far inside it.  The split is the same wherever it is
+// made (split kernel, LayerNorm, attention kernels, GEMM epilogues), so a
+// value gives the same planes on every path.
 #pragma once
-#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 namespace nllb {
 
-__device__ __forceinline__ void split3_value(float x, __nv_bfloat16& p0, __nv_bfloat16& p1, __nv_bfloat16& p2) {
-    p0 = __float2bfloat16_rn(x);
-    const float r1 = x - __bfloat162float(p0);
-    p1 = __float2bfloat16_rn(r1);
-    p2 = __float2bfloat16_rn(r1 - __bfloat162float(p1));
+using plane_t = __half;
+constexpr int kPlanes = 2;
+
+__device__ __forceinline__ void split_value(float x, plane_t& p0, plane_t& p1) {
+    p0 = __float2half_rn(x);
+    p1 = __float2half_rn(x - __half2float(p0));
 }
 
 // Four consecutive values -> 8 bytes in each plane (plane stride in elements).
-__device__ __forceinline__ void store_split3_x4(__nv_bfloat16* planes, size_t plane_stride, size_t o, float4 v) {
-    __nv_bfloat16 p[3][4];
-    split3_value(v.x, p[0][0], p[1][0], p[2][0]);
-    split3_value(v.y, p[0][1], p[1][1], p[2][1]);
-    split3_value(v.z, p[0][2], p[1][2], p[2][2]);
-    split3_value(v.w, p[0][3], p[1][3], p[2][3]);
+__device__ __forceinline__ void store_planes_x4(plane_t* planes, size_t plane_stride, size_t o, float4 v) {
+    plane_t p[kPlanes][4];
+    split_value(v.x, p[0][0], p[1][0]);
+    split_value(v.y, p[0][1], p[1][1]);
+    split_value(v.z, p[0][2], p[1][2]);
+    split_value(v.w, p[0][3], p[1][3]);
 #pragma unroll
-    for (int q = 0; q < 3; ++q)
+    for (int q = 0; q < kPlanes; ++q)
         *reinterpret_cast<uint2*>(planes + q * plane_stride + o) = *reinterpret_cast<const uint2*>(p[q]);
 }
 
-__device__ __forceinline__ void store_split3_x1(__nv_bfloat16* planes, size_t plane_stride, size_t o, float v) {
-    __nv_bfloat16 p0, p1, p2;
-    split3_value(v, p0, p1, p2);
+__device__ __forceinline__ void store_planes_x1(plane_t* planes, size_t plane_stride, size_t o, float v) {
+    plane_t p0, p1;
+    split_value(v, p0, p1);
     planes[o] = p0;
     planes[plane_stride + o] = p1;
-    planes[2 * plane_stride + o] = p2;
 }
 
 }  // namespace nllb

@@ -758,8 +758,8 @@ def roofline_from_profile(prof, hbm_peak, tflops_sust, peak_kind):
         ach = v["flops"] / (v["ms"] / 1e3) / 1e12
         roof = {"bound": "tensor", "achieved": round(ach, 1), "peak": tflops_sust, "unit": "TFLOP/s",
                 "frac": round(ach / tflops_sust, 4),
-                "note": "dense FLOPs 2*M*N*K of the linear layers; each product runs as three bf16 MMAs "
-                        "(activations split into three bf16 parts), so the tensor pipe does 3x this work",
+                "note": "dense FLOPs 2*M*N*K of the linear layers; each product runs as two fp16 MMAs "
+                        "(activations split into two fp16 parts), so the tensor pipe does 2x this work",
                 "peak_which": "bf16_tflops_sustained (kernel timed inside a long run)"}
     else:
         ach = v["bytes"] / (v["ms"] / 1e3) / 1e9

@@ -3,7 +3,7 @@ rows) on the GPU against a float64 evaluation of the reference arithmetic:
 out[m][n] = sum_k x[m][k] * (w[n][k] * (1/scale[n])) + bias[n].
 
 Rows <= 16 take the SIMT kernel, more rows the tcgen05 kernel (int8 weights
-exact in bf16, activations split into three bf16 parts); the tolerance is
+exact in fp16, activations split into two fp16 parts); the tolerance is
 fp32 accumulation error relative to the sum of |terms|.
 """
 import numpy as np
