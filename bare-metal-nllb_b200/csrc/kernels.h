@@ -143,6 +143,10 @@ cudaError_t launch_set_memory(float* km, float* vm, int max_src, int H, const fl
                               const float* v, long long stride_head, long long stride_row,
                               int n_src, int* n_src_slot, cudaStream_t st);
 cudaError_t launch_prefill(const PrefillParams& p, cudaStream_t st);
+// attention_head's softmaxed score matrix (tensor.c:258-277): p [S][S] from
+// q, k [S][64] and an additive mask [S][S] (may be null).
+cudaError_t launch_head_scores(const float* q, const float* k, const float* mask, float* p, int S, float scale,
+                               cudaStream_t st);
 // seq_len range served by the tcgen05 kernel (others: FFMA kernel)
 bool prefill_uses_tensor_cores(int seq_len);
 

@@ -793,8 +793,12 @@ int dropin_ctx(nllb_attn_ctx** out) {
     return NLLB_ATTN_OK;
 }
 
+// attention_head / attention_head_flash on the calling thread's context;
+// with scores_buf (attention_head) the softmaxed score matrix is written
+// there too, from the Q, K and mask the prefill call just staged on the
+// device (staging slots 0, 1 and 5) into slot 3 (its output, already copied).
 void single_head(const char* name, const float* Q, const float* K, const float* V, const float* mask,
-                 float* out, int seq_len, int head_dim) {
+                 float* out, int seq_len, int head_dim, float* scores_buf = nullptr) {
     nllb_attn_ctx* c = nullptr;
     int rc = dropin_ctx(&c);
     if (rc == NLLB_ATTN_OK) {
@@ -815,6 +819,20 @@ void single_head(const char* name, const float* Q, const float* K, const float* 
         a.mask_stride_head = 0;
         a.scale = 1.0f / sqrtf((float)head_dim);  // tensor.c:258, 289
         rc = nllb_attn_prefill_host(c, &a);
+        if (rc == NLLB_ATTN_OK && scores_buf) {
+            const size_t bytes = (size_t)seq_len * seq_len * sizeof(float);
+            rc = ensure_stage(c, 3, bytes);
+            if (rc == NLLB_ATTN_OK) {
+                cudaError_t e = launch_head_scores(static_cast<const float*>(c->stg[0]),
+                                                   static_cast<const float*>(c->stg[1]),
+                                                   mask ? static_cast<const float*>(c->stg[5]) : nullptr,
+                                                   static_cast<float*>(c->stg[3]), seq_len, a.scale, c->stream);
+                if (e == cudaSuccess)
+                    e = cudaMemcpyAsync(scores_buf, c->stg[3], bytes, cudaMemcpyDeviceToHost, c->stream);
+                if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+                if (e != cudaSuccess) rc = fail(NLLB_ATTN_ECUDA, std::string("scores: ") + cudaGetErrorString(e));
+            }
+        }
     }
     t_last_status = rc;
     if (rc) std::fprintf(stderr, "%s: %s (%s)\n", name, nllb_attn_strerror(rc), t_last_error.c_str());
@@ -825,8 +843,7 @@ extern "C" {
 
 void nllb_attention_head(const float* Q, const float* K, const float* V, const float* mask, float* out,
                          float* scores_buf, int seq_len, int head_dim) {
-    (void)scores_buf;
-    single_head("nllb_attention_head", Q, K, V, mask, out, seq_len, head_dim);
+    single_head("nllb_attention_head", Q, K, V, mask, out, seq_len, head_dim, scores_buf);
 }
 
 void nllb_attention_head_flash(const float* Q, const float* K, const float* V, const float* mask,

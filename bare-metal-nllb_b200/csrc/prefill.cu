@@ -532,7 +532,68 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
     }
 }
 
+// The score matrix of attention_head (tensor.c:258-277): row i holds
+// softmax_j((q_i . k_j) * scale + mask[i][j]) over j < S, the max subtracted
+// before the exponentials (softmax, tensor.c:227-238).  One CTA per row;
+// q, k: [S][64], mask [S][S] or null, p: [S][S].
+__global__ void __launch_bounds__(256) head_scores_kernel(const float* q, const float* k, const float* mask,
+                                                          float* p, int S, float scale) {
+    __shared__ float qs[64];
+    __shared__ float red[8];
+    const int i = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid < 64) qs[tid] = q[(size_t)i * 64 + tid];
+    __syncthreads();
+    float* row = p + (size_t)i * S;
+    float mx = -INFINITY;
+    for (int j = tid; j < S; j += blockDim.x) {
+        const float4* kj = reinterpret_cast<const float4*>(k + (size_t)j * 64);
+        float dot = 0.f;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+            const float4 kv = kj[c];
+            dot = fmaf(qs[4 * c], kv.x, dot);
+            dot = fmaf(qs[4 * c + 1], kv.y, dot);
+            dot = fmaf(qs[4 * c + 2], kv.z, dot);
+            dot = fmaf(qs[4 * c + 3], kv.w, dot);
+        }
+        float sc = dot * scale;
+        if (mask) sc += mask[(size_t)i * S + j];
+        row[j] = sc;
+        mx = fmaxf(mx, sc);
+    }
+    auto block_reduce = [&](float v, bool is_max) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float w = __shfl_xor_sync(0xffffffffu, v, o);
+            v = is_max ? fmaxf(v, w) : v + w;
+        }
+        __syncthreads();
+        if (lane == 0) red[warp] = v;
+        __syncthreads();
+        float t = red[0];
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) t = is_max ? fmaxf(t, red[w]) : t + red[w];
+        return t;
+    };
+    mx = block_reduce(mx, true);
+    float sum = 0.f;
+    for (int j = tid; j < S; j += blockDim.x) {
+        const float e = expf(row[j] - mx);
+        row[j] = e;
+        sum += e;
+    }
+    sum = block_reduce(sum, false);
+    const float inv = 1.0f / sum;
+    for (int j = tid; j < S; j += blockDim.x) row[j] *= inv;
+}
+
 }  // namespace
+
+cudaError_t launch_head_scores(const float* q, const float* k, const float* mask, float* p, int S, float scale,
+                               cudaStream_t st) {
+    if (S <= 0) return cudaSuccess;
+    head_scores_kernel<<<S, 256, 0, st>>>(q, k, mask, p, S, scale);
+    return cudaGetLastError();
+}
 
 // The fp32 tensor map of q, k or v for the tensor-core kernel: 4-D, column
 // (64, contiguous) first, then the row, head and sequence axes in the order

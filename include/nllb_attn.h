@@ -197,7 +197,8 @@ NLLB_ATTN_API int nllb_attn_cross_host(nllb_attn_ctx* ctx, int layer, int n_sent
  * pointers, Q/K/V/out [seq_len][head_dim], optional additive mask
  * [seq_len][seq_len].  They run on the calling thread's own context (device
  * from $NLLB_ATTN_DEVICE, default 0), created on first use.  head_dim must be
- * 64.  scores_buf is caller scratch in the reference and is not written.
+ * 64.  attention_head also leaves the softmaxed score matrix [seq_len][seq_len]
+ * in scores_buf, as the reference does (tensor.c:258-277).
  * They return void like the originals; a failure is printed to stderr and
  * reported by nllb_attn_last_status(). */
 NLLB_ATTN_API void nllb_attention_head(const float* Q, const float* K, const float* V,

@@ -228,17 +228,20 @@ def ref_linear(x, w, scale, bias=None) -> np.ndarray:
     return out
 
 
-def ref_attention_head(Q, K, V, mask, flash: bool) -> np.ndarray:
+def ref_attention_head(Q, K, V, mask, flash: bool, return_scores: bool = False):
+    """The reference's attention_head_flash (tensor.c:286) or attention_head
+    (tensor.c:255); with return_scores (attention_head only) also the
+    softmaxed score matrix it leaves in scores_buf (tensor.c:266-277)."""
     Q, K, V = (np.ascontiguousarray(a, dtype=np.float32) for a in (Q, K, V))
     out = np.zeros_like(Q)
     m = None if mask is None else np.ascontiguousarray(mask, dtype=np.float32)
     lib = ref_lib()
     if flash:
         lib.attention_head_flash(_p(Q), _p(K), _p(V), _p(m), _p(out), Q.shape[0], Q.shape[1])
-    else:
-        sb = np.zeros((Q.shape[0], Q.shape[0]), dtype=np.float32)
-        lib.attention_head(_p(Q), _p(K), _p(V), _p(m), _p(out), _p(sb), Q.shape[0], Q.shape[1])
-    return out
+        return out
+    sb = np.zeros((Q.shape[0], Q.shape[0]), dtype=np.float32)
+    lib.attention_head(_p(Q), _p(K), _p(V), _p(m), _p(out), _p(sb), Q.shape[0], Q.shape[1])
+    return (out, sb) if return_scores else out
 
 
 def ref_decode_sweep(q, k, v, parents=None) -> np.ndarray:

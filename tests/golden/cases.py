@@ -8,7 +8,8 @@ make_golden.py from the reference's own C (compiled into oracle/_ref).
 Routines pinned (reference file:line):
   prefill_*        attention_head_flash   tensor.c:286-332 (key padding as -1e9)
   head_flash_mask  attention_head_flash   tensor.c:286-332 (general additive mask)
-  head_mask        attention_head         tensor.c:255-282
+  head_mask        attention_head         tensor.c:255-282 (and head_mask_scores: the
+                   softmaxed score matrix it leaves in scores_buf, tensor.c:266-277)
   decode_*         decoder_self_attn_cached decoder.c:48-99, reorder by copy main.c:481-482
   cross_*          decoder_cross_attn_cached decoder.c:103-152
   pen_*            apply_repetition_penalty + apply_no_repeat_ngram main.c:186-213

@@ -30,7 +30,8 @@ def main() -> None:
         out[name] = po.ref_prefill_flash(q, k, v, vl)
     Q, K, V, mask = cases.head_mask_case()
     out["head_flash_mask"] = po.ref_attention_head(Q, K, V, mask, flash=True)
-    out["head_mask"] = po.ref_attention_head(Q, K, V, mask, flash=False)
+    out["head_mask"], out["head_mask_scores"] = po.ref_attention_head(Q, K, V, mask, flash=False,
+                                                                      return_scores=True)
     for name, steps in cases.DECODE_CASES.items():
         q, k, v, parents = cases.decode_case(name)
         full = po.ref_decode_sweep(q, k, v, parents)

@@ -130,6 +130,8 @@ def test_dropins_match_reference_single_head(cuda_device):
     scratch = np.zeros((Q.shape[0], Q.shape[0]), np.float32)
     assert na.attention_head(Q, K, V, mask, out2, scratch, Q.shape[0]) == na.OK
     assert_attn_close(out2, g["head_mask"], "attention_head")
+    # the softmaxed scores the reference leaves in scores_buf (tensor.c:258-277)
+    assert_attn_close(scratch, g["head_mask_scores"], "attention_head scores_buf")
     out3 = np.zeros_like(Q)
     assert na.attention_head_flash(Q, K, V, None, out3, Q.shape[0]) == na.OK
     assert_attn_close(out3, po.attention_head_flash(Q, K, V, None), "no mask")

@@ -121,3 +121,13 @@ def test_linear_restatement_matches_reference(golden, name):
     err = np.abs(golden[name].astype(np.float64) - y)
     bound = 2e-6 * (terms + 1.0) + 1e-6 * np.abs(y)
     assert (err <= bound).all(), f"{name}: max err {err.max():.3e}, worst ratio {(err / bound).max():.2f}"
+
+
+def test_head_scores_golden_is_a_softmax(golden):
+    """The reference's scores_buf after attention_head: each row the softmax of
+    q.k/8 + mask (float64 restatement within fp32 rounding)."""
+    Q, K, V, mask = cases.head_mask_case()
+    s = (Q.astype(np.float64) @ K.astype(np.float64).T) * 0.125 + mask
+    s = np.exp(s - s.max(axis=1, keepdims=True))
+    s /= s.sum(axis=1, keepdims=True)
+    np.testing.assert_allclose(golden["head_mask_scores"], s, atol=2e-6, rtol=1e-5)
