@@ -197,6 +197,7 @@ struct Lin {
     void* wb = nullptr;  // fp16 copy of w (exact), operand of the TMA-fed tensor-core kernel
     CUtensorMap tm{};    // tensor map of wb: [out][in], box 64 x 128, 128-byte swizzle
     CUtensorMap tm256{}; // the same, box 32 x 256, 64-byte swizzle (persistent kernel)
+    CUtensorMap tm_pair{};  // the same, box 32 x 128, 64-byte swizzle (persistent kernel on CTA pairs)
 };
 
 }  // namespace
@@ -354,6 +355,7 @@ struct Loader {
         ENG_CK(launch_int8_to_f16(L->w, wb, (size_t)L->out * L->in, m->stream));
         ENG_CK(encode_half_map(&L->tm, wb, L->in, L->out, 1));
         ENG_CK(encode_half_maps_persistent(nullptr, nullptr, L->in, 0, &L->tm256, wb, L->out));
+        ENG_CK(encode_half_map_pair(&L->tm_pair, wb, L->in, L->out));
         L->wb = wb;
         return NLLB_ATTN_OK;
     }
@@ -580,7 +582,8 @@ int run_linear(nllb_model* m, const Lin& L, const float* x, int M, float* out, c
         const double flops = 2.0 * M * L.out * L.in;
         if (pers) {
             ProfScope ps(m, 0, flops, (double)L.out * L.in * 2);
-            ENG_CK(launch_linear_tma_persistent(a, &it->second, &L.tm256, m->num_sms, m->attn->err, m->stream));
+            ENG_CK(launch_linear_tma_persistent(a, &it->second, &L.tm256, &L.tm_pair, m->num_sms, m->attn->err,
+                                                m->stream));
         } else {
             ProfScope ps(m, 1, flops, (double)L.out * L.in * 2);
             ENG_CK(launch_linear_tma(a, &it->second, &L.tm, linear_tma_splits(M, L.out, L.in, m->num_sms),

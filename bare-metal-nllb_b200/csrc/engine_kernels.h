@@ -64,8 +64,13 @@ int linear_tma_splits(int M, int N, int K, int num_sms);
 bool linear_tma_use_persistent(int M, int N, int K, int num_sms);
 cudaError_t encode_half_maps_persistent(CUtensorMap* x_map, const void* planes, int K, int M, CUtensorMap* w_map,
                                         const void* wb, int N);
+// From 129 rows the launch runs 256 x 256 tiles on CTA pairs (cta_group::2)
+// when tw_pair is given: the weight's map with box 32 x 128 (64-byte swizzle,
+// encode_half_map_pair); the planes map is the same.
+bool linear_tma_use_pair(int M);
+cudaError_t encode_half_map_pair(CUtensorMap* map, const void* wb, int K, int N);
 cudaError_t launch_linear_tma_persistent(const LinearArgs& a, const CUtensorMap* tx, const CUtensorMap* tw,
-                                         int num_sms, int* err, cudaStream_t st);
+                                         const CUtensorMap* tw_pair, int num_sms, int* err, cudaStream_t st);
 cudaError_t launch_split_planes(const float* x, int ldx, int M, int K, void* planes, cudaStream_t st);
 cudaError_t launch_int8_to_f16(const int8_t* w, void* out, size_t n, cudaStream_t st);
 cudaError_t launch_linear_tma(const LinearArgs& a, const CUtensorMap* tx, const CUtensorMap* tw, int splits, int* err,

@@ -31,6 +31,7 @@ struct nllb_linear {
     void* wb = nullptr;       // [N][K] fp16
     CUtensorMap tm{};         // of wb, box 64 x 128 (split-K kernel)
     CUtensorMap tm256{};      // of wb, box 32 x 256 (persistent kernel)
+    CUtensorMap tm_pair{};    // of wb, box 32 x 128 (persistent kernel on CTA pairs)
     void* planes = nullptr;   // [2][M][K] fp16, grow-only
     size_t planes_elems = 0;
     int map_rows = -1;        // rows the plane maps were encoded for
@@ -93,7 +94,8 @@ int nllb_linear_prepare(const int8_t* w, const float* weight_scale, const float*
     if (launch_int8_to_f16(w, L->wb, (size_t)N * K, st) != cudaSuccess)
         return fail(nllb::set_error(NLLB_ATTN_ECUDA, "weight conversion launch failed"));
     if (encode_half_map(&L->tm, L->wb, K, N, 1) != cudaSuccess ||
-        encode_half_maps_persistent(nullptr, nullptr, K, 0, &L->tm256, L->wb, N) != cudaSuccess)
+        encode_half_maps_persistent(nullptr, nullptr, K, 0, &L->tm256, L->wb, N) != cudaSuccess ||
+        encode_half_map_pair(&L->tm_pair, L->wb, K, N) != cudaSuccess)
         return fail(nllb::set_error(NLLB_ATTN_ECUDA, "cuTensorMapEncodeTiled failed for the weight"));
     *out = L;
     return NLLB_ATTN_OK;
@@ -146,7 +148,7 @@ int nllb_linear_run(nllb_linear* L, const float* x, int M, float* out, const flo
     }
     LP_CK(launch_split_planes(x, L->K, M, L->K, L->planes, st));
     if (linear_tma_use_persistent(M, L->N, L->K, L->num_sms))
-        LP_CK(launch_linear_tma_persistent(a, &L->tx_pers, &L->tm256, L->num_sms, L->err, st));
+        LP_CK(launch_linear_tma_persistent(a, &L->tx_pers, &L->tm256, &L->tm_pair, L->num_sms, L->err, st));
     else
         LP_CK(launch_linear_tma(a, &L->tx, &L->tm, linear_tma_splits(M, L->N, L->K, L->num_sms), L->err, st));
     return NLLB_ATTN_OK;

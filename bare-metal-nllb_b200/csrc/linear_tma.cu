@@ -18,6 +18,10 @@
 // rank order (distributed shared memory; deterministic; no workspace).
 // Grid x = (row tile, split) fastest, so the row tiles that share a weight
 // tile run together and the weight tile is read from DRAM once.
+//
+// Larger outputs take a persistent kernel over 128 x 256 tiles (one CTA per
+// SM), or from 129 rows its pair form: 256 x 256 tiles on two-CTA clusters
+// with tcgen05.mma.cta_group::2, each CTA loading half of the weight tile.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
@@ -360,6 +364,48 @@ __device__ __forceinline__ bool warp_wait_bounded(uint64_t* bar, uint32_t parity
     return __all_sync(0xffffffffu, ok);
 }
 
+// Epilogue of one 128 x 256 accumulator by one warp: TMEM lanes of rows
+// mrow..mrow+31 (taddr: the warp's lane quarter and the accumulator's first
+// column), columns n0 + half*128 .. +127, 32 at a time: TMEM -> registers ->
+// the warp's transpose buffer (32 x BUF_LD floats) -> stores of 32
+// consecutive columns per row, with the per-column factors loaded once.
+__device__ __forceinline__ void drain_tile_256(const LinearArgs& a, uint32_t taddr, float* buf, int lane, int half,
+                                               int mrow, int n0) {
+    constexpr int BUF_LD = pers::BUF_LD;
+#pragma unroll 1
+    for (int ch = 0; ch < 4; ++ch) {
+        const int col0 = half * 128 + ch * 32;
+        float v[32];
+        tmem_ld32(taddr + (uint32_t)col0, v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) buf[lane * BUF_LD + j] = v[j];
+        __syncwarp();
+        // lane = column: per-column factors once, then one row per store
+        const int n = n0 + col0 + lane;
+        const bool nok = n < a.N;
+        const float inv = nok ? 1.0f / a.scale[n] : 0.f;  // 1/scale as tensor.c:75
+        const float bias = (nok && a.bias) ? a.bias[n] : 0.f;
+        const bool masked = a.mask_from >= 0 && n >= a.mask_from;
+        const size_t colbase = nok ? (size_t)(n / a.cblock) * ((size_t)a.M * a.cblock) + (size_t)(n % a.cblock) : 0;
+        const int rows = min(32, a.M - mrow);
+        if (nok) {
+            for (int r = 0; r < rows; ++r) {
+                float y = buf[r * BUF_LD + lane] * inv;
+                if (a.bias) y += bias;
+                if (a.relu) y = fmaxf(y, 0.f);
+                if (masked) y = -1e30f;
+                const size_t o = colbase + (size_t)(mrow + r) * a.cblock;
+                if (a.residual) y += a.residual[o];
+                if (a.out_planes)
+                    store_planes_x1(static_cast<plane_t*>(a.out_planes), (size_t)a.M * a.N, o, y);
+                else
+                    a.out[o] = y;
+            }
+        }
+        __syncwarp();
+    }
+}
+
 __global__ void __launch_bounds__(pers::THREADS, 1)
     linear_tma_persistent_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw,
                                  const LinearArgs a, int* err) {
@@ -490,40 +536,8 @@ __global__ void __launch_bounds__(pers::THREADS, 1)
                 break;
             }
             tc_fence_after();
-            const int mrow = (t % MT) * TM + quarter * 32, n0 = (t / MT) * TN;
-#pragma unroll 1
-            for (int ch = 0; ch < 4; ++ch) {
-                const int col0 = half * 128 + ch * 32;
-                float v[32];
-                tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + acc * TN + (uint32_t)col0, v);
-#pragma unroll
-                for (int j = 0; j < 32; ++j) buf[lane * BUF_LD + j] = v[j];
-                __syncwarp();
-                // lane = column: per-column factors once, then one row per store
-                const int n = n0 + col0 + lane;
-                const bool nok = n < a.N;
-                const float inv = nok ? 1.0f / a.scale[n] : 0.f;  // 1/scale as tensor.c:75
-                const float bias = (nok && a.bias) ? a.bias[n] : 0.f;
-                const bool masked = a.mask_from >= 0 && n >= a.mask_from;
-                const size_t colbase =
-                    nok ? (size_t)(n / a.cblock) * ((size_t)a.M * a.cblock) + (size_t)(n % a.cblock) : 0;
-                const int rows = min(32, a.M - mrow);
-                if (nok) {
-                    for (int r = 0; r < rows; ++r) {
-                        float y = buf[r * BUF_LD + lane] * inv;
-                        if (a.bias) y += bias;
-                        if (a.relu) y = fmaxf(y, 0.f);
-                        if (masked) y = -1e30f;
-                        const size_t o = colbase + (size_t)(mrow + r) * a.cblock;
-                        if (a.residual) y += a.residual[o];
-                        if (a.out_planes)
-                            store_planes_x1(static_cast<plane_t*>(a.out_planes), (size_t)a.M * a.N, o, y);
-                        else
-                            a.out[o] = y;
-                    }
-                }
-                __syncwarp();
-            }
+            drain_tile_256(a, tmem + ((uint32_t)(quarter * 32) << 16) + acc * TN, buf, lane, half,
+                           (t % MT) * TM + quarter * 32, (t / MT) * TN);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -534,6 +548,229 @@ __global__ void __launch_bounds__(pers::THREADS, 1)
     if (warp == 0) {
         tc_fence_after();
         tmem_dealloc(tmem, TMEM_COLS);
+    }
+    if (tid == 0 && *s_abort) atomicOr(err, NLLB_DEV_ERR_TIMEOUT);
+}
+
+// ---------------------------------------------------------------------------
+// Pair form of the persistent kernel: 256 x 256 output tiles, each run by a
+// cluster of two CTAs on two SMs with tcgen05.mma.cta_group::2.  CTA r of the
+// pair loads rows [128r, 128r + 128) of the tile's activation planes and
+// weight rows (output columns) [128r, 128r + 128) of its 256, 24 KB per
+// 32-wide K chunk instead of the 32 KB of the one-CTA form, where both row
+// halves of a 256-column weight tile read all of it; each CTA's TMEM holds
+// its 128 output rows x 256 columns.  CTA 0 issues the MMAs of both: every
+// TMA load of the pair completes on CTA 0's `full` barrier (loads in the
+// cta_group::2 form, each into its own CTA's shared memory), every MMA batch
+// commits to the `empty` and accumulator-ready barriers of both CTAs, and the
+// epilogue warps of both arrive on CTA 0's accumulator-free barrier.  The
+// roles, stage ring and double-buffered accumulators are the one-CTA form's.
+// ---------------------------------------------------------------------------
+namespace pair {
+constexpr int TM = 128, TN = 256, TK = 32, STAGES = 7;  // TM: rows per CTA, 256 per pair
+constexpr int EPI_WARPS = 8, THREADS = (EPI_WARPS + 2) * 32;
+constexpr uint32_t A_PLANE = TM * TK * 2;                      // 8 KB
+constexpr uint32_t B_HALF = (TN / 2) * TK * 2;                 // 8 KB: this CTA's half of the weight tile
+constexpr uint32_t W_OFF = kPlanes * A_PLANE;
+constexpr uint32_t STAGE_BYTES = kPlanes * A_PLANE + B_HALF;   // 24 KB per CTA
+constexpr uint32_t SMEM_EPI = STAGES * STAGE_BYTES;
+constexpr uint32_t SMEM_BAR = SMEM_EPI + EPI_WARPS * 32 * pers::BUF_LD * 4;
+constexpr uint32_t SMEM_TOTAL = SMEM_BAR + 256 + 1024;
+constexpr uint32_t TMEM_COLS = 512;
+static_assert(SMEM_TOTAL <= 232448, "fits the 227 KB of shared memory a CTA may use");
+}  // namespace pair
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void mma_f16_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+// One arrival on `bar` in each CTA of the pair once the MMAs issued so far are done.
+__device__ __forceinline__ void tc_commit_pair(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"((uint16_t)3)
+        : "memory");
+}
+// TMA loads into this CTA's shared memory that complete on the barrier at
+// cluster address `bar` (CTA 0's).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+        "%3}], [%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map, int x, int y, int z,
+                                                 uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+        "%3, %4}], [%5];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t bar) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::THREADS, 1)
+    linear_tma_pair_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw,
+                           const LinearArgs a, int* err) {
+    constexpr int TM = pair::TM, TN = pair::TN, TK = pair::TK, STAGES = pair::STAGES, EPI_WARPS = pair::EPI_WARPS;
+    constexpr int BUF_LD = pers::BUF_LD;
+    constexpr uint32_t A_PLANE = pair::A_PLANE, STAGE_BYTES = pair::STAGE_BYTES, SMEM_EPI = pair::SMEM_EPI;
+    constexpr uint32_t W_OFF = pair::W_OFF;
+    constexpr uint32_t SMEM_BAR = pair::SMEM_BAR, TMEM_COLS = pair::TMEM_COLS;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base_addr = (raw + 1023u) & ~1023u;  // the same offset in both CTAs (same kernel, same layout)
+    unsigned char* base = smem_raw + (base_addr - raw);
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + SMEM_BAR);  // used in CTA 0
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;  // used in CTA 0
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int MT = (a.M + 2 * TM - 1) / (2 * TM), NT = (a.N + TN - 1) / TN;
+    const int tiles = MT * NT, nk = a.K / TK;
+    const int pair_id = (int)blockIdx.x >> 1, npairs = (int)gridDim.x >> 1;
+
+    if (warp == 0) tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    if (tid == 32) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 2 * EPI_WARPS);
+        }
+        *s_abort = 0;
+        fence_barrier_init();
+    }
+    pdl_launch_dependents();
+    tc_fence_before();
+    cluster_sync_all();  // both CTAs' barriers exist before the first load or arrival from the partner
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    if (!(warp == 0 && lane == 0)) pdl_wait_primary();  // the output may still be read by earlier kernels
+
+    if (warp == 0) {
+        if (lane == 0) {  // ---- TMA producer (both CTAs)
+            prefetch_tensormap(&tx);
+            prefetch_tensormap(&tw);
+            const uint32_t full0 = map_rank(full, 0);  // CTA 0's full[s] at full0 + 8 s
+            const int pre = pair_id < tiles ? (nk < STAGES ? nk : STAGES) : 0;
+            if (a.static_weights) {
+                const int wrow = (pair_id / MT) * TN + (int)rank * (TN / 2);
+                for (int c = 0; c < pre; ++c) {
+                    if (rank == 0) mbar_arrive_expect_tx(&full[c], 2 * STAGE_BYTES);
+                    tma_load_2d_pair(base + c * STAGE_BYTES + W_OFF, &tw, c * TK, wrow, full0 + 8u * c);
+                }
+            }
+            pdl_wait_primary();
+            uint32_t g = 0;
+            for (int t = pair_id; t < tiles && !*s_abort; t += npairs) {
+                const int m0 = (t % MT) * (2 * TM) + (int)rank * TM, n0 = (t / MT) * TN + (int)rank * (TN / 2);
+                for (int c = 0; c < nk; ++c, ++g) {
+                    const uint32_t s = g % STAGES, use = g / STAGES;
+                    unsigned char* st = base + s * STAGE_BYTES;
+                    if ((int)g < pre) {  // fresh stage of the first tile
+                        if (!a.static_weights) {
+                            if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * STAGE_BYTES);
+                            tma_load_2d_pair(st + W_OFF, &tw, c * TK, n0, full0 + 8u * s);
+                        }
+                        tma_load_3d_pair(st, &tx, c * TK, m0, 0, full0 + 8u * s);  // box 32 x 128 x 2
+                        continue;
+                    }
+                    if (!mbar_wait_bounded(&empty[s], (use & 1u) ^ 1u)) {
+                        *s_abort = 1;
+                        break;
+                    }
+                    if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * STAGE_BYTES);
+                    tma_load_3d_pair(st, &tx, c * TK, m0, 0, full0 + 8u * s);
+                    tma_load_2d_pair(st + W_OFF, &tw, c * TK, n0, full0 + 8u * s);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {  // ---- MMA issuer for the pair (CTA 0)
+            constexpr uint32_t idesc = idesc_f16(2 * TM, TN);
+            uint32_t g = 0, i = 0;
+            for (int t = pair_id; t < tiles && !*s_abort; t += npairs, ++i) {
+                const uint32_t acc = i & 1u;
+                if (!mbar_wait_bounded(&tempty[acc], ((i >> 1) & 1u) ^ 1u)) {
+                    *s_abort = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem + acc * TN;
+                bool ok = true;
+                for (int c = 0; c < nk; ++c, ++g) {
+                    const uint32_t s = g % STAGES, use = g / STAGES;
+                    if (!mbar_wait_bounded(&full[s], use & 1u)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = base_addr + s * STAGE_BYTES;
+#pragma unroll
+                    for (int ks = 0; ks < TK / 16; ++ks) {
+                        const uint64_t bw = umma_desc_k_sw64(sa + W_OFF + ks * 32);
+                        mma_f16_pair(d, umma_desc_k_sw64(sa + 0 * A_PLANE + ks * 32), bw, idesc,
+                                     (c > 0 || ks > 0) ? 1u : 0u);
+                        mma_f16_pair(d, umma_desc_k_sw64(sa + 1 * A_PLANE + ks * 32), bw, idesc, 1u);
+                    }
+                    tc_commit_pair(&empty[s]);
+                }
+                if (!ok) {
+                    *s_abort = 1;
+                    break;
+                }
+                tc_commit_pair(&tfull[acc]);
+            }
+        }
+    } else {  // ---- epilogue warps 2-9 (both CTAs): lane quarter warp % 4, column half (warp - 2) / 4
+        const int quarter = warp & 3, half = (warp - 2) >> 2;
+        float* buf = reinterpret_cast<float*>(base + SMEM_EPI) + (warp - 2) * 32 * BUF_LD;
+        const uint32_t tempty0 = map_rank(tempty, 0);
+        uint32_t i = 0;
+        for (int t = pair_id; t < tiles; t += npairs, ++i) {
+            const uint32_t acc = i & 1u;
+            const bool go = __all_sync(0xffffffffu, *s_abort == 0);  // warp-uniform
+            if (!go || !warp_wait_bounded(&tfull[acc], (i >> 1) & 1u)) {
+                *s_abort = 1;
+                break;
+            }
+            tc_fence_after();
+            drain_tile_256(a, tmem + ((uint32_t)(quarter * 32) << 16) + acc * TN, buf, lane, half,
+                           (t % MT) * (2 * TM) + (int)rank * TM + quarter * 32, (t / MT) * TN);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(tempty0 + 8u * acc);
+        }
+    }
+    __syncwarp();
+    tc_fence_before();
+    cluster_sync_all();  // neither CTA leaves while its partner may still use its barriers or TMEM
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, TMEM_COLS);
     }
     if (tid == 0 && *s_abort) atomicOr(err, NLLB_DEV_ERR_TIMEOUT);
 }
@@ -566,6 +803,9 @@ cudaError_t configure_linear_tma() {
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(linear_tma_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)pers::SMEM_TOTAL);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(linear_tma_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)pair::SMEM_TOTAL);
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(linear_tma_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
 }
@@ -624,13 +864,56 @@ bool linear_tma_use_persistent(int M, int N, int K, int num_sms) {
     return tiles * 148 >= 80LL * num_sms;
 }
 
+// CTA pairs of the pair kernel that can be resident at once on the current
+// device (both CTAs of a cluster sit in one GPC), queried once per device;
+// 0 if the query fails.
+int pair_capacity() {
+    static std::mutex mu;
+    static int cap[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    std::lock_guard<std::mutex> lock(mu);
+    if (cap[dev] == 0) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2, 1, 1);
+        cfg.blockDim = dim3(pair::THREADS, 1, 1);
+        cfg.dynamicSmemBytes = pair::SMEM_TOTAL;  // cluster shape: the kernel's own __cluster_dims__
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, linear_tma_pair_kernel, &cfg) != cudaSuccess || n < 1) {
+            cudaGetLastError();  // clear
+            n = -1;
+        }
+        cap[dev] = n;
+    }
+    return cap[dev] > 0 ? cap[dev] : 0;
+}
+
+// The pair kernel takes the persistent kernel's shapes from NLLB_PAIR_MIN_ROWS
+// rows up: below that a 256-row pair tile would be mostly rows past M.
+#ifndef NLLB_PAIR_MIN_ROWS
+#define NLLB_PAIR_MIN_ROWS 129
+#endif
+bool linear_tma_use_pair(int M) { return M >= NLLB_PAIR_MIN_ROWS && pair_capacity() > 0; }
+
 cudaError_t launch_linear_tma_persistent(const LinearArgs& a, const CUtensorMap* tx, const CUtensorMap* tw,
-                                         int num_sms, int* err, cudaStream_t st) {
+                                         const CUtensorMap* tw_pair, int num_sms, int* err, cudaStream_t st) {
+    if (tw_pair && linear_tma_use_pair(a.M)) {
+        const int tiles = ((a.M + 2 * pair::TM - 1) / (2 * pair::TM)) * ((a.N + pair::TN - 1) / pair::TN);
+        const int cap = pair_capacity();
+        const int pairs = tiles < cap ? tiles : cap;
+        if (pairs < 1) return cudaSuccess;
+        return launch_pdl(linear_tma_pair_kernel, dim3(2 * pairs), dim3(pair::THREADS), pair::SMEM_TOTAL, st, *tx,
+                          *tw_pair, a, err);
+    }
     const int tiles = ((a.M + pers::TM - 1) / pers::TM) * ((a.N + pers::TN - 1) / pers::TN);
     const int grid = tiles < num_sms ? tiles : num_sms;
     if (grid < 1) return cudaSuccess;
     return launch_pdl(linear_tma_persistent_kernel, dim3(grid), dim3(pers::THREADS), pers::SMEM_TOTAL, st, *tx, *tw, a,
                       err);
+}
+
+cudaError_t encode_half_map_pair(CUtensorMap* map, const void* wb, int K, int N) {
+    return encode_half_map_box(map, wb, K, N, 1, pair::TK, pair::TN / 2);
 }
 
 // Clusters of S CTAs of the split-K kernel that can be resident at once on the

@@ -145,8 +145,8 @@ def parse_args():
     ap.add_argument("--translate-sentences", type=int, default=1024,
                     help="sentences of the sentence-batched translation")
     ap.add_argument("--no-sweep", action="store_true", help="skip the decode-attention sweep")
-    ap.add_argument("--ncu-case", choices=("decode", "decode1", "cross", "cross128", "prefill", "linear", "translate",
-                                           "topk"),
+    ap.add_argument("--ncu-case", choices=("decode", "decode1", "cross", "cross128", "prefill", "linear", "linear512",
+                                           "translate", "topk"),
                     help="run one small fixed case for an ncu capture and exit")
     return ap.parse_args()
 
@@ -834,6 +834,21 @@ def ncu_case(which: str) -> None:
                 torch.cuda.synchronize()
                 assert lin.status() == 0
         print("ncu case linear: ok")
+        return
+    elif which == "linear512":
+        # the decoder's linear layers at 512 rows (a step of 128 sentences x 4 beams, the
+        # per-GPU share of config 4 on 8 GPUs): 1024 -> 3072 (q/k/v), 1024 -> 1024 (output),
+        # 1024 -> 4096 (fc1), 4096 -> 1024 (fc2); 3 launches each
+        for n_in, n_out in ((1024, 3072), (1024, 1024), (1024, 4096), (4096, 1024)):
+            x = torch.randn((512, n_in), generator=g, device=dev)
+            w = torch.randint(-127, 128, (n_out, n_in), generator=g, device=dev, dtype=torch.int8)
+            sc = torch.full((n_out,), 3666.19, device=dev)
+            with na.PreparedLinear(w, sc) as lin:
+                for _ in range(3):
+                    lin(x)
+                torch.cuda.synchronize()
+                assert lin.status() == 0
+        print("ncu case linear512: ok")
         return
     elif which == "translate":
         # the translation engine on 64 sentences of config 4's workload, 40 target tokens at most

@@ -7,7 +7,8 @@ Checked against a float64 evaluation of mat_vec_int8's arithmetic
 then relu and the residual.  Tolerance: fp32 accumulation error relative to
 the sum of |terms|, as for nllb_linear_int8.  The shapes reach every split-K
 depth of the cluster reduction (1, 2, 4, 8 CTAs per tile), the persistent
-128 x 256-tile kernel (outputs with at least one such tile per SM), row
+128 x 256-tile kernel (outputs with at least one such tile per SM) and its
+256 x 256-tile form on CTA pairs (tcgen05.mma.cta_group::2, from 129 rows), row
 counts that are not multiples of the 128-row tile, output counts that are
 not multiples of the tile or of 4 (the scalar store path), and the full
 vocabulary projection.
@@ -59,9 +60,17 @@ def _dev(a, device):
     (1024, 4096, 1024, "bias_relu"),   # 2 CTAs per tile
     (2048, 4096, 1024, "plain"),       # no split (plain launch, no cluster)
     (2048, 1024, 1024, "residual"),    # no split, K = 1024
-    # persistent kernel (at least 80 tiles of 128 x 256)
+    # split-K kernel at the decoder's small-batch shapes
+    (512, 1024, 3072, "bias_relu"),    # q/k/v projection of 128 sentences x 4 beams
+    (200, 1024, 4096, "residual"),     # fc1 shape, M tail
+    (77, 4096, 1000, "plain"),         # fc2-like (K = 4096), N tail
+    (512, 1024, 2050, "residual"),     # N % 4 != 0 (scalar stores)
+    # persistent kernel (at least 80 tiles of 128 x 256); from 129 rows on CTA pairs
+    # (256 x 256 tiles, tcgen05.mma.cta_group::2)
     (4100, 1024, 4096, "bias_relu"),   # M tail
-    (40, 1024, 256206, "plain"),       # vocabulary projection shape, N tail
+    (40, 1024, 256206, "plain"),       # vocabulary projection shape, N tail (one-CTA form)
+    (129, 1024, 24000, "bias_relu"),   # pair: the second CTA of each pair has one row
+    (200, 1024, 20000, "residual"),    # pair: M tail inside the second CTA
     (2000, 1024, 3001, "residual"),    # M and N tails, N % 4 != 0
     (1100, 4096, 3072, "bias_relu"),   # K = 4096
 ])

@@ -13,7 +13,7 @@ ulp, so such a step may resolve either way under other rounding).
 
 Cases: config 0 (one 16-token sentence, 32 tokens), three hand-picked
 config-4-shaped sentences, and the first 32 sentences of the sentence-batched
-workload (seed 4) translated as one batch.
+workload (seed 4) translated as one batch, and twice over in one batch of 64.
 """
 import json
 import os
@@ -35,7 +35,7 @@ N_CFG4 = GOLDEN["cfg4_first"]
 @pytest.fixture(scope="module")
 def model(cuda_device):
     sm.ensure_model(MODEL_PATH, seed=GOLDEN["model"]["seed"])
-    with na.Model(MODEL_PATH, device=0, max_sentences=N_CFG4, max_src=256, max_gen=132) as m:
+    with na.Model(MODEL_PATH, device=0, max_sentences=2 * N_CFG4, max_src=256, max_gen=132) as m:
         yield m
 
 
@@ -106,6 +106,21 @@ def test_sentence_batched_workload_matches_reference(model, capsys):
     assert st.tokens_out == sum(len(t) for t in toks)
 
 
+def test_reference_sentences_in_a_larger_batch(model):
+    """The 32 reference sentences followed by the same 32 again: 256 beam rows,
+    so the vocabulary projection runs on CTA pairs as well as the encoder's
+    layers.  Both copies of every sentence must equal the reference output
+    (or differ only after a reference near-tie), and each other."""
+    names = [f"cfg4_s{i:02d}" for i in range(N_CFG4)]
+    srcs = [GOLDEN["cases"][n]["src"] for n in names]
+    toks, scores, st = model.translate(srcs + srcs, GOLDEN["tgt_lang_id"], max_gen=132)
+    for i, n in enumerate(names):
+        check_against_reference(toks[i], GOLDEN["cases"][n], n)
+        check_against_reference(toks[N_CFG4 + i], GOLDEN["cases"][n], n + " (second copy)")
+        assert toks[i] == toks[N_CFG4 + i], f"{n}: the two copies differ"
+    assert st.tokens_out == sum(len(t) for t in toks)
+
+
 def test_batching_is_transparent(model):
     """A sentence alone and inside a batch decodes the same way."""
     a = GOLDEN["cases"]["cfg4_len16"]["src"]
@@ -134,7 +149,7 @@ def test_translate_argument_errors(model):
         model.translate([[256047] * 300], GOLDEN["tgt_lang_id"])
     assert ei.value.status == na.ECAPACITY
     with pytest.raises(na.NllbAttnError) as ei:
-        model.translate([[256047, 5, 2]] * (N_CFG4 + 1), GOLDEN["tgt_lang_id"])
+        model.translate([[256047, 5, 2]] * (2 * N_CFG4 + 1), GOLDEN["tgt_lang_id"])
     assert ei.value.status == na.ECAPACITY
     with pytest.raises(na.NllbAttnError) as ei:
         model.translate([[256047, 999999, 2]], GOLDEN["tgt_lang_id"])
