@@ -36,7 +36,10 @@ namespace nllb {
 
 namespace {
 
-constexpr int TM = 128, TN = 128, TK = 64, STAGES = 3;
+#ifndef NLLB_SPLIT_STAGES
+#define NLLB_SPLIT_STAGES 3
+#endif
+constexpr int TM = 128, TN = 128, TK = 64, STAGES = NLLB_SPLIT_STAGES;
 constexpr int EPI_WARPS = 8, THREADS = (EPI_WARPS + 2) * 32;
 constexpr uint32_t PLANE = TM * TK * 2;                 // 16 KB
 constexpr uint32_t W_OFF = kPlanes * PLANE;             // the weight tile follows the X planes
@@ -45,6 +48,10 @@ constexpr uint32_t SMEM_BAR = STAGES * STAGE_BYTES;
 constexpr uint32_t SMEM_TOTAL = SMEM_BAR + 128 + 1024;
 constexpr uint32_t TMEM_COLS = 128;
 constexpr int PART_STRIDE = TN + 4;  // floats per row of the partial tile in shared memory
+static_assert(TM * PART_STRIDE * 4 <= SMEM_BAR, "the partial tile overlays the stage ring");
+// dynamic shared memory a launch may take: the 227 KB of a CTA less the static per-column factors
+constexpr uint32_t kSplitSmemMax = 232448 - 2 * TN * 4;
+static_assert(SMEM_TOTAL <= kSplitSmemMax, "fits the 227 KB of shared memory a CTA may use");
 
 // Instruction descriptor, kind::f16: fp32 accumulator, A and B fp16, both K-major.
 __host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
@@ -77,6 +84,17 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
         "[%5];" ::"r"(smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
         : "memory");
+}
+
+// 16-byte asynchronous copy global -> shared (no registers), and its completion
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ __forceinline__ uint32_t dynamic_smem_bytes() {
+    uint32_t r;
+    asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(r));
+    return r;
 }
 
 // y = accumulator / scale[n] (the per-column dequantisation factor of tensor.c:75)
@@ -130,8 +148,26 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const bool producer = warp == EPI_WARPS && lane == 0;
+    // rows [z*R, (z+1)*R) of the tile are finished by this rank
+    const int R = TM / S, r_begin = z * R;
+    const bool vec = (a.cblock % 4 == 0) && ((reinterpret_cast<uintptr_t>(a.out) & 15) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(a.residual) & 15) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(a.bias) & 15) == 0);
+    // The residual rows of this rank's share are copied into shared memory
+    // (behind the stage ring, when the launch gave the room) by the epilogue
+    // warps while the MMAs run, instead of being loaded after them.
+    float* res_s = reinterpret_cast<float*>(base + SMEM_BAR + 128);
+    const bool res_pre = a.residual && vec && a.cblock % TN == 0 && n0 + TN <= a.N &&
+                         (base_addr - raw) + SMEM_BAR + 128 + (uint32_t)R * TN * 4 <= dynamic_smem_bytes();
     if (!producer) {
         pdl_wait_primary();  // the output may still be read by earlier kernels
+        if (res_pre && warp < EPI_WARPS) {
+            const size_t tb = (size_t)(n0 / a.cblock) * ((size_t)a.M * a.cblock) + (n0 % a.cblock);
+            for (int i = tid; i < R * (TN / 4); i += EPI_WARPS * 32) {
+                const int rr = i / (TN / 4), q = i % (TN / 4), m = m0 + r_begin + rr;
+                if (m < a.M) cp_async16(res_s + rr * TN + q * 4, a.residual + tb + (size_t)m * a.cblock + q * 4);
+            }
+        }
         if (tid < TN) s_inv[tid] = (n0 + tid < a.N) ? 1.0f / a.scale[n0 + tid] : 0.f;  // 1/scale as tensor.c:75
         else if (tid < 2 * TN)
             s_bias[tid - TN] = (a.bias && n0 + tid - TN < a.N) ? a.bias[n0 + tid - TN] : 0.f;
@@ -209,6 +245,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
             for (int j = 0; j < 16; ++j) row[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
         }
+        if (res_pre) cp_async_wait_all();  // this thread's residual copies (the barrier below shares them)
     }
     if (S == 1) __syncthreads();
     else cluster_sync_all();
@@ -222,10 +259,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (aborted) {
         if (tid == 0) atomicOr(err, NLLB_DEV_ERR_TIMEOUT);
     } else {
-        const int R = TM / S;
-        const bool vec = (a.cblock % 4 == 0) && ((reinterpret_cast<uintptr_t>(a.out) & 15) == 0) &&
-                         ((reinterpret_cast<uintptr_t>(a.residual) & 15) == 0) &&
-                         ((reinterpret_cast<uintptr_t>(a.bias) & 15) == 0);
         if (vec && a.cblock % TN == 0) {
             // A warp stores one 128-column row as float4s.  THREADS is a
             // multiple of the 32 float4 of a row, so a thread keeps one column
@@ -261,7 +294,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                         }
                     }
                     res[u] = (a.residual && live && full4)
-                                 ? *reinterpret_cast<const float4*>(a.residual + tile_off + (size_t)m * a.cblock)
+                                 ? (res_pre ? *reinterpret_cast<const float4*>(res_s + rr * TN + nl)
+                                            : *reinterpret_cast<const float4*>(a.residual + tile_off +
+                                                                               (size_t)m * a.cblock))
                                  : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
 #pragma unroll
@@ -799,7 +834,8 @@ std::once_flag g_encode_once;
 }  // namespace
 
 cudaError_t configure_linear_tma() {
-    cudaError_t e = cudaFuncSetAttribute(linear_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_TOTAL);
+    cudaError_t e =
+        cudaFuncSetAttribute(linear_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSplitSmemMax);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(linear_tma_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)pers::SMEM_TOTAL);
@@ -982,7 +1018,9 @@ cudaError_t launch_linear_tma(const LinearArgs& a, const CUtensorMap* tx, const 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(mt * splits, nt, 1);
     cfg.blockDim = dim3(THREADS, 1, 1);
-    cfg.dynamicSmemBytes = SMEM_TOTAL;
+    // with a residual: room for this rank's residual rows behind the stage ring, where it fits
+    const uint32_t res_bytes = a.residual ? (uint32_t)(TM / splits) * TN * 4 : 0;
+    cfg.dynamicSmemBytes = SMEM_TOTAL + res_bytes <= kSplitSmemMax ? SMEM_TOTAL + res_bytes : SMEM_TOTAL;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
