@@ -53,18 +53,6 @@ static_assert(TM * PART_STRIDE * 4 <= SMEM_BAR, "the partial tile overlays the s
 constexpr uint32_t kSplitSmemMax = 232448 - 2 * TN * 4;
 static_assert(SMEM_TOTAL <= kSplitSmemMax, "fits the 227 KB of shared memory a CTA may use");
 
-// Instruction descriptor, kind::f16: fp32 accumulator, A and B fp16, both K-major.
-__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
-    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_f16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
-        "l"(a), "l"(b), "r"(idesc), "r"(acc)
-        : "memory");
-}
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
     asm volatile(
@@ -208,7 +196,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
     } else if (warp == EPI_WARPS + 1 && lane == 0) {
         // ---- MMA issuer
-        constexpr uint32_t idesc = idesc_f16(TM, TN);
+        constexpr uint32_t idesc = umma_idesc_f16(TM, TN);
         for (int c = 0; c < nk; ++c) {
             const int s = c % STAGES;
             if (!mbar_wait_bounded(&full[s], (uint32_t)((c / STAGES) & 1))) {
@@ -220,8 +208,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
             for (int ks = 0; ks < TK / 16; ++ks) {
                 const uint64_t bw = umma_desc_k_sw128(st + W_OFF + ks * 32);
-                mma_f16(tmem, umma_desc_k_sw128(st + 0 * PLANE + ks * 32), bw, idesc, (c > 0 || ks > 0) ? 1u : 0u);
-                mma_f16(tmem, umma_desc_k_sw128(st + 1 * PLANE + ks * 32), bw, idesc, 1u);
+                tc_mma_f16(tmem, umma_desc_k_sw128(st + 0 * PLANE + ks * 32), bw, idesc, (c > 0 || ks > 0) ? 1u : 0u);
+                tc_mma_f16(tmem, umma_desc_k_sw128(st + 1 * PLANE + ks * 32), bw, idesc, 1u);
             }
             tc_commit(&empty[s]);
         }
@@ -525,7 +513,7 @@ __global__ void __launch_bounds__(pers::THREADS, 1)
         }
     } else if (warp == 1) {
         if (lane == 0) {  // ---- MMA issuer
-            constexpr uint32_t idesc = idesc_f16(TM, TN);
+            constexpr uint32_t idesc = umma_idesc_f16(TM, TN);
             uint32_t g = 0, i = 0;
             for (int t = blockIdx.x; t < tiles && !*s_abort; t += gridDim.x, ++i) {
                 const uint32_t acc = i & 1u;
@@ -547,8 +535,8 @@ __global__ void __launch_bounds__(pers::THREADS, 1)
 #pragma unroll
                     for (int ks = 0; ks < TK / 16; ++ks) {
                         const uint64_t bw = umma_desc_k_sw64(sa + W_OFF + ks * 32);
-                        mma_f16(d, umma_desc_k_sw64(sa + 0 * A_PLANE + ks * 32), bw, idesc, (c > 0 || ks > 0) ? 1u : 0u);
-                        mma_f16(d, umma_desc_k_sw64(sa + 1 * A_PLANE + ks * 32), bw, idesc, 1u);
+                        tc_mma_f16(d, umma_desc_k_sw64(sa + 0 * A_PLANE + ks * 32), bw, idesc, (c > 0 || ks > 0) ? 1u : 0u);
+                        tc_mma_f16(d, umma_desc_k_sw64(sa + 1 * A_PLANE + ks * 32), bw, idesc, 1u);
                     }
                     tc_commit(&empty[s]);
                 }
@@ -745,7 +733,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::THREADS, 1)
         }
     } else if (warp == 1) {
         if (lane == 0 && rank == 0) {  // ---- MMA issuer for the pair (CTA 0)
-            constexpr uint32_t idesc = idesc_f16(2 * TM, TN);
+            constexpr uint32_t idesc = umma_idesc_f16(2 * TM, TN);
             uint32_t g = 0, i = 0;
             for (int t = pair_id; t < tiles && !*s_abort; t += npairs, ++i) {
                 const uint32_t acc = i & 1u;

@@ -6,25 +6,23 @@
 // prefill_tc_kernel (seq_len 33..256): 5th-generation tensor cores.  One CTA
 //   per (128-query tile, head, sequence) with 8 warps: query row r is TMEM
 //   lane r, owned by two threads (warps w and w+4 reach the same lane quarter)
-//   that take alternate 32-key halves of every 64-key chunk.  Inputs are split while they are staged into
-//   128-byte-swizzled shared memory: hi = x with the low 13 mantissa bits
-//   cleared (exact in tf32), lo = x - hi.  Each product is taken as
-//   hi*hi' + hi*lo' + lo*hi' (3xTF32 on tcgen05.mma kind::tf32, fp32
-//   accumulation in TMEM), which keeps fp32 accuracy.  The softmax is the
-//   reference's two-pass form: all scores of a row sit in TMEM (256 columns),
-//   pass 1 takes the row max, pass 2 forms P = exp(s - max) 64 keys at a time,
-//   stages P (split) and V^T (split) in shared memory and accumulates
-//   O += P.V in TMEM; the row sum is divided out at the end.  Q.K^T runs in
-//   groups of 128 keys (one N=128 MMA group for seq_len <= 128).  The loads of
-//   Q and the first K group are all issued before any is stored, and the V
-//   chunks travel in registers while the score MMAs and softmax run, so a CTA
-//   pays about two DRAM latencies, not one per tile.
+//   that take alternate 32-key halves of every 64 keys.  Q, K and V arrive by
+//   TMA as fp32 and are split into two fp16 parts each (x = hi + lo, hi
+//   rounded to 11 significant bits, lo the rest); every product is taken as hi*hi' + hi*lo' +
+//   lo*hi' on tcgen05.mma kind::f16 with fp32 accumulation in TMEM, which keeps
+//   fp32 accuracy for |q|, |k|, |v| < 65504.  The softmax is the reference's
+//   two-pass form: all scores of a row sit in TMEM (256 columns), pass 1
+//   takes the row max, pass 2 forms P = exp(s - max) per 128-key group
+//   (scaled by 2^15 before its split), stages its parts in shared memory and
+//   accumulates O += P.V in TMEM with V read as an MN-major operand (no
+//   transpose); the row sum is divided out at the end.
 // prefill_ffma_kernel (other lengths): SIMT fp32 flash attention with an
 //   online softmax over 64-key tiles.
 #include <algorithm>
 
 #include "device_common.cuh"
 #include "kernels.h"
+#include "planes.cuh"
 
 namespace nllb {
 
@@ -195,46 +193,110 @@ __global__ void __launch_bounds__(kThreads) prefill_ffma_kernel(const PrefillPar
 // tcgen05 kernel
 // ---------------------------------------------------------------------------
 constexpr int TC_THREADS = 256;  // two threads per query row / TMEM lane
-constexpr int TC_THREADS_SPLIT = TC_THREADS;
-constexpr int TC_Q = 128;      // queries per CTA (MMA M)
-constexpr int TC_KG = 128;     // keys per score group (MMA N of Q.K^T)
-constexpr int TC_K = 64;       // keys per P.V chunk (MMA K of P.V)
-constexpr int TC_MAX_S = 256;  // score columns held in TMEM
+constexpr int TC_Q = 128;        // queries per CTA (MMA M)
+constexpr int TC_KG = 128;       // keys per group: N of the score MMAs, K of a group's P.V MMAs
+constexpr int TC_MAX_S = 256;    // score columns held in TMEM
 constexpr uint32_t TC_TMEM_COLS = 512;
-// shared-memory plan (bytes from a 1024-byte aligned base); every operand is
-// K-major, 128-byte swizzled, in 32-column k-blocks of rows*128 bytes -- the
-// layout a TMA box of [rows][32 fp32] lands in with the 128-byte swizzle
-constexpr uint32_t SQH = 0, SQL = 32768;        // Q hi/lo [2][128 rows][128 B]; P hi/lo after the scores
-constexpr uint32_t SKH = 65536, SKL = 98304;    // K hi/lo [2][128 keys][128 B]
-constexpr uint32_t SVH = 131072, SVL = 147456;  // V^T hi/lo [2][64 dims][128 B]
-constexpr uint32_t SVR = 163840;                // V as loaded: [2][128 keys][128 B] (two P.V chunks)
+// P is scaled by 2^15 before its split so that weights down to ~2e-9 keep
+// both fp16 parts normal; the output is scaled back exactly.
+constexpr float kPScale = 32768.0f, kPUnscale = 1.0f / 32768.0f;
+// Shared-memory plan (bytes from a 1024-byte aligned base).  TMA lands fp32
+// tiles as [rows][32 fp32] boxes (128-byte swizzle); the threads split them
+// into the fp16 MMA operands, K-major with the 128-byte swizzle: rows of 64
+// fp16 (128 B), 8-row atoms 1024 B apart.
+constexpr uint32_t SQF = 0, SKF = 32768;        // Q, K group fp32 staging, 2 boxes each
+constexpr uint32_t SPP = 0;                     // P parts [2][2 k-blocks][128 rows][128 B] over SQF/SKF
+constexpr uint32_t SVF = 65536;                 // V group fp32 staging, 2 boxes
+constexpr uint32_t SQP = 98304;                 // Q parts [2][128 rows][128 B]
+constexpr uint32_t SKP = 131072;                // K group parts [2][128 keys][128 B]
+constexpr uint32_t SVP = 163840;                // V group parts [2][128 keys][128 B] (MN-major B)
 constexpr uint32_t SBAR = 196608;
 constexpr uint32_t TC_SMEM = SBAR + 64 + 1024;  // + alignment slack
 constexpr uint32_t TC_BOX_BYTES = 128 * 128;    // one [128 rows][32 fp32] box
+constexpr uint32_t PART16 = 16384;              // one fp16 part of a [128][64] operand
+constexpr uint32_t P_PART = 32768;              // one fp16 part of P ([128 queries][128 keys])
 
-// byte offset of (row, col) in a K-major SWIZZLE_128B operand of `nrows`
-// rows x 64 fp32 columns: 32-column k-blocks of nrows*128 B, 128-B rows,
-// 16-B chunks XOR-ed with row % 8.
+// byte offset of (row, col) in an fp32 [nrows][64] tile as TMA lands it:
+// 32-column boxes of nrows*128 B, 128-B rows, 16-B chunks XOR-ed with row % 8.
 __device__ __forceinline__ uint32_t sw128_off(int row, int col, int nrows) {
     return (uint32_t)((col >> 5) * nrows * 128 + row * 128 + ((((col & 31) >> 2) ^ (row & 7)) << 4) +
                       ((col & 3) << 2));
 }
 
-// D[128 x N] (+)= A[128 x 64] . B[N x 64]^T with both operands split:
-// Ah.Bh + Ah.Bl + Al.Bh over 8 k-steps of 8 (A has 128 rows, B has N rows).
-template <int N>
-__device__ __forceinline__ void mma_3xtf32(uint32_t d, uint32_t ah, uint32_t al, uint32_t bh, uint32_t bl,
-                                           bool accumulate_first) {
-    constexpr uint32_t idesc = umma_idesc_tf32(128, N);
+// byte offset of the 16-byte chunk holding fp16 elements k .. k+7 (k % 8 == 0)
+// of row `row` in a K-major 128-byte-swizzled fp16 operand of `nrows` rows:
+// 64-element k-blocks of nrows*128 B.
+__device__ __forceinline__ uint32_t sw128_f16_chunk(int row, int k, int nrows) {
+    return (uint32_t)((k >> 6) * nrows * 128 + row * 128 + ((((k & 63) >> 3) ^ (row & 7)) << 4));
+}
+
+// fp32 -> two fp16 parts x = hi + lo, packed in pairs: hi = x rounded to 11
+// significant bits in fp32 (exact in fp16), lo = x - hi (exact in fp32, then
+// rounded to fp16: |x - hi - lo| <= 2^-23 |x| for |x| in fp16's normal
+// range).  Two packed conversions per pair of values instead of six scalar
+// ones: the conversion pipe, not the math, bounds these splits.
+__device__ __forceinline__ float round11(float x) {
+    return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
+}
+__device__ __forceinline__ void split8(const float (&x)[8], uint4& hi, uint4& lo) {
+    uint32_t h[4], l[4];
 #pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-        const uint32_t ao = (ks >> 2) * (128 * 128) + (ks & 3) * 32;
-        const uint32_t bo = (ks >> 2) * (N * 128) + (ks & 3) * 32;
-        const uint64_t dah = umma_desc_k_sw128(ah + ao), dal = umma_desc_k_sw128(al + ao);
-        const uint64_t dbh = umma_desc_k_sw128(bh + bo), dbl = umma_desc_k_sw128(bl + bo);
-        tc_mma_tf32(d, dah, dbh, idesc, (accumulate_first || ks > 0) ? 1u : 0u);
-        tc_mma_tf32(d, dah, dbl, idesc, 1u);
-        tc_mma_tf32(d, dal, dbh, idesc, 1u);
+    for (int i = 0; i < 4; ++i) {
+        const float a = round11(x[2 * i]), b = round11(x[2 * i + 1]);
+        const __half2 hh = __floats2half2_rn(a, b);  // .x (low half) = element 2i
+        const __half2 ll = __floats2half2_rn(x[2 * i] - a, x[2 * i + 1] - b);
+        h[i] = *reinterpret_cast<const uint32_t*>(&hh);
+        l[i] = *reinterpret_cast<const uint32_t*>(&ll);
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// A [128 rows][64 fp32] tile staged by TMA at src -> its two fp16 parts at
+// dst and dst + PART16 ([128 rows][64], 128-byte swizzle: K-major for Q and
+// K, MN-major for V).  Rows >= valid are zero.
+__device__ __forceinline__ void split_rows64(const unsigned char* src, unsigned char* dst, int valid, int tid) {
+#pragma unroll
+    for (int it = 0; it < (128 * 8) / TC_THREADS; ++it) {
+        const int item = tid + it * TC_THREADS;
+        const int row = item >> 3, k = (item & 7) * 8;
+        float x[8];
+        const float4 a = *reinterpret_cast<const float4*>(src + sw128_off(row, k, 128));
+        const float4 b = *reinterpret_cast<const float4*>(src + sw128_off(row, k + 4, 128));
+        x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
+        if (row >= valid) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) x[i] = 0.f;
+        }
+        uint4 hi, lo;
+        split8(x, hi, lo);
+        const uint32_t o = sw128_f16_chunk(row, k, 128);
+        *reinterpret_cast<uint4*>(dst + o) = hi;
+        *reinterpret_cast<uint4*>(dst + PART16 + o) = lo;
+    }
+}
+
+// D[128 x N] (+)= (A0 + A1)[128 x K] . (B0 + B1)^T as A0.B0 + A0.B1 + A1.B0
+// over K / 16 k-steps (fp16 parts, fp32 accumulation; A1.B1 is below the
+// fp32 rounding of the sum).  A is K-major with the 128-byte swizzle: a0
+// addresses the first 64-element k-block of part 0, a_part the distance to
+// part 1, a_kb between k-blocks.  B is either K-major like A ([N rows][K],
+// b_kb between k-blocks) or, with B_MN, MN-major: [K rows][N = 64 elements],
+// one 128-byte swizzled row per k, so a k-step of 16 is 2048 bytes.
+template <int N, int K, bool B_MN>
+__device__ __forceinline__ void mma_2part(uint32_t d, uint32_t a0, uint32_t a_part, uint32_t a_kb, uint32_t b0,
+                                          uint32_t b_part, uint32_t b_kb, bool accumulate_first) {
+    static_assert(!B_MN || N == 64, "an MN-major B operand here is one 64-element row per k");
+    constexpr uint32_t idesc = umma_idesc_f16(128, N) | (B_MN ? (1u << 16) : 0u);  // bit 16: B is MN-major
+#pragma unroll
+    for (int ks = 0; ks < K / 16; ++ks) {
+        const uint32_t ao = (ks >> 2) * a_kb + (ks & 3) * 32;
+        const uint32_t bo = B_MN ? (uint32_t)ks * 2048u : (ks >> 2) * b_kb + (ks & 3) * 32;
+        const uint64_t da0 = umma_desc_k_sw128(a0 + ao), da1 = umma_desc_k_sw128(a0 + a_part + ao);
+        const uint64_t db0 = umma_desc_k_sw128(b0 + bo), db1 = umma_desc_k_sw128(b0 + b_part + bo);
+        tc_mma_f16(d, da0, db0, idesc, (accumulate_first || ks > 0) ? 1u : 0u);
+        tc_mma_f16(d, da0, db1, idesc, 1u);
+        tc_mma_f16(d, da1, db0, idesc, 1u);
     }
 }
 
@@ -263,25 +325,6 @@ __device__ __forceinline__ void tma_rows128(uint32_t dst, const CUtensorMap* map
     tma_load_4d(dst + TC_BOX_BYTES, map, 32, c0, c1, c2, bar);
 }
 
-// In place over `bytes` of loaded fp32 at hi: hi = x with the low 13 mantissa
-// bits cleared (exact in tf32), lo (same offset at lo) = x - hi.
-__device__ __forceinline__ void split_in_place(unsigned char* hi, unsigned char* lo, uint32_t bytes, int tid) {
-    for (uint32_t off = (uint32_t)tid * 16; off < bytes; off += TC_THREADS_SPLIT * 16) {
-        const float4 x = *reinterpret_cast<const float4*>(hi + off);
-        const float4 h = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
-        *reinterpret_cast<float4*>(hi + off) = h;
-        *reinterpret_cast<float4*>(lo + off) = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
-    }
-}
-
-__device__ __forceinline__ void split_store4(unsigned char* hi_base, unsigned char* lo_base, uint32_t off,
-                                             float4 x) {
-    float4 h = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
-    float4 l = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
-    *reinterpret_cast<float4*>(hi_base + off) = h;
-    *reinterpret_cast<float4*>(lo_base + off) = l;
-}
-
 __device__ __forceinline__ float ex2_approx(float x) {  // 2^x, -inf -> +0
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -289,10 +332,13 @@ __device__ __forceinline__ float ex2_approx(float x) {  // 2^x, -inf -> +0
 }
 
 // One CTA per (128-query tile, head, sequence), 8 warps.  Q, K and V tiles
-// arrive by TMA (one thread issues the boxes after the wait on the previous
-// kernel; V for the first 128 keys travels while the scores are computed)
-// in the 128-byte-swizzled K-major layout the MMAs read; the threads then
-// split Q and K in place (hi, lo) and transpose-split V chunk by chunk.
+// arrive by TMA as fp32 (one thread issues the boxes after the wait on the
+// previous kernel); the threads split them into two fp16 parts each, and
+// every product runs as three kind::f16 MMAs with fp32 accumulation in TMEM.
+// Scores go to TMEM in groups of 128 keys (the next group's K loads while a
+// group is split); V's parts are made while the score MMAs run; the softmax
+// is the two-pass form (row max, then P = exp(s - max) per 128-key group,
+// split into parts and accumulated as O += P.V with V an MN-major operand).
 __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const PrefillParams p,
                                                                    const __grid_constant__ CUtensorMap map_q,
                                                                    const __grid_constant__ CUtensorMap map_k,
@@ -303,7 +349,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
     unsigned char* base = smem_raw + (base_addr - raw_addr);
     uint64_t* mma_bar = reinterpret_cast<uint64_t*>(base + SBAR);
     uint64_t* qk_bar = reinterpret_cast<uint64_t*>(base + SBAR + 8);  // Q and K group loads
-    uint64_t* v_bar = reinterpret_cast<uint64_t*>(base + SBAR + 16);  // V loads
+    uint64_t* v_bar = reinterpret_cast<uint64_t*>(base + SBAR + 16);  // V group loads
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + SBAR + 24);
     volatile int* s_abort = reinterpret_cast<volatile int*>(base + SBAR + 32);
     __shared__ float s_red[TC_THREADS];
@@ -360,8 +406,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
         }
         return;
     }
-    const int n_kg = (kv_len + TC_KG - 1) / TC_KG;  // score groups of 128 keys
-    const int n_kc = (kv_len + TC_K - 1) / TC_K;    // P.V chunks of 64 keys
+    const int n_kg = (kv_len + TC_KG - 1) / TC_KG;  // key groups of 128 (at most 2)
     const int rloc = quarter * 32 + lane;           // query row within the tile = TMEM lane
     const int row = q0 + rloc;
     const float* mrow = (p.mask && row < S)
@@ -369,15 +414,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
                             : nullptr;
     const float sl2 = p.scale_log2;
 
-    // Q, K group 0 and V keys 0..127: every box issued at once.  A box counts
-    // its full bytes toward the barrier, rows outside the tensor included
-    // (they arrive as zeros).
+    // Q, K group 0 and V group 0: every box issued at once.  A box counts its
+    // full bytes toward the barrier, rows outside the tensor included (they
+    // arrive as zeros).
     if (tid == 0) {
         mbar_arrive_expect_tx(qk_bar, 4 * TC_BOX_BYTES);
-        tma_rows128(base_addr + SQH, &map_q, p, row0 + q0, h, bq, qk_bar);
-        tma_rows128(base_addr + SKH, &map_k, p, row0, h, bq, qk_bar);
+        tma_rows128(base_addr + SQF, &map_q, p, row0 + q0, h, bq, qk_bar);
+        tma_rows128(base_addr + SKF, &map_k, p, row0, h, bq, qk_bar);
         mbar_arrive_expect_tx(v_bar, 2 * TC_BOX_BYTES);
-        tma_rows128(base_addr + SVR, &map_v, p, row0, h, bq, v_bar);
+        tma_rows128(base_addr + SVF, &map_v, p, row0, h, bq, v_bar);
     }
 
     uint32_t phase = 0, qk_phase = 0, v_phase = 0;         // waits completed per barrier
@@ -404,39 +449,51 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
         }
     };
 
+    // ---- scores S = Q.K^T, group g in TMEM columns [128 g, 128 g + 128)
     bool ok = wait_bar(qk_bar, qk_phase);  // Q and K group 0 have landed
-    if (ok) split_in_place(base + SQH, base + SQL, 2 * TC_BOX_BYTES, tid);
+    if (ok) split_rows64(base + SQF, base + SQP, TC_Q, tid);
     for (int g = 0; g < n_kg && ok; ++g) {
         if (g > 0) {
-            if (!(ok = wait_bar(mma_bar, phase))) break;  // group g-1's MMAs have read KH/KL
-            if (tid == 0) {
-                mbar_arrive_expect_tx(qk_bar, 2 * TC_BOX_BYTES);
-                tma_rows128(base_addr + SKH, &map_k, p, row0 + g * TC_KG, h, bq, qk_bar);
-                ++qk_issued;
-            }
-            if (!(ok = wait_bar(qk_bar, qk_phase))) break;
+            if (!(ok = wait_bar(mma_bar, phase))) break;   // group g-1's MMAs have read the K parts
+            if (!(ok = wait_bar(qk_bar, qk_phase))) break;  // K group g has landed
         }
-        split_in_place(base + SKH, base + SKL, 2 * TC_BOX_BYTES, tid);
+        split_rows64(base + SKF, base + SKP, TC_KG, tid);
         fence_async_smem();
         tc_fence_before();
-        __syncthreads();
+        __syncthreads();  // the parts are visible to the tensor core, the K staging is free
         if (tid == 0) {
+            if (g + 1 < n_kg) {
+                mbar_arrive_expect_tx(qk_bar, 2 * TC_BOX_BYTES);
+                tma_rows128(base_addr + SKF, &map_k, p, row0 + (g + 1) * TC_KG, h, bq, qk_bar);
+                ++qk_issued;
+            }
             tc_fence_after();
-            mma_3xtf32<TC_KG>(tmem + (uint32_t)(g * TC_KG), base_addr + SQH, base_addr + SQL, base_addr + SKH,
-                              base_addr + SKL, false);
+            mma_2part<TC_KG, 64, false>(tmem + (uint32_t)(g * TC_KG), base_addr + SQP, PART16, 0, base_addr + SKP,
+                                        PART16, 0, false);
             tc_commit(mma_bar);
             ++mma_issued;
         }
     }
-    if (ok) ok = wait_bar(mma_bar, phase);  // scores in TMEM; Q's buffers are free (P goes there)
+    // ---- V group 0's parts while the score MMAs run; the staging then takes group 1
+    if (ok && (ok = wait_bar(v_bar, v_phase))) {
+        split_rows64(base + SVF, base + SVP, kv_len, tid);
+        __syncthreads();  // every thread is done reading the V staging
+        if (tid == 0 && n_kg > 1) {
+            mbar_arrive_expect_tx(v_bar, 2 * TC_BOX_BYTES);
+            tma_rows128(base_addr + SVF, &map_v, p, row0 + TC_KG, h, bq, v_bar);
+            ++v_issued;
+        }
+    }
+    if (ok) ok = wait_bar(mma_bar, phase);  // scores in TMEM; the Q and K staging is free (P goes there)
     tc_fence_after();
 
-    // pass 1: row max (this thread: columns half*32 + 64c .. +31 of every chunk)
+    // pass 1: row max (this thread: columns half*32 + 64c .. +31 of every 64-key chunk)
     float mx = -INFINITY;
     if (ok) {
+        const int n_kc = (kv_len + 63) / 64;
         for (int kc = 0; kc < n_kc; ++kc) {
             float v[32];
-            scores32(kc * TC_K + half * 32, v);
+            scores32(kc * 64 + half * 32, v);
 #pragma unroll
             for (int i = 0; i < 32; ++i) mx = fmaxf(mx, v[i]);
         }
@@ -445,57 +502,43 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
     __syncthreads();
     if (ok) mx = fmaxf(mx, s_red[tid ^ 128]);
 
-    // pass 2: P chunk by chunk, O += P . V_chunk
+    // pass 2, per key group: P = exp(s - max) (keys past the length give 0),
+    // scaled and split into parts, then O += P.V
     float sum = 0.f;
-    for (int kc = 0; kc < n_kc && ok; ++kc) {
-        if (kc > 0 && !(ok = wait_bar(mma_bar, phase))) break;  // previous chunk's MMAs have read P and V^T
-        if ((kc & 1) == 0) {  // V keys 128*(kc/2) .. +127 have landed in SVR
-            if (kc > 0 && tid == 0) {
-                mbar_arrive_expect_tx(v_bar, 2 * TC_BOX_BYTES);
-                tma_rows128(base_addr + SVR, &map_v, p, row0 + kc * TC_K, h, bq, v_bar);
-                ++v_issued;
-            }
-            if (!(ok = wait_bar(v_bar, v_phase))) break;
+    for (int g = 0; g < n_kg && ok; ++g) {
+        if (g > 0) {
+            if (!(ok = wait_bar(mma_bar, phase))) break;  // group g-1's P.V MMAs have read P and V's parts
+            if (!(ok = wait_bar(v_bar, v_phase))) break;  // V group g has landed
+            split_rows64(base + SVF, base + SVP, kv_len - g * TC_KG, tid);
         }
-        {
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+            const int jl = c * 64 + half * 32;  // first key of this thread's 32 within the group
             float v[32];
-            scores32(kc * TC_K + half * 32, v);
+            scores32(g * TC_KG + jl, v);
 #pragma unroll
-            for (int c4 = 0; c4 < 8; ++c4) {
-                float e[4];
+            for (int q = 0; q < 4; ++q) {
+                float x[8];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    e[i] = ex2_approx(v[c4 * 4 + i] - mx);
-                    sum += e[i];
+                for (int i = 0; i < 8; ++i) {
+                    const float e = ex2_approx(v[q * 8 + i] - mx);
+                    sum += e;
+                    x[i] = e * kPScale;
                 }
-                split_store4(base + SQH, base + SQL, sw128_off(rloc, half * 32 + c4 * 4, TC_Q),
-                             make_float4(e[0], e[1], e[2], e[3]));
-            }
-        }
-        // V chunk kc, transposed (row = head dim, column = key) and split;
-        // keys past the sequence's length as zeros
-#pragma unroll
-        for (int it = 0; it < 4; ++it) {
-            const int jj = tid & 63, d4 = (tid >> 6) + 4 * it;  // key within the chunk, head-dim quad
-            const int jr = (kc & 1) * TC_K + jj;                 // key row within SVR
-            float4 x = *reinterpret_cast<const float4*>(base + SVR + sw128_off(jr, d4 * 4, 128));
-            if (kc * TC_K + jj >= kv_len) x = make_float4(0.f, 0.f, 0.f, 0.f);
-            const float xs[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint32_t off = sw128_off(d4 * 4 + i, jj, 64);
-                const float hv = tf32_hi(xs[i]);
-                *reinterpret_cast<float*>(base + SVH + off) = hv;
-                *reinterpret_cast<float*>(base + SVL + off) = xs[i] - hv;
+                uint4 hi, lo;
+                split8(x, hi, lo);
+                const uint32_t o = sw128_f16_chunk(rloc, jl + q * 8, TC_Q);
+                *reinterpret_cast<uint4*>(base + SPP + o) = hi;
+                *reinterpret_cast<uint4*>(base + SPP + P_PART + o) = lo;
             }
         }
         fence_async_smem();
         tc_fence_before();
-        __syncthreads();  // also: every thread is done reading SVR for this chunk
+        __syncthreads();
         if (tid == 0) {
             tc_fence_after();
-            mma_3xtf32<TC_K>(tmem + TC_MAX_S, base_addr + SQH, base_addr + SQL, base_addr + SVH, base_addr + SVL,
-                             kc > 0);
+            mma_2part<64, TC_KG, true>(tmem + TC_MAX_S, base_addr + SPP, P_PART, TC_Q * 128, base_addr + SVP, PART16,
+                                       0, g > 0);
             tc_commit(mma_bar);
             ++mma_issued;
         }
@@ -510,7 +553,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
         float o[32];
         tmem_ld32(tO + (uint32_t)(half * 32), o);
         if (row < q_lim) {
-            const float inv = 1.0f / sum;
+            const float inv = kPUnscale / sum;  // P was scaled by 2^15
             float4* dst = reinterpret_cast<float4*>(p.out + hbase + (long long)row * p.sr) + half * 8;
 #pragma unroll
             for (int c4 = 0; c4 < 8; ++c4)
