@@ -52,6 +52,10 @@ static_assert(TM * PART_STRIDE * 4 <= SMEM_BAR, "the partial tile overlays the s
 // dynamic shared memory a launch may take: the 227 KB of a CTA less the static per-column factors
 constexpr uint32_t kSplitSmemMax = 232448 - 2 * TN * 4;
 static_assert(SMEM_TOTAL <= kSplitSmemMax, "fits the 227 KB of shared memory a CTA may use");
+// CTAs of the split-K kernel an SM holds (228 KB per SM, 1 KB reserved per
+// CTA), and the dynamic shared memory a launch may take without losing one
+constexpr int kSplitCtasPerSm = 2 * (SMEM_TOTAL + 2 * TN * 4 + 1024) <= 233472 ? 2 : 1;
+constexpr uint32_t kSplitSmemKeep = kSplitCtasPerSm == 2 ? 233472 / 2 - 1024 - 2 * TN * 4 : kSplitSmemMax;
 
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -98,7 +102,7 @@ __device__ __forceinline__ void epilogue_store(const LinearArgs& a, int m, int n
         a.out[o] = y;
 }
 
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(THREADS, kSplitCtasPerSm)
     linear_tma_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw,
                       const LinearArgs a, int splits, int* err) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -980,7 +984,9 @@ int linear_tma_splits(int M, int N, int K, int num_sms) {
     const int tiles = ((N + TN - 1) / TN) * ((M + TM - 1) / TM);
     const int nk = K / TK;
     int S = 1;
-    while (S < 8 && tiles * 2 * S <= num_sms && nk / (2 * S) >= 2 && tiles <= cluster_capacity(2 * S)) S *= 2;
+    while (S < 8 && tiles * 2 * S <= num_sms * kSplitCtasPerSm && nk / (2 * S) >= 2 &&
+           tiles <= cluster_capacity(2 * S))
+        S *= 2;
     return S;
 }
 
@@ -1008,7 +1014,7 @@ cudaError_t launch_linear_tma(const LinearArgs& a, const CUtensorMap* tx, const 
     cfg.blockDim = dim3(THREADS, 1, 1);
     // with a residual: room for this rank's residual rows behind the stage ring, where it fits
     const uint32_t res_bytes = a.residual ? (uint32_t)(TM / splits) * TN * 4 : 0;
-    cfg.dynamicSmemBytes = SMEM_TOTAL + res_bytes <= kSplitSmemMax ? SMEM_TOTAL + res_bytes : SMEM_TOTAL;
+    cfg.dynamicSmemBytes = SMEM_TOTAL + res_bytes <= kSplitSmemKeep ? SMEM_TOTAL + res_bytes : SMEM_TOTAL;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
