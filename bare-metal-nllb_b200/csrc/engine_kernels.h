@@ -64,10 +64,11 @@ int linear_tma_splits(int M, int N, int K, int num_sms);
 bool linear_tma_use_persistent(int M, int N, int K, int num_sms);
 cudaError_t encode_half_maps_persistent(CUtensorMap* x_map, const void* planes, int K, int M, CUtensorMap* w_map,
                                         const void* wb, int N);
-// From 129 rows the launch runs 256 x 256 tiles on CTA pairs (cta_group::2)
-// when tw_pair is given: the weight's map with box 32 x 128 (64-byte swizzle,
-// encode_half_map_pair); the planes map is the same.
-bool linear_tma_use_pair(int M);
+// From 129 rows and 2 * num_sms tiles of 128 x 256 the launch runs 256 x 256
+// tiles on CTA pairs (cta_group::2) when tw_pair is given: the weight's map
+// with box 32 x 128 (64-byte swizzle, encode_half_map_pair); the planes map is
+// the same.
+bool linear_tma_use_pair(int M, int N, int num_sms);
 cudaError_t encode_half_map_pair(CUtensorMap* map, const void* wb, int K, int N);
 cudaError_t launch_linear_tma_persistent(const LinearArgs& a, const CUtensorMap* tx, const CUtensorMap* tw,
                                          const CUtensorMap* tw_pair, int num_sms, int* err, cudaStream_t st);

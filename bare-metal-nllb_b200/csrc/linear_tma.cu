@@ -20,8 +20,9 @@
 // tile run together and the weight tile is read from DRAM once.
 //
 // Larger outputs take a persistent kernel over 128 x 256 tiles (one CTA per
-// SM), or from 129 rows its pair form: 256 x 256 tiles on two-CTA clusters
-// with tcgen05.mma.cta_group::2, each CTA loading half of the weight tile.
+// SM), or, from 129 rows and two rounds of such tiles per SM, its pair form:
+// 256 x 256 tiles on two-CTA clusters with tcgen05.mma.cta_group::2, each CTA
+// loading half of the weight tile.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
@@ -52,10 +53,6 @@ static_assert(TM * PART_STRIDE * 4 <= SMEM_BAR, "the partial tile overlays the s
 // dynamic shared memory a launch may take: the 227 KB of a CTA less the static per-column factors
 constexpr uint32_t kSplitSmemMax = 232448 - 2 * TN * 4;
 static_assert(SMEM_TOTAL <= kSplitSmemMax, "fits the 227 KB of shared memory a CTA may use");
-// CTAs of the split-K kernel an SM holds (228 KB per SM, 1 KB reserved per
-// CTA), and the dynamic shared memory a launch may take without losing one
-constexpr int kSplitCtasPerSm = 2 * (SMEM_TOTAL + 2 * TN * 4 + 1024) <= 233472 ? 2 : 1;
-constexpr uint32_t kSplitSmemKeep = kSplitCtasPerSm == 2 ? 233472 / 2 - 1024 - 2 * TN * 4 : kSplitSmemMax;
 
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -102,7 +99,7 @@ __device__ __forceinline__ void epilogue_store(const LinearArgs& a, int m, int n
         a.out[o] = y;
 }
 
-__global__ void __launch_bounds__(THREADS, kSplitCtasPerSm)
+__global__ void __launch_bounds__(THREADS, 1)
     linear_tma_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw,
                       const LinearArgs a, int splits, int* err) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -917,15 +914,23 @@ int pair_capacity() {
 }
 
 // The pair kernel takes the persistent kernel's shapes from NLLB_PAIR_MIN_ROWS
-// rows up: below that a 256-row pair tile would be mostly rows past M.
+// rows up (below that a 256-row pair tile would be mostly rows past M) when the
+// output has at least two rounds of 128 x 256 tiles per SM.  Measured on B200
+// (prepared linear, 4096 rows): 1024 -> 256206 in 3131 us on pairs against
+// 3385 on single CTAs, 1024 -> 3072 and -> 4096 equal, 1024 -> 1024 26.6
+// against 24.8 us and 4096 -> 1024 75.3 against 72.3 (one round of tiles:
+// the pairs' co-scheduling costs more than the operand bytes they save).
 #ifndef NLLB_PAIR_MIN_ROWS
 #define NLLB_PAIR_MIN_ROWS 129
 #endif
-bool linear_tma_use_pair(int M) { return M >= NLLB_PAIR_MIN_ROWS && pair_capacity() > 0; }
+bool linear_tma_use_pair(int M, int N, int num_sms) {
+    const long long tiles = (long long)((M + pers::TM - 1) / pers::TM) * ((N + pers::TN - 1) / pers::TN);
+    return M >= NLLB_PAIR_MIN_ROWS && tiles >= 2LL * num_sms && pair_capacity() > 0;
+}
 
 cudaError_t launch_linear_tma_persistent(const LinearArgs& a, const CUtensorMap* tx, const CUtensorMap* tw,
                                          const CUtensorMap* tw_pair, int num_sms, int* err, cudaStream_t st) {
-    if (tw_pair && linear_tma_use_pair(a.M)) {
+    if (tw_pair && linear_tma_use_pair(a.M, a.N, num_sms)) {
         const int tiles = ((a.M + 2 * pair::TM - 1) / (2 * pair::TM)) * ((a.N + pair::TN - 1) / pair::TN);
         const int cap = pair_capacity();
         const int pairs = tiles < cap ? tiles : cap;
@@ -984,9 +989,7 @@ int linear_tma_splits(int M, int N, int K, int num_sms) {
     const int tiles = ((N + TN - 1) / TN) * ((M + TM - 1) / TM);
     const int nk = K / TK;
     int S = 1;
-    while (S < 8 && tiles * 2 * S <= num_sms * kSplitCtasPerSm && nk / (2 * S) >= 2 &&
-           tiles <= cluster_capacity(2 * S))
-        S *= 2;
+    while (S < 8 && tiles * 2 * S <= num_sms && nk / (2 * S) >= 2 && tiles <= cluster_capacity(2 * S)) S *= 2;
     return S;
 }
 
@@ -1014,7 +1017,7 @@ cudaError_t launch_linear_tma(const LinearArgs& a, const CUtensorMap* tx, const 
     cfg.blockDim = dim3(THREADS, 1, 1);
     // with a residual: room for this rank's residual rows behind the stage ring, where it fits
     const uint32_t res_bytes = a.residual ? (uint32_t)(TM / splits) * TN * 4 : 0;
-    cfg.dynamicSmemBytes = SMEM_TOTAL + res_bytes <= kSplitSmemKeep ? SMEM_TOTAL + res_bytes : SMEM_TOTAL;
+    cfg.dynamicSmemBytes = SMEM_TOTAL + res_bytes <= kSplitSmemMax ? SMEM_TOTAL + res_bytes : SMEM_TOTAL;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;

@@ -65,14 +65,14 @@ def _dev(a, device):
     (200, 1024, 4096, "residual"),     # fc1 shape, M tail
     (77, 4096, 1000, "plain"),         # fc2-like (K = 4096), N tail
     (512, 1024, 2050, "residual"),     # N % 4 != 0 (scalar stores)
-    # persistent kernel (at least 80 tiles of 128 x 256); from 129 rows on CTA pairs
-    # (256 x 256 tiles, tcgen05.mma.cta_group::2)
-    (4100, 1024, 4096, "bias_relu"),   # M tail
+    # persistent kernel (at least 80 tiles of 128 x 256); on CTA pairs (256 x 256 tiles,
+    # tcgen05.mma.cta_group::2) from 129 rows and 296 such tiles (two per SM of a B200)
+    (4100, 1024, 4096, "bias_relu"),   # pairs, M tail
     (40, 1024, 256206, "plain"),       # vocabulary projection shape, N tail (one-CTA form)
-    (129, 1024, 24000, "bias_relu"),   # pair: the second CTA of each pair has one row
-    (200, 1024, 20000, "residual"),    # pair: M tail inside the second CTA
-    (2000, 1024, 3001, "residual"),    # M and N tails, N % 4 != 0
-    (1100, 4096, 3072, "bias_relu"),   # K = 4096
+    (129, 1024, 40000, "bias_relu"),   # pairs: the second CTA of each pair has one row
+    (200, 1024, 40000, "residual"),    # pairs: M tail inside the second CTA
+    (2000, 1024, 3001, "residual"),    # one-CTA form (one round of tiles), M and N tails, N % 4 != 0
+    (1100, 4096, 3072, "bias_relu"),   # one-CTA form, K = 4096
 ])
 def test_prepared_linear_matches_reference(cuda_device, M, K, N, epilogue):
     import torch
