@@ -312,6 +312,30 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Two 32-column loads of this thread's TMEM lane (warp-wide) under one wait.
+__device__ __forceinline__ void tmem_ld32x2(uint32_t ta, uint32_t tb, float* va, float* vb) {
+    uint32_t r[64];
+#define NLLB_TMEM_LD32(T, R)                                                                                  \
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 "                                                    \
+                 "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "                    \
+                 "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"    \
+                 : "=r"(R[0]), "=r"(R[1]), "=r"(R[2]), "=r"(R[3]), "=r"(R[4]), "=r"(R[5]), "=r"(R[6]),        \
+                   "=r"(R[7]), "=r"(R[8]), "=r"(R[9]), "=r"(R[10]), "=r"(R[11]), "=r"(R[12]), "=r"(R[13]),    \
+                   "=r"(R[14]), "=r"(R[15]), "=r"(R[16]), "=r"(R[17]), "=r"(R[18]), "=r"(R[19]), "=r"(R[20]), \
+                   "=r"(R[21]), "=r"(R[22]), "=r"(R[23]), "=r"(R[24]), "=r"(R[25]), "=r"(R[26]), "=r"(R[27]), \
+                   "=r"(R[28]), "=r"(R[29]), "=r"(R[30]), "=r"(R[31])                                         \
+                 : "r"(T))
+    NLLB_TMEM_LD32(ta, r);
+    NLLB_TMEM_LD32(tb, (r + 32));
+#undef NLLB_TMEM_LD32
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        va[i] = __uint_as_float(r[i]);
+        vb[i] = __uint_as_float(r[32 + i]);
+    }
+}
+
 // fp32 -> (hi, lo) with hi exactly representable in tf32 (low 13 mantissa
 // bits cleared) and lo = x - hi exact; hi*hi' + hi*lo' + lo*hi' reproduces an
 // fp32 product to ~2^-21 relative.

@@ -348,10 +348,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
     const uint32_t base_addr = (raw_addr + 1023u) & ~1023u;
     unsigned char* base = smem_raw + (base_addr - raw_addr);
     uint64_t* mma_bar = reinterpret_cast<uint64_t*>(base + SBAR);
-    uint64_t* qk_bar = reinterpret_cast<uint64_t*>(base + SBAR + 8);  // Q and K group loads
+    uint64_t* k_bar = reinterpret_cast<uint64_t*>(base + SBAR + 8);   // K group loads
     uint64_t* v_bar = reinterpret_cast<uint64_t*>(base + SBAR + 16);  // V group loads
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + SBAR + 24);
     volatile int* s_abort = reinterpret_cast<volatile int*>(base + SBAR + 32);
+    uint64_t* q_bar = reinterpret_cast<uint64_t*>(base + SBAR + 40);  // the Q load
     __shared__ float s_red[TC_THREADS];
 
     pdl_launch_dependents();
@@ -365,7 +366,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
     if (warp == 0) tmem_alloc(tmem_slot, TC_TMEM_COLS);
     if (tid == 0) {
         mbar_init(mma_bar, 1);
-        mbar_init(qk_bar, 1);
+        mbar_init(q_bar, 1);
+        mbar_init(k_bar, 1);
         mbar_init(v_bar, 1);
         fence_barrier_init();
         *s_abort = 0;
@@ -414,19 +416,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
                             : nullptr;
     const float sl2 = p.scale_log2;
 
-    // Q, K group 0 and V group 0: every box issued at once.  A box counts its
-    // full bytes toward the barrier, rows outside the tensor included (they
-    // arrive as zeros).
+    // Q, K group 0 and V group 0: every box issued at once, Q on its own
+    // barrier so that its split overlaps K's arrival.  A box counts its full
+    // bytes toward the barrier, rows outside the tensor included (they arrive
+    // as zeros).
     if (tid == 0) {
-        mbar_arrive_expect_tx(qk_bar, 4 * TC_BOX_BYTES);
-        tma_rows128(base_addr + SQF, &map_q, p, row0 + q0, h, bq, qk_bar);
-        tma_rows128(base_addr + SKF, &map_k, p, row0, h, bq, qk_bar);
+        mbar_arrive_expect_tx(q_bar, 2 * TC_BOX_BYTES);
+        tma_rows128(base_addr + SQF, &map_q, p, row0 + q0, h, bq, q_bar);
+        mbar_arrive_expect_tx(k_bar, 2 * TC_BOX_BYTES);
+        tma_rows128(base_addr + SKF, &map_k, p, row0, h, bq, k_bar);
         mbar_arrive_expect_tx(v_bar, 2 * TC_BOX_BYTES);
         tma_rows128(base_addr + SVF, &map_v, p, row0, h, bq, v_bar);
     }
 
-    uint32_t phase = 0, qk_phase = 0, v_phase = 0;         // waits completed per barrier
-    uint32_t mma_issued = 0, qk_issued = 1, v_issued = 1;  // (thread 0) phases armed per barrier
+    uint32_t phase = 0, q_phase = 0, k_phase = 0, v_phase = 0;  // waits completed per barrier
+    uint32_t mma_issued = 0, k_issued = 1, v_issued = 1;        // (thread 0) phases armed per barrier
     auto wait_bar = [&](uint64_t* bar, uint32_t& ph) -> bool {
         if (!mbar_wait_bounded(bar, ph & 1u)) *s_abort = 1;
         ++ph;
@@ -434,38 +438,43 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
         return *s_abort == 0;
     };
     // 32 scores (base-2 logits) of this thread's row, keys j0..j0+31
-    auto scores32 = [&](int j0, float* v) {
-        tmem_ld32(tS + (uint32_t)j0, v);
-        if (uniform) {
+    // 32 scores (base-2 logits) of this thread's row at keys j0..j0+31 and at
+    // j1..j1+31, both TMEM loads under one wait; keys at or past the length
+    // (and columns no MMA wrote) become -inf
+    auto scores32x2 = [&](int j0, int j1, float* v0, float* v1) {
+        tmem_ld32x2(tS + (uint32_t)j0, tS + (uint32_t)j1, v0, v1);
+        auto fix = [&](int jb, float* v) {
+            if (uniform) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = (j0 + i < kv_len) ? 0.f : -INFINITY;
-        } else if (mrow) {
+                for (int i = 0; i < 32; ++i) v[i] = (jb + i < kv_len) ? 0.f : -INFINITY;
+            } else if (mrow) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-                v[i] = (j0 + i < kv_len) ? fmaf(__ldg(mrow + j0 + i), kLog2e, v[i] * sl2) : -INFINITY;
-        } else {
+                for (int i = 0; i < 32; ++i)
+                    v[i] = (jb + i < kv_len) ? fmaf(__ldg(mrow + jb + i), kLog2e, v[i] * sl2) : -INFINITY;
+            } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = (j0 + i < kv_len) ? v[i] * sl2 : -INFINITY;
-        }
+                for (int i = 0; i < 32; ++i) v[i] = (jb + i < kv_len) ? v[i] * sl2 : -INFINITY;
+            }
+        };
+        fix(j0, v0);
+        fix(j1, v1);
     };
 
     // ---- scores S = Q.K^T, group g in TMEM columns [128 g, 128 g + 128)
-    bool ok = wait_bar(qk_bar, qk_phase);  // Q and K group 0 have landed
+    bool ok = wait_bar(q_bar, q_phase);  // Q has landed
     if (ok) split_rows64(base + SQF, base + SQP, TC_Q, tid);
     for (int g = 0; g < n_kg && ok; ++g) {
-        if (g > 0) {
-            if (!(ok = wait_bar(mma_bar, phase))) break;   // group g-1's MMAs have read the K parts
-            if (!(ok = wait_bar(qk_bar, qk_phase))) break;  // K group g has landed
-        }
+        if (g > 0 && !(ok = wait_bar(mma_bar, phase))) break;  // group g-1's MMAs have read the K parts
+        if (!(ok = wait_bar(k_bar, k_phase))) break;           // K group g has landed
         split_rows64(base + SKF, base + SKP, TC_KG, tid);
         fence_async_smem();
         tc_fence_before();
         __syncthreads();  // the parts are visible to the tensor core, the K staging is free
         if (tid == 0) {
             if (g + 1 < n_kg) {
-                mbar_arrive_expect_tx(qk_bar, 2 * TC_BOX_BYTES);
-                tma_rows128(base_addr + SKF, &map_k, p, row0 + (g + 1) * TC_KG, h, bq, qk_bar);
-                ++qk_issued;
+                mbar_arrive_expect_tx(k_bar, 2 * TC_BOX_BYTES);
+                tma_rows128(base_addr + SKF, &map_k, p, row0 + (g + 1) * TC_KG, h, bq, k_bar);
+                ++k_issued;
             }
             tc_fence_after();
             mma_2part<TC_KG, 64, false>(tmem + (uint32_t)(g * TC_KG), base_addr + SQP, PART16, 0, base_addr + SKP,
@@ -490,12 +499,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
     // pass 1: row max (this thread: columns half*32 + 64c .. +31 of every 64-key chunk)
     float mx = -INFINITY;
     if (ok) {
-        const int n_kc = (kv_len + 63) / 64;
-        for (int kc = 0; kc < n_kc; ++kc) {
-            float v[32];
-            scores32(kc * 64 + half * 32, v);
+        const int n_kc = (kv_len + 63) / 64;  // 64-key chunks, two per load (TMEM columns < 256)
+        for (int kc = 0; kc < n_kc; kc += 2) {
+            float v0[32], v1[32];
+            scores32x2(kc * 64 + half * 32, kc * 64 + 64 + half * 32, v0, v1);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) mx = fmaxf(mx, v[i]);
+            for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fmaxf(v0[i], v1[i]));
         }
         s_red[tid] = mx;
     }
@@ -511,17 +520,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
             if (!(ok = wait_bar(v_bar, v_phase))) break;  // V group g has landed
             split_rows64(base + SVF, base + SVP, kv_len - g * TC_KG, tid);
         }
-#pragma unroll 1
+        float vv[2][32];
+        scores32x2(g * TC_KG + half * 32, g * TC_KG + 64 + half * 32, vv[0], vv[1]);
+#pragma unroll
         for (int c = 0; c < 2; ++c) {
             const int jl = c * 64 + half * 32;  // first key of this thread's 32 within the group
-            float v[32];
-            scores32(g * TC_KG + jl, v);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 float x[8];
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
-                    const float e = ex2_approx(v[q * 8 + i] - mx);
+                    const float e = ex2_approx(vv[c][q * 8 + i] - mx);
                     sum += e;
                     x[i] = e * kPScale;
                 }
@@ -564,7 +573,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) prefill_tc_kernel(const Prefill
         // let what is still in flight land (MMAs, TMA boxes): each barrier's
         // armed phases not waited for yet, oldest first
         for (; phase < mma_issued; ++phase) (void)mbar_wait_bounded(mma_bar, phase & 1u);
-        for (; qk_phase < qk_issued; ++qk_phase) (void)mbar_wait_bounded(qk_bar, qk_phase & 1u);
+        for (; q_phase < 1; ++q_phase) (void)mbar_wait_bounded(q_bar, 0u);
+        for (; k_phase < k_issued; ++k_phase) (void)mbar_wait_bounded(k_bar, k_phase & 1u);
         for (; v_phase < v_issued; ++v_phase) (void)mbar_wait_bounded(v_bar, v_phase & 1u);
     }
     tc_fence_before();
