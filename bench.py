@@ -747,6 +747,20 @@ def measure_translation(args, rank, world, local_rank, smi_index, host_cpus):
     return res, sources
 
 
+def _gemm_traffic_sample():
+    """DRAM traffic of one captured launch of the GEMM kernel against its
+    algorithmic bytes (profiles/gemm_pair_traffic.json): the class's launches
+    differ in shape, so no single per-launch traffic figure stands for them."""
+    tf = os.path.join(REPO, "profiles", "gemm_pair_traffic.json")
+    if not os.path.exists(tf):
+        return None
+    with open(tf) as f:
+        d = json.load(f)
+    return {"kernel": d["kernel"], "shape": d["shape"],
+            "dram_bytes": d["dram_bytes_read"] + d["dram_bytes_write"],
+            "algorithmic_bytes": d["algorithmic_bytes"], "ratio": d["ratio"]}
+
+
 def roofline_from_profile(prof, hbm_peak, tflops_sust, peak_kind):
     """The dominant kernel class of the translation (largest summed time):
     its algorithmic rate against the measured peak; the attention classes'
@@ -767,7 +781,8 @@ def roofline_from_profile(prof, hbm_peak, tflops_sust, peak_kind):
                 "frac": round(ach / hbm_peak, 4)}
     roof.update({"kernel_class": top, "share_of_kernel_time": round(v["ms"] / total, 4),
                  "launches": v["launches"], "avg_launch_us": round(v["ms"] / max(1, v["launches"]) * 1e3, 2),
-                 "traffic": None, "peak_kind": peak_kind,
+                 "traffic": None, "traffic_sample": _gemm_traffic_sample() if v["flops"] > 0 else None,
+                 "peak_kind": peak_kind,
                  "how": "algorithmic work of the class's launches / their summed durations, CUDA events "
                         "around each launch on the engine's stream in one profiled call of the same shard"})
     classes = {}
