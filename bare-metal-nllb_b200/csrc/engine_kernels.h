@@ -24,6 +24,8 @@ struct LinearArgs {
                              // (a kernel may fetch them before waiting for its predecessor)
     void* out_planes;        // TMA kernels only: write fp16 planes [2][M][N] (planes.cuh split of the result)
                              // instead of out; requires cblock == N and no residual
+    int test_expire = 0;     // split-K TMA kernel only: the MMA issuer first waits ~1 ms on a barrier nothing
+                             // arrives on, so that the launch takes its timeout path (tests of the bounded waits)
 };
 
 cudaError_t launch_embed_pos(float* x, const int* tokens, const int* positions, int pos_const, const int8_t* emb,

@@ -37,6 +37,7 @@ struct nllb_linear {
     int map_rows = -1;        // rows the plane maps were encoded for
     CUtensorMap tx{}, tx_pers{};
     int* err = nullptr;       // bounded-wait error word
+    bool expire_next = false; // nllb_linear_test_expire_next_wait: the next split-K launch times out
 };
 
 #define LP_CK(call)                                                                                   \
@@ -123,6 +124,8 @@ int nllb_linear_run(nllb_linear* L, const float* x, int M, float* out, const flo
     a.N = L->N;
     a.K = L->K;
     a.cblock = L->N;
+    a.test_expire = L->expire_next ? 1 : 0;  // read by the split-K kernel only
+    L->expire_next = false;
     a.relu = (flags & NLLB_LINEAR_RELU) ? 1 : 0;
     a.mask_from = -1;
     a.static_weights = 0;
@@ -154,6 +157,12 @@ int nllb_linear_run(nllb_linear* L, const float* x, int M, float* out, const flo
     return NLLB_ATTN_OK;
 }
 
+int nllb_linear_test_expire_next_wait(nllb_linear* L) {
+    if (!L) return nllb::set_error(NLLB_ATTN_EINVAL, "layer required");
+    L->expire_next = true;
+    return NLLB_ATTN_OK;
+}
+
 int nllb_linear_status(nllb_linear* L) {
     if (!L) return nllb::set_error(NLLB_ATTN_EINVAL, "layer required");
     int cur = 0, h = 0;
@@ -161,6 +170,7 @@ int nllb_linear_status(nllb_linear* L) {
     LP_CK(cudaSetDevice(L->device));
     LP_CK(cudaDeviceSynchronize());
     LP_CK(cudaMemcpy(&h, L->err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (h) LP_CK(cudaMemset(L->err, 0, sizeof(int)));  // reported once; the layer stays usable
     cudaSetDevice(cur);
     if (h) return nllb::set_error(NLLB_ATTN_ETIMEOUT, "a bounded device wait of the linear kernel gave up");
     return NLLB_ATTN_OK;

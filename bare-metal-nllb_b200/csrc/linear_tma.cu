@@ -109,7 +109,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint64_t* full = reinterpret_cast<uint64_t*>(base + SMEM_BAR);
     uint64_t* empty = full + STAGES;
     uint64_t* done = empty + STAGES;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    uint64_t* never = done + 1;  // test_expire: a barrier nothing arrives on
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(never + 1);
     int* s_abort = reinterpret_cast<int*>(tmem_slot + 1);
     __shared__ __align__(16) float s_inv[TN];
     __shared__ __align__(16) float s_bias[TN];
@@ -128,6 +129,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(&empty[s], 1);
         }
         mbar_init(done, 1);
+        mbar_init(never, 1);
         fence_barrier_init();
         *s_abort = 0;
     }
@@ -198,7 +200,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else if (warp == EPI_WARPS + 1 && lane == 0) {
         // ---- MMA issuer
         constexpr uint32_t idesc = umma_idesc_f16(TM, TN);
-        for (int c = 0; c < nk; ++c) {
+        // test of the bounded waits: this one runs out after ~1 ms, no MMA is
+        // issued and `done` never fires, so the producer's and the epilogue's
+        // waits run out in turn and the launch writes nothing
+        const bool expired = a.test_expire && !mbar_wait_bounded(never, 0u, kTestWaitBudgetCycles);
+        if (expired) atomicExch(s_abort, 1);
+        for (int c = 0; c < nk && !expired; ++c) {
             const int s = c % STAGES;
             if (!mbar_wait_bounded(&full[s], (uint32_t)((c / STAGES) & 1))) {
                 atomicExch(s_abort, 1);

@@ -100,6 +100,7 @@ SIGNATURES = {
     "nllb_linear_prepare": (_c_int, [_fp, _fp, _fp, _c_int, _c_int, _c_void_p, ctypes.POINTER(_c_void_p)]),
     "nllb_linear_run": (_c_int, [_c_void_p, _fp, _c_int, _fp, _fp, _c_int, _c_void_p]),
     "nllb_linear_status": (_c_int, [_c_void_p]),
+    "nllb_linear_test_expire_next_wait": (_c_int, [_c_void_p]),
     "nllb_linear_free": (None, [_c_void_p]),
     "nllb_apply_penalties": (_c_int, [_fp, ctypes.c_longlong, _c_int, _fp, _c_int, _fp, ctypes.c_float, _c_int,
                                       _c_void_p]),
@@ -425,6 +426,10 @@ class PreparedLinear:
 
     def status(self) -> int:
         return self._lib.nllb_linear_status(self._h)
+
+    def test_expire_next_wait(self) -> None:
+        """The next run on the split-K kernel times out (tests of the bounded waits)."""
+        _check(self._lib, self._lib.nllb_linear_test_expire_next_wait(self._h), "nllb_linear_test_expire_next_wait")
 
     def close(self) -> None:
         if getattr(self, "_h", None):

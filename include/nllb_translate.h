@@ -142,9 +142,9 @@ NLLB_ATTN_API int nllb_linear_int8_noalloc_status(void* stream);
  * A LinearInt8 (pico.h:26-32) made resident on the current GPU: the layer
  * keeps the caller's device pointers w [N][K], weight_scale [N] and bias [N]
  * (NULL: none) -- they must stay valid until nllb_linear_free -- plus its own
- * bf16 copy of w (exact) with a TMA tensor map.  nllb_linear_run computes
+ * fp16 copy of w (exact) with TMA tensor maps.  nllb_linear_run computes
  * what nllb_linear_int8 computes for those weights: more than 16 rows run on
- * the TMA-fed tcgen05 kernel over the bf16 copy, fewer on the SIMT kernel
+ * the TMA-fed tcgen05 kernels over the fp16 copy, fewer on the SIMT kernel
  * over the int8 matrix.  K must be a positive multiple of 64.  The reference
  * dequantises inside every mat_vec_int8 (tensor.c:144-196) and has no
  * prepared form; this is the form the translation engine keeps its layers in.
@@ -159,6 +159,14 @@ NLLB_ATTN_API int nllb_linear_prepare(const int8_t* w, const float* weight_scale
 NLLB_ATTN_API int nllb_linear_run(nllb_linear* layer, const float* x, int M, float* out, const float* residual,
                                   int flags, void* stream);
 NLLB_ATTN_API int nllb_linear_status(nllb_linear* layer);
+/* Test of the bounded device waits: if the next nllb_linear_run of this layer
+ * takes the split-K tensor-core kernel (more than 16 rows, fewer output tiles
+ * than the persistent kernel needs), its MMA thread first waits about 1 ms on
+ * a barrier nothing arrives on; the launch then takes its timeout path,
+ * writes no output and sets the layer's error word, which the next
+ * nllb_linear_status reports as NLLB_ATTN_ETIMEOUT (and clears).  The layer
+ * stays usable.  No counterpart in the reference. */
+NLLB_ATTN_API int nllb_linear_test_expire_next_wait(nllb_linear* layer);
 NLLB_ATTN_API void nllb_linear_free(nllb_linear* layer);
 
 /* ---- per-step vocabulary operations of the beam search --------------------

@@ -107,6 +107,31 @@ def test_prepared_linear_equals_int8_entry_point_across_row_counts(cuda_device):
         assert lin.status() == 0
 
 
+def test_bounded_wait_runs_out_and_layer_recovers(cuda_device):
+    """A split-K launch (4 CTAs per tile) whose MMA thread's wait runs out
+    (about 1 ms, the layer's test hook): it writes nothing, the status call
+    reports NLLB_ATTN_ETIMEOUT once, and the same layer then computes the
+    right result.  No fault, trap or endless wait is involved."""
+    import torch
+    M, K, N = 300, 4096, 1024
+    x, w, scale, b, _ = _case(11, M, K, N, True, False)
+    with na.PreparedLinear(_dev(w, cuda_device), _dev(scale, cuda_device), _dev(b, cuda_device)) as lin:
+        dx = _dev(x, cuda_device)
+        sentinel = torch.full((M, N), 7.0, device=cuda_device)
+        lin.test_expire_next_wait()
+        lin(dx, out=sentinel)
+        torch.cuda.synchronize()
+        assert lin.status() == na.ETIMEOUT
+        assert bool((sentinel == 7.0).all()), "the timed-out launch wrote output"
+        assert lin.status() == na.OK
+        out = lin(dx)
+        torch.cuda.synchronize()
+        assert lin.status() == na.OK
+    ref, bound = _reference(x, w, scale, b, False, None)
+    err = np.abs(out.cpu().numpy().astype(np.float64) - ref)
+    assert (err <= bound).all(), f"after the timeout: max err {err.max():.3e}"
+
+
 def test_prepared_linear_rejects_bad_arguments(cuda_device):
     import torch
     w = torch.zeros((64, 100), dtype=torch.int8, device=cuda_device)
