@@ -26,6 +26,7 @@ struct nllb_attn_ctx {
     const int* pending_parent = nullptr;  // device [pending_n][n_beams]
     int pending_n = 0;
     bool expire_next_wait = false;  // test: the next self-attention launch's wait runs out
+    bool expire_next_cross = false;  // test: the next cross-attention launch's wait runs out
     float* km = nullptr;  // [L][S][H][max_src][64]
     float* vm = nullptr;
     int* n_src_dev = nullptr;  // [L][S]

@@ -340,7 +340,10 @@ __global__ void __launch_bounds__(kThreads) decode_self_kernel(const P p) {
 // ---------------------------------------------------------------------------
 // Cross-attention: all beams of a sentence share each memory row.
 // ---------------------------------------------------------------------------
-template <int NB, int CP, int kCrossStages, bool PLANES>
+// EXPIRE: the bounded-wait test -- chunk 0 is never requested and the main
+// loop waits for it with a ~1 ms budget, so the wait runs out and the kernel
+// takes its timeout path (error bit, drain of the copies it did issue, no output).
+template <int NB, int CP, int kCrossStages, bool PLANES, bool EXPIRE = false>
 __global__ void __launch_bounds__(kThreads) cross_kernel(const CrossParams p) {
     constexpr int RPH = CP / 8;  // rows per half-warp per chunk
     constexpr int KV_FLOATS = CP * 64;
@@ -387,7 +390,8 @@ __global__ void __launch_bounds__(kThreads) cross_kernel(const CrossParams p) {
         bulk_g2s(sV + st * KV_FLOATS, gV + (size_t)pc0 * 64, kvb, &bar[st]);
     };
     if (tid == 0) {
-        for (int c = 0; c < kCrossStages - 1 && c < nchunk; ++c) issue(c);
+        for (int c = 0; c < kCrossStages - 1 && c < nchunk; ++c)
+            if (!EXPIRE || c != 0) issue(c);
     }
     pdl_wait_primary();  // q comes from the previous kernel; the output may still be read by it
 
@@ -410,7 +414,7 @@ __global__ void __launch_bounds__(kThreads) cross_kernel(const CrossParams p) {
     for (int c = 0; c < nchunk; ++c) {
         const int st = c % kCrossStages;
         const uint32_t par = (uint32_t)((c / kCrossStages) & 1);
-        if (!mbar_wait_bounded(&bar[st], par)) s_abort = 1;
+        if (!mbar_wait_bounded(&bar[st], par, EXPIRE ? kTestWaitBudgetCycles : kWaitBudgetCycles)) s_abort = 1;
         __syncthreads();
         if (s_abort) break;
         consumed = c + 1;
@@ -479,7 +483,8 @@ __global__ void __launch_bounds__(kThreads) cross_kernel(const CrossParams p) {
             atomicOr(p.err, NLLB_DEV_ERR_TIMEOUT);
             const int issued = min(nchunk, consumed + kCrossStages - 1);
             for (int c = consumed; c < issued; ++c)
-                (void)mbar_wait_bounded(&bar[c % kCrossStages], (uint32_t)((c / kCrossStages) & 1));
+                if (!EXPIRE || c != 0)  // the test form never requested chunk 0
+                    (void)mbar_wait_bounded(&bar[c % kCrossStages], (uint32_t)((c / kCrossStages) & 1));
         }
     } else {
         __syncthreads();
@@ -637,6 +642,10 @@ cudaError_t configure_nb_out() {
         e = cudaFuncSetAttribute(decode_self_kernel<4, false, 2, SelfParams>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)self_smem_bytes<4>());
         if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(cross_kernel<4, kCrossShortRows, 3, false, true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)cross_smem_bytes<4, kCrossShortRows, 3>());
+        if (e != cudaSuccess) return e;
     }
     e = cudaFuncSetAttribute(cross_kernel<NB, kCrossShortRows, 3, PLANES>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -725,7 +734,12 @@ cudaError_t launch_decode_self(const SelfParams& p, int n_sent, int n_beams, cud
 }
 
 cudaError_t launch_cross(const CrossParams& p, int n_sent, int n_beams, int chunk_rows, cudaStream_t st,
-                         bool planes) {
+                         bool planes, bool expire_wait) {
+    if (expire_wait) {
+        if (n_beams != 4 || planes || chunk_rows != kCrossShortRows) return cudaErrorInvalidValue;
+        return launch_ex(cross_kernel<4, kCrossShortRows, 3, false, true>, dim3(p.n_split, p.H, n_sent),
+                         cross_smem_bytes<4, kCrossShortRows, 3>(), p.n_split, st, p);
+    }
     switch (n_beams) {
         case 1: return launch_cross_nb<1>(p, n_sent, chunk_rows, st, planes);
         case 2: return launch_cross_nb<2>(p, n_sent, chunk_rows, st, planes);

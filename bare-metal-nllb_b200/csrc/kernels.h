@@ -134,8 +134,9 @@ cudaError_t configure_prefill_kernels();
 cudaError_t launch_decode_self(const SelfParams& p, int n_sent, int n_beams, cudaStream_t st, bool planes = false,
                                SelfMode mode = SelfMode::plain, const int* parent = nullptr);
 // chunk_rows: cross_chunk_rows(longest memory of the call)
+// expire_wait: the bounded-wait test form (4 beams, fp32 output, 16-row chunks)
 cudaError_t launch_cross(const CrossParams& p, int n_sent, int n_beams, int chunk_rows, cudaStream_t st,
-                         bool planes = false);
+                         bool planes = false, bool expire_wait = false);
 cudaError_t launch_reorder(uint8_t* hist, int Tp, const int* parent, int n_sent, int n_beams,
                            int* err, cudaStream_t st);
 cudaError_t launch_hist_init(uint8_t* hist, int Tp, int n_sent, cudaStream_t st);

@@ -578,6 +578,13 @@ int nllb_attn_test_expire_next_wait(nllb_attn_ctx* c) {
     return NLLB_ATTN_OK;
 }
 
+int nllb_attn_test_expire_next_cross_wait(nllb_attn_ctx* c) {
+    if (!c) return fail(NLLB_ATTN_EINVAL, "ctx is NULL");
+    if (c->d.n_beams != 4) return fail(NLLB_ATTN_EINVAL, "the bounded-wait test takes 4 beams");
+    c->expire_next_cross = true;
+    return NLLB_ATTN_OK;
+}
+
 int nllb_attn_reorder(nllb_attn_ctx* c, int n_sent, const int* parent) {
     if (!c) return fail(NLLB_ATTN_EINVAL, "ctx is NULL");
     if (c->d.max_sentences == 0) return fail(NLLB_ATTN_ESTATE, "context was created without sentence slots");
@@ -705,6 +712,14 @@ static int cross_dev(nllb_attn_ctx* c, int layer, int n_sent, const float* q, fl
     }
     p.scale_log2 = (1.0f / std::sqrt(64.0f)) * kLog2e;
     p.err = c->err;
+    if (c->expire_next_cross) {  // the bounded-wait test form, taken once
+        c->expire_next_cross = false;
+        if (d.n_beams != 4 || planes) return fail(NLLB_ATTN_EINVAL, "the bounded-wait test takes 4 beams, fp32 output");
+        chunk_rows = kCrossShortRows;
+        choose_split(c, n_sent * d.n_heads, max_len, chunk_rows, &p.n_split, &p.pos_per_split);
+        NLLB_CK(launch_cross(p, n_sent, d.n_beams, chunk_rows, c->stream, false, true));
+        return NLLB_ATTN_OK;
+    }
     NLLB_CK(launch_cross(p, n_sent, d.n_beams, chunk_rows, c->stream, planes));
     return NLLB_ATTN_OK;
 }

@@ -74,6 +74,7 @@ SIGNATURES = {
     "nllb_attn_reorder": (_c_int, [_c_void_p, _c_int, _fp]),
     "nllb_attn_reorder_host": (_c_int, [_c_void_p, _c_int, _fp]),
     "nllb_attn_test_expire_next_wait": (_c_int, [_c_void_p]),
+    "nllb_attn_test_expire_next_cross_wait": (_c_int, [_c_void_p]),
     "nllb_attn_set_memory": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _fp, _fp,
                                       ctypes.c_int64, ctypes.c_int64]),
     "nllb_attn_set_memory_host": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _fp, _fp,
@@ -234,6 +235,11 @@ class Context:
         """nllb_attn_test_expire_next_wait: the next self-attention launch's
         bounded wait runs out (a chunk that is never requested)."""
         _check(self.lib, self.lib.nllb_attn_test_expire_next_wait(self.handle), "test_expire_next_wait")
+
+    def test_expire_next_cross_wait(self) -> None:
+        """nllb_attn_test_expire_next_cross_wait: the next cross-attention
+        launch's bounded wait runs out (a chunk that is never requested)."""
+        _check(self.lib, self.lib.nllb_attn_test_expire_next_cross_wait(self.handle), "test_expire_next_cross_wait")
 
     def reorder_host(self, n_sent, parent) -> None:
         _check(self.lib, self.lib.nllb_attn_reorder_host(self.handle, n_sent, ptr(parent)),

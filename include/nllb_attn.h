@@ -169,6 +169,10 @@ NLLB_ATTN_API int nllb_attn_reorder_host(nllb_attn_ctx* ctx, int n_sentences, co
  * the call (_host) or the next nllb_attn_sync reports as NLLB_ATTN_ETIMEOUT;
  * the context stays usable.  No counterpart in the reference. */
 NLLB_ATTN_API int nllb_attn_test_expire_next_wait(nllb_attn_ctx* ctx);
+/* The same for the next cross-attention launch (nllb_attn_cross or _host,
+ * 4 beams): it waits ~1 ms for a memory chunk that it never requests, writes
+ * no output, and the error is reported as above. */
+NLLB_ATTN_API int nllb_attn_test_expire_next_cross_wait(nllb_attn_ctx* ctx);
 
 /* ---- cross-attention over the shared encoder memory ---------------------
  * Stores one sentence's projected encoder keys/values for one layer

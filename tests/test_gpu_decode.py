@@ -270,6 +270,39 @@ def test_cross_ragged_sentences_and_layers(cuda_device):
     np.testing.assert_array_equal(out_host, out[1])
 
 
+@pytest.mark.parametrize("n_sent", [1, 40])
+def test_cross_bounded_wait_runs_out_and_context_recovers(cuda_device, n_sent):
+    """The cross-attention launch's wait for a memory chunk runs out (a chunk
+    that is never requested, ~1 ms budget): the sync reports
+    NLLB_ATTN_ETIMEOUT, nothing is written, and the same call made again on
+    the same context gives the oracle's outputs.  1 sentence splits the
+    memory over a cluster of CTAs; 40 sentences do not split."""
+    import torch
+    rng = np.random.default_rng(95 + n_sent)
+    NB, n_src = 4, 100
+    with na.Context(0, n_layers=1, max_sentences=n_sent, n_beams=NB, max_tgt=4, max_src=n_src) as ctx:
+        mem = []
+        for s in range(n_sent):
+            K, V = (rng.standard_normal((n_src, 1024), dtype=np.float32) for _ in range(2))
+            mem.append((K, V))
+            ctx.set_memory_host(0, s, n_src, K, V, 64, 1024)
+        q = rng.standard_normal((n_sent, NB, 1024), dtype=np.float32)
+        dq = torch.from_numpy(q).cuda()
+        dout = torch.full_like(dq, 7.0)
+        ctx.test_expire_next_cross_wait()
+        ctx.cross(0, n_sent, dq, dout)
+        with pytest.raises(na.NllbAttnError) as ei:
+            ctx.sync()
+        assert ei.value.status == na.ETIMEOUT
+        assert bool((dout == 7.0).all()), "the timed-out launch wrote output"
+        ctx.cross(0, n_sent, dq, dout)
+        ctx.sync()
+        out = dout.cpu().numpy()
+    for s in range(0, n_sent, max(1, n_sent // 4)):
+        K, V = mem[s]
+        assert_attn_close(out[s], po.cross(K, V, q[s]), f"s{s}")
+
+
 def test_cross_many_sentences_no_split(cuda_device):
     import torch
     rng = np.random.default_rng(6)
