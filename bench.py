@@ -774,6 +774,7 @@ def roofline_from_profile(prof, hbm_peak, tflops_sust, peak_kind):
                 "frac": round(ach / tflops_sust, 4),
                 "note": "dense FLOPs 2*M*N*K of the linear layers; each product runs as two fp16 MMAs "
                         "(activations split into two fp16 parts), so the tensor pipe does 2x this work",
+                "mma_frac": round(2 * ach / tflops_sust, 4),
                 "peak_which": "bf16_tflops_sustained (kernel timed inside a long run)"}
     else:
         ach = v["bytes"] / (v["ms"] / 1e3) / 1e9
