@@ -17,7 +17,7 @@ positions decide which candidates survive and in which beam order).  A token
 difference is exempt only after a step whose margin is below 1e-4.
 
 Cases: config 0 (one 16-token sentence, 32 target tokens), three hand-picked
-config-4-shaped sentences, and the first 32 sentences of the sentence-batched
+config-4-shaped sentences, and the first 64 sentences of the sentence-batched
 workload (nllb_attn.synth_model.config4_sources, seed 4), max 128 tokens.
 
     python tests/golden/make_e2e_golden.py [model path] [--jobs J]
@@ -48,7 +48,7 @@ HAND_PICKED = {
     "cfg4_len40": (42, 40, 132),
     "cfg4_len100": (43, 100, 132),
 }
-N_CFG4 = 32
+N_CFG4 = 64
 SRC, TGT = "eng_Latn", "fra_Latn"
 
 

@@ -12,8 +12,9 @@ parity rule: sums of log-probabilities near -1000 are 6.1e-5 apart per fp32
 ulp, so such a step may resolve either way under other rounding).
 
 Cases: config 0 (one 16-token sentence, 32 tokens), three hand-picked
-config-4-shaped sentences, and the first 32 sentences of the sentence-batched
-workload (seed 4) translated as one batch, and twice over in one batch of 64.
+config-4-shaped sentences, and the first 64 sentences of the sentence-batched
+workload (seed 4) translated as one batch, and twice over in one batch of 128
+(512 beam rows: the per-GPU share of the workload on 8 GPUs).
 """
 import json
 import os
@@ -87,7 +88,7 @@ def test_hand_picked_batch_matches_reference(model):
 
 
 def test_sentence_batched_workload_matches_reference(model, capsys):
-    """The first 32 sentences of the 1024-sentence workload, one batch: every
+    """The first 64 sentences of the 1024-sentence workload, one batch: every
     sentence equals the reference program's output, or differs only after a
     reference near-tie; the counts are printed."""
     names = [f"cfg4_s{i:02d}" for i in range(N_CFG4)]
@@ -107,9 +108,9 @@ def test_sentence_batched_workload_matches_reference(model, capsys):
 
 
 def test_reference_sentences_in_a_larger_batch(model):
-    """The 32 reference sentences followed by the same 32 again: 256 beam rows,
-    so the vocabulary projection runs on CTA pairs as well as the encoder's
-    layers.  Both copies of every sentence must equal the reference output
+    """The 64 reference sentences followed by the same 64 again: 512 beam rows
+    (the per-GPU share of the workload on 8 GPUs), so the decoder's GEMMs run at
+    that size and the vocabulary projection on CTA pairs.  Both copies of every sentence must equal the reference output
     (or differ only after a reference near-tie), and each other."""
     names = [f"cfg4_s{i:02d}" for i in range(N_CFG4)]
     srcs = [GOLDEN["cases"][n]["src"] for n in names]
