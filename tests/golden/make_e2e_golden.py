@@ -17,10 +17,13 @@ positions decide which candidates survive and in which beam order).  A token
 difference is exempt only after a step whose margin is below 1e-4.
 
 Cases: config 0 (one 16-token sentence, 32 target tokens), three hand-picked
-config-4-shaped sentences, and the first 64 sentences of the sentence-batched
+config-4-shaped sentences, and the first 128 sentences of the sentence-batched
 workload (nllb_attn.synth_model.config4_sources, seed 4), max 128 tokens.
 
-    python tests/golden/make_e2e_golden.py [model path] [--jobs J]
+    python tests/golden/make_e2e_golden.py [model path] [--jobs J] [--reuse]
+
+--reuse keeps the cases of the existing file whose inputs (source ids,
+max_gen) are unchanged instead of running the reference again for them.
 """
 from __future__ import annotations
 
@@ -48,7 +51,7 @@ HAND_PICKED = {
     "cfg4_len40": (42, 40, 132),
     "cfg4_len100": (43, 100, 132),
 }
-N_CFG4 = 64
+N_CFG4 = 128
 SRC, TGT = "eng_Latn", "fra_Latn"
 
 
@@ -84,7 +87,12 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("model", nargs="?", default=sm.default_model_path(0))
     ap.add_argument("--jobs", type=int, default=max(1, (os.cpu_count() or 4) // 4))
+    ap.add_argument("--reuse", action="store_true", help="keep unchanged cases of the existing file")
     a = ap.parse_args()
+    old = {}
+    if a.reuse and os.path.exists(OUT):
+        with open(OUT) as f:
+            old = json.load(f)["cases"]
     sm.ensure_model(a.model, seed=0)
     subprocess.run(["make", "-C", os.path.join(REPO, "oracle"), "ref-main"], check=True)
     jobs = []
@@ -97,6 +105,9 @@ def main() -> None:
 
     def work(job):
         name, meta, src, max_gen = job
+        prev = old.get(name)
+        if prev is not None and prev["src"] == src and prev["max_gen"] == max_gen:
+            return name, prev
         toks, margins, info = run_reference(a.model, src, max_gen)
         print(name, len(src), "->", len(toks), f"min margin {min(margins):.3g}", info, flush=True)
         return name, dict(meta, src=src, tokens=toks, margins=[float(f"{g:.6g}") for g in margins],

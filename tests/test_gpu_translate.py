@@ -12,9 +12,9 @@ parity rule: sums of log-probabilities near -1000 are 6.1e-5 apart per fp32
 ulp, so such a step may resolve either way under other rounding).
 
 Cases: config 0 (one 16-token sentence, 32 tokens), three hand-picked
-config-4-shaped sentences, and the first 64 sentences of the sentence-batched
-workload (seed 4) translated as one batch, and twice over in one batch of 128
-(512 beam rows: the per-GPU share of the workload on 8 GPUs).
+config-4-shaped sentences, and the first 128 sentences of the sentence-batched
+workload (seed 4) translated as one batch (512 beam rows: the per-GPU share of
+the workload on 8 GPUs), and twice over in one batch of 256.
 """
 import json
 import os
@@ -88,7 +88,7 @@ def test_hand_picked_batch_matches_reference(model):
 
 
 def test_sentence_batched_workload_matches_reference(model, capsys):
-    """The first 64 sentences of the 1024-sentence workload, one batch: every
+    """The first 128 sentences of the 1024-sentence workload, one batch: every
     sentence equals the reference program's output, or differs only after a
     reference near-tie; the counts are printed."""
     names = [f"cfg4_s{i:02d}" for i in range(N_CFG4)]
@@ -108,9 +108,9 @@ def test_sentence_batched_workload_matches_reference(model, capsys):
 
 
 def test_reference_sentences_in_a_larger_batch(model):
-    """The 64 reference sentences followed by the same 64 again: 512 beam rows
-    (the per-GPU share of the workload on 8 GPUs), so the decoder's GEMMs run at
-    that size and the vocabulary projection on CTA pairs.  Both copies of every sentence must equal the reference output
+    """The 128 reference sentences followed by the same 128 again: 1024 beam
+    rows, so more of the decoder's GEMMs run on the persistent kernels and the
+    vocabulary projection on CTA pairs.  Both copies of every sentence must equal the reference output
     (or differ only after a reference near-tie), and each other."""
     names = [f"cfg4_s{i:02d}" for i in range(N_CFG4)]
     srcs = [GOLDEN["cases"][n]["src"] for n in names]
