@@ -49,7 +49,8 @@ constexpr uint32_t SMEM_BAR = STAGES * STAGE_BYTES;
 constexpr uint32_t SMEM_TOTAL = SMEM_BAR + 128 + 1024;
 constexpr uint32_t TMEM_COLS = 128;
 constexpr int PART_STRIDE = TN + 4;  // floats per row of the partial tile in shared memory
-static_assert(TM * PART_STRIDE * 4 <= SMEM_BAR, "the partial tile overlays the stage ring");
+// the partial tile and, behind it, the rows the other ranks send (fewer than TM)
+static_assert(2 * TM * PART_STRIDE * 4 <= SMEM_BAR, "the partial tile and the received rows overlay the stage ring");
 // dynamic shared memory a launch may take: the 227 KB of a CTA less the static per-column factors
 constexpr uint32_t kSplitSmemMax = 232448 - 2 * TN * 4;
 static_assert(SMEM_TOTAL <= kSplitSmemMax, "fits the 227 KB of shared memory a CTA may use");
@@ -86,6 +87,16 @@ __device__ __forceinline__ uint32_t dynamic_smem_bytes() {
     return r;
 }
 
+// Bulk copy from this CTA's shared memory into another CTA's of the cluster
+// (dst and bar: shared::cluster addresses there), completing on that CTA's
+// barrier.  16-byte aligned addresses, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_s2s_cluster(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+        "r"(smem_u32(src)), "r"(bytes), "r"(bar)
+        : "memory");
+}
+
 // y = accumulator / scale[n] (the per-column dequantisation factor of tensor.c:75)
 __device__ __forceinline__ void epilogue_store(const LinearArgs& a, int m, int n, float y) {
     if (a.bias) y += a.bias[n];
@@ -110,7 +121,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint64_t* empty = full + STAGES;
     uint64_t* done = empty + STAGES;
     uint64_t* never = done + 1;  // test_expire: a barrier nothing arrives on
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(never + 1);
+    uint64_t* recv = never + 1;  // split-K: the other ranks' rows of this rank's share have landed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv + 1);
     int* s_abort = reinterpret_cast<int*>(tmem_slot + 1);
     __shared__ __align__(16) float s_inv[TN];
     __shared__ __align__(16) float s_bias[TN];
@@ -130,6 +142,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         mbar_init(done, 1);
         mbar_init(never, 1);
+        mbar_init(recv, 1);
         fence_barrier_init();
         *s_abort = 0;
     }
@@ -243,15 +256,42 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         if (res_pre) cp_async_wait_all();  // this thread's residual copies (the barrier below shares them)
     }
-    if (S == 1) __syncthreads();
-    else cluster_sync_all();
+    // ---- split-K: every rank sends the rows of its partial tile that rank d
+    // finishes to rank d (one bulk shared-to-shared copy per pair, into the
+    // idle stage ring behind the partial tile); the first sent row's padding
+    // column carries the sender's abort flag
+    const uint32_t slot_bytes = (uint32_t)R * PART_STRIDE * 4;
+    float* recv_buf = part + TM * PART_STRIDE;  // [S-1][R][PART_STRIDE]: from ranks 0..S-1 without z
+    if (S == 1) {
+        __syncthreads();
+    } else {
+        fence_async_smem();  // the partial tile's generic writes, seen by the copies
+        if (tid == 0) mbar_arrive_expect_tx(recv, (uint32_t)(S - 1) * slot_bytes);
+        cluster_sync_all();  // every rank's partial tile written and its receive barrier armed
+        if (tid == 0) {
+            const int my_abort = *(volatile int*)s_abort;  // final: the producer and MMA threads are done
+            for (int d = 0; d < S; ++d) {
+                if (d == (int)z) continue;
+                float* rows = part + d * R * PART_STRIDE;
+                rows[TN] = __int_as_float(my_abort);
+                fence_async_smem();
+                const int slot = z < d ? z : z - 1;  // this rank's slot at rank d
+                bulk_s2s_cluster(map_rank(recv_buf + (size_t)slot * R * PART_STRIDE, d), rows, slot_bytes,
+                                 map_rank(recv, d));
+            }
+        }
+        if (!mbar_wait_bounded(recv, 0u)) atomicExch(s_abort, 1);
+    }
 
     // ---- rank z finishes rows [z*R, (z+1)*R) of the tile: sum of the S partials
     // in rank order, epilogue, coalesced stores (one warp per 128-column row)
-    int aborted = 0;
-    if (S == 1) aborted = *(volatile int*)s_abort;
-    else
-        for (int r = 0; r < S; ++r) aborted |= ld_cluster_s32(map_rank(s_abort, r));
+    int aborted = *(volatile int*)s_abort;
+    for (int r = 0; r < S - 1; ++r) aborted |= __float_as_int(recv_buf[(size_t)r * R * PART_STRIDE + TN]);
+    // the partial of rank r for row rr of this rank's share
+    auto part_row = [&](int r, int rr) -> const float* {
+        return r == (int)z ? part + (z * R + rr) * PART_STRIDE
+                           : recv_buf + ((size_t)(r < (int)z ? r : r - 1) * R + rr) * PART_STRIDE;
+    };
     if (aborted) {
         if (tid == 0) atomicOr(err, NLLB_DEV_ERR_TIMEOUT);
     } else {
@@ -279,15 +319,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const int rr = r0 + u * kRowStep;  // row within this rank's share
                     const int m = m0 + z * R + rr;
                     const bool live = rr < R && m < a.M;
-                    const float* src = part + (z * R + (live ? rr : 0)) * PART_STRIDE + nl;
-                    if (S == 1) {
-                        acc[u] = *reinterpret_cast<const float4*>(src);
-                    } else {
-                        acc[u] = ld_cluster_f4(map_rank(src, 0));
-                        for (int r = 1; r < S; ++r) {  // rank order: the sum is the same on every run
-                            const float4 q = ld_cluster_f4(map_rank(src, r));
-                            acc[u].x += q.x, acc[u].y += q.y, acc[u].z += q.z, acc[u].w += q.w;
-                        }
+                    const int rl = live ? rr : 0;
+                    acc[u] = *reinterpret_cast<const float4*>(part_row(0, rl) + nl);
+                    for (int r = 1; r < S; ++r) {  // rank order: the sum is the same on every run
+                        const float4 q = *reinterpret_cast<const float4*>(part_row(r, rl) + nl);
+                        acc[u].x += q.x, acc[u].y += q.y, acc[u].z += q.z, acc[u].w += q.w;
                     }
                     res[u] = (a.residual && live && full4)
                                  ? (res_pre ? *reinterpret_cast<const float4*>(res_s + rr * TN + nl)
@@ -326,24 +362,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         } else {
             // a warp stores 32 consecutive columns of one row per instruction
             for (int item = tid; item < R * TN; item += THREADS) {
-                const int rr = z * R + item / TN, nl = item % TN;
-                const int m = m0 + rr, n = n0 + nl;
+                const int rl = item / TN, nl = item % TN;
+                const int m = m0 + z * R + rl, n = n0 + nl;
                 if (m >= a.M) break;
                 if (n >= a.N) continue;
-                const float* src = part + rr * PART_STRIDE + nl;
-                float acc;
-                if (S == 1) {
-                    acc = *src;
-                } else {
-                    float p[8];
-#pragma unroll
-                    for (int r = 0; r < 8; ++r)
-                        if (r < S) p[r] = ld_cluster_f32(map_rank(src, r));
-                    acc = p[0];
-#pragma unroll
-                    for (int r = 1; r < 8; ++r)
-                        if (r < S) acc += p[r];
-                }
+                float acc = part_row(0, rl)[nl];
+                for (int r = 1; r < S; ++r) acc += part_row(r, rl)[nl];  // rank order
                 epilogue_store(a, m, n, acc * s_inv[nl]);
             }
         }
