@@ -846,9 +846,14 @@ extern "C" int nllb_translate(nllb_model* m, int n_sent, const int* src_tokens, 
     // Internal order: sentences by decreasing max_out (stable), so that the
     // sentences still running at any step are a prefix of the batch and a
     // step processes only that prefix (perm: internal index -> caller's).
+    // Equal max_out: the longer source first, so the per-sentence attention
+    // CTAs (dispatched sentence by sentence) start with the longest memories
+    // and the last wave holds the short ones.
     std::vector<int> perm(n_sent);
     for (int s = 0; s < n_sent; ++s) perm[s] = s;
-    std::stable_sort(perm.begin(), perm.end(), [&](int a, int b) { return max_out[a] > max_out[b]; });
+    std::stable_sort(perm.begin(), perm.end(), [&](int a, int b) {
+        return max_out[a] != max_out[b] ? max_out[a] > max_out[b] : n_src[a] > n_src[b];
+    });
     {
         std::vector<int> ns(n_sent), mo(n_sent);
         for (int s = 0; s < n_sent; ++s) ns[s] = n_src[perm[s]], mo[s] = max_out[perm[s]];
