@@ -444,13 +444,25 @@ __device__ __forceinline__ void drain_tile_256(const LinearArgs& a, uint32_t tad
         const size_t colbase = nok ? (size_t)(n / a.cblock) * ((size_t)a.M * a.cblock) + (size_t)(n % a.cblock) : 0;
         const int rows = min(32, a.M - mrow);
         if (nok) {
-            for (int r = 0; r < rows; ++r) {
+            // The residual may be the output itself (in-place x += f(x)): its
+            // 32 rows are all loaded before the first store, so the loads are
+            // in flight together instead of one per store.  Each element is
+            // still read before it is written.
+            float res[32];
+            if (a.residual) {
+#pragma unroll
+                for (int r = 0; r < 32; ++r)
+                    res[r] = r < rows ? a.residual[colbase + (size_t)(mrow + r) * a.cblock] : 0.f;
+            }
+#pragma unroll
+            for (int r = 0; r < 32; ++r) {
+                if (r >= rows) break;
                 float y = buf[r * BUF_LD + lane] * inv;
                 if (a.bias) y += bias;
                 if (a.relu) y = fmaxf(y, 0.f);
                 if (masked) y = -1e30f;
                 const size_t o = colbase + (size_t)(mrow + r) * a.cblock;
-                if (a.residual) y += a.residual[o];
+                if (a.residual) y += res[r];
                 if (a.out_planes)
                     store_planes_x1(static_cast<plane_t*>(a.out_planes), (size_t)a.M * a.N, o, y);
                 else
