@@ -226,6 +226,12 @@ __global__ void __launch_bounds__(256) linear_gemv_kernel(const LinearArgs a) {
     for (int m = 0; m < MT; ++m) red[warp][m][lane] = acc[m];
     __syncthreads();
     if (warp == 0 && n < a.N) {
+        const size_t col = (size_t)(n / a.cblock) * ((size_t)a.M * a.cblock) + (n % a.cblock);
+        // the residual may be the output itself: every row's value is loaded
+        // before the first store, so the loads overlap
+        float res[MT];
+#pragma unroll
+        for (int m = 0; m < MT; ++m) res[m] = (a.residual && m < a.M) ? a.residual[col + (size_t)m * a.cblock] : 0.f;
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
             if (m >= a.M) break;
@@ -236,10 +242,8 @@ __global__ void __launch_bounds__(256) linear_gemv_kernel(const LinearArgs a) {
             if (a.bias) y += bias;
             if (a.relu) y = fmaxf(y, 0.f);
             if (a.mask_from >= 0 && n >= a.mask_from) y = -1e30f;
-            const size_t o =
-                (size_t)(n / a.cblock) * ((size_t)a.M * a.cblock) + (size_t)m * a.cblock + (n % a.cblock);
-            if (a.residual) y += a.residual[o];
-            a.out[o] = y;
+            if (a.residual) y += res[m];
+            a.out[col + (size_t)m * a.cblock] = y;
         }
     }
 }

@@ -190,14 +190,19 @@ __global__ void __launch_bounds__(THREADS, 1) linear_tc_kernel(const LinearArgs 
     }
 
     // ---- epilogue (warps 0-7): accumulator rows from TMEM
-    auto store_out = [&](int m, int n, float acc) {
+    // The residual may be the output itself: callers load the residual
+    // values of a run of outputs before storing any of them (the loads
+    // overlap; each element is still read before it is written).
+    auto out_index = [&](int m, int n) -> size_t {
+        return (size_t)(n / a.cblock) * ((size_t)a.M * a.cblock) + (size_t)m * a.cblock + (n % a.cblock);
+    };
+    auto store_out = [&](int m, int n, float acc, float res) {
         float y = acc * (1.0f / a.scale[n]);
         if (a.bias) y += a.bias[n];
         if (a.relu) y = fmaxf(y, 0.f);
         if (a.mask_from >= 0 && n >= a.mask_from) y = -1e30f;
-        const size_t o = (size_t)(n / a.cblock) * ((size_t)a.M * a.cblock) + (size_t)m * a.cblock + (n % a.cblock);
-        if (a.residual) y += a.residual[o];
-        a.out[o] = y;
+        if (a.residual) y += res;
+        a.out[out_index(m, n)] = y;
     };
     bool ok = true;
     const int quarter = warp & 3, half = warp >> 2;
@@ -214,9 +219,13 @@ __global__ void __launch_bounds__(THREADS, 1) linear_tc_kernel(const LinearArgs 
             if (S == 1) {
                 const int m = m0 + rloc;
                 if (m < a.M) {
+                    float res[32];
 #pragma unroll
                     for (int j = 0; j < 32; ++j)
-                        if (n0 + col0 + j < a.N) store_out(m, n0 + col0 + j, v[j]);
+                        res[j] = (a.residual && n0 + col0 + j < a.N) ? a.residual[out_index(m, n0 + col0 + j)] : 0.f;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (n0 + col0 + j < a.N) store_out(m, n0 + col0 + j, v[j], res[j]);
                 }
             } else {
                 float4* dst = reinterpret_cast<float4*>(ws + ((size_t)tile * S + z) * (TM * TN) + rloc * TN + col0);
@@ -246,9 +255,13 @@ __global__ void __launch_bounds__(THREADS, 1) linear_tc_kernel(const LinearArgs 
                 }
                 if (m < a.M) {
                     const float av[4] = {acc.x, acc.y, acc.z, acc.w};
+                    float res[4];
 #pragma unroll
                     for (int j = 0; j < 4; ++j)
-                        if (n0 + col0 + j < a.N) store_out(m, n0 + col0 + j, av[j]);
+                        res[j] = (a.residual && n0 + col0 + j < a.N) ? a.residual[out_index(m, n0 + col0 + j)] : 0.f;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        if (n0 + col0 + j < a.N) store_out(m, n0 + col0 + j, av[j], res[j]);
                 }
             }
             if (tid == 0) tile_count[tile] = 0;
