@@ -139,3 +139,34 @@ def test_prepared_linear_rejects_bad_arguments(cuda_device):
     with pytest.raises(na.NllbAttnError) as ei:
         na.PreparedLinear(w, s)  # K not a multiple of 64
     assert ei.value.status == na.EINVAL
+
+
+@pytest.mark.parametrize("M,K,N,entry", [
+    (4, 1024, 1024, "prepared"),      # few rows: the weight-streaming GEMV
+    (512, 1024, 1024, "prepared"),    # split-K cluster kernel (4 CTAs per tile)
+    (4096, 1024, 1024, "prepared"),   # one-CTA persistent kernel (128 tiles of 128 x 256)
+    (4096, 1024, 3072, "prepared"),   # CTA pairs (384 tiles of 128 x 256)
+    (300, 1024, 1024, "int8"),        # nllb_linear_int8: split-K with the last-CTA reduction
+    (2048, 1024, 1024, "int8"),       # nllb_linear_int8: no split
+])
+def test_residual_in_place(cuda_device, M, K, N, entry):
+    """x += f(x) as the decoder's residual layers run it: the output buffer is
+    also the residual.  The kernels load a run of residual values before
+    storing any of them; every element must still see its own old value."""
+    import torch
+    x, w, scale, b, r = _case(7 * M + N, M, K, N, True, True)
+    wd, sd, bd = _dev(w, cuda_device), _dev(scale, cuda_device), _dev(b, cuda_device)
+    buf = _dev(r, cuda_device)
+    if entry == "prepared":
+        with na.PreparedLinear(wd, sd, bd) as lin:
+            lin(_dev(x, cuda_device), out=buf, residual=buf)
+            torch.cuda.synchronize()
+            assert lin.status() == 0
+    else:
+        na.linear_int8(_dev(x, cuda_device), wd, sd, bd, out=buf, residual=buf)
+        torch.cuda.synchronize()
+        assert na.linear_int8_status() == 0
+    ref, bound = _reference(x, w, scale, b, False, r)
+    err = np.abs(buf.cpu().numpy().astype(np.float64) - ref)
+    assert np.isfinite(err).all() and (err <= bound).all(), \
+        f"max err {np.nanmax(err):.3e}, worst ratio {np.nanmax(err / bound):.2f}"
